@@ -1,0 +1,201 @@
+/*
+ * memopt_b200.h — C-ABI of the B200 (sm_100a) KV-cache data plane.
+ *
+ * Every entry point takes plain pointers and sizes; no PyTorch types cross
+ * this boundary.  Device pointers must point to memory of the device that is
+ * current on the calling thread.  `stream` is a cudaStream_t passed as void*
+ * (NULL = legacy default stream).  All kernel entry points are asynchronous
+ * with respect to the host: they enqueue work on `stream` and return a
+ * status code describing argument validation and launch errors only.
+ *
+ * Reference interfaces replaced (paths relative to the reference project
+ * TheRadDani/memopt-transformer-runtime):
+ *   pool / free-list ........ src/csrc/kv_cache.cu:83-201, kv_cache.h:24-54
+ *   write_cache ............. src/csrc/kv_cache.cu:228-348, kv_cache.h:69-73
+ *   evict_cache ............. src/csrc/kv_cache.cu:379-559, kv_cache.h:88-92
+ *   evict_tokens ............ src/csrc/kv_cache.cu:609-1156, kv_cache.h:117-122
+ *   quantize / dequantize ... src/csrc/quantization.cu:104-428, quantization.h:22,35
+ *   dynamic_sparse_attention  src/csrc/attention.cu:98-521, attention.h:21-29
+ * The Python-facing module `memopt_C` (src/csrc/extension.cpp:10-124) is a
+ * thin wrapper that validates tensors and forwards to these functions.
+ */
+#ifndef MEMOPT_B200_H
+#define MEMOPT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status codes                                                               */
+/* ------------------------------------------------------------------------ */
+#define MEMOPT_OK                    0
+#define MEMOPT_ERR_INVALID_ARG      (-1)
+#define MEMOPT_ERR_NOT_INITIALIZED  (-2)
+#define MEMOPT_ERR_UNSUPPORTED      (-3)
+#define MEMOPT_ERR_CUDA             (-4)
+#define MEMOPT_ERR_OUT_OF_RANGE     (-5)
+#define MEMOPT_ERR_WORKSPACE        (-6)
+
+/* Version of this ABI (bumped on any signature change). */
+int memopt_abi_version(void);
+/* Static description of a status code. */
+const char* memopt_status_string(int status);
+/* Human-readable message of the last failing call on this host thread. */
+const char* memopt_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Page pool free-list (host side).                                           */
+/* Replaces KVCachePool / init_pool / allocate_block / free_block /           */
+/* free_blocks_count (kv_cache.cu:83-201).  The pool's device memory is owned */
+/* by the caller (the Python module allocates it with the caching allocator); */
+/* this library keeps the FIFO free-list and the pool geometry.               */
+/* ------------------------------------------------------------------------ */
+
+/* (Re)initialise the free-list with blocks 0..num_blocks-1 in FIFO order.
+ * Returns MEMOPT_OK, or MEMOPT_ERR_INVALID_ARG (the pool is then left
+ * uninitialised).  Same geometry as the live pool -> no-op (kv_cache.cu:116). */
+int memopt_pool_init(int num_blocks, int block_size, int num_heads, int head_dim);
+/* Drop the pool: afterwards every pool call reports NOT_INITIALIZED. */
+void memopt_pool_reset(void);
+int memopt_pool_is_initialized(void);
+/* Writes the live geometry; NOT_INITIALIZED when there is no pool. */
+int memopt_pool_config(int* num_blocks, int* block_size, int* num_heads, int* head_dim);
+/* Pops the oldest free block: >=0 on success, -1 when exhausted,
+ * MEMOPT_ERR_NOT_INITIALIZED (-2) without a pool (kv_cache.cu:163-172). */
+int memopt_pool_allocate_block(void);
+/* Pushes a block back (kv_cache.cu:179-185): OK, NOT_INITIALIZED or OUT_OF_RANGE. */
+int memopt_pool_free_block(int block_idx);
+/* Number of free blocks, 0 without a pool (kv_cache.cu:198-201). */
+int memopt_pool_free_blocks_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* write_cache (kv_cache.cu:228-348).                                         */
+/* keys/values: fp16 [num_tokens, num_heads, head_dim], contiguous.           */
+/* slot_mapping: int32 [num_tokens], slot = block * block_size + position.    */
+/* Slots outside [0, num_blocks*block_size) are skipped (the reference writes */
+/* out of bounds); when `bad_slot_count` (device int32, nullable) is given,   */
+/* the kernel atomically adds the number of skipped tokens to it.             */
+/* ------------------------------------------------------------------------ */
+
+/* fp16 pool, reference layout [num_blocks, block_size, num_heads, head_dim]. */
+int memopt_write_cache_f16(const void* keys, const void* values,
+                           const int32_t* slot_mapping, int64_t num_tokens,
+                           int num_heads, int head_dim,
+                           void* key_pool, void* value_pool,
+                           int64_t num_blocks, int block_size,
+                           int32_t* bad_slot_count, void* stream);
+
+/* INT4 pool with on-the-fly quantisation (new page format, no reference
+ * counterpart for the fused op; the codes follow quantization.cu:129-202).
+ * codes  : uint8 [num_blocks, num_heads, block_size, head_dim/2]
+ * scales : fp16  [num_blocks, num_heads, block_size, head_dim/64]
+ * Groups are 64 consecutive head_dim elements of one (token, head); the code
+ * is computed from the fp32 scale absmax/7 (1.0 for an all-zero group) and
+ * the stored scale is that fp32 scale rounded to fp16. head_dim % 64 == 0. */
+int memopt_write_cache_int4(const void* keys, const void* values,
+                            const int32_t* slot_mapping, int64_t num_tokens,
+                            int num_heads, int head_dim,
+                            uint8_t* key_codes, void* key_scales,
+                            uint8_t* value_codes, void* value_scales,
+                            int64_t num_blocks, int block_size,
+                            int32_t* bad_slot_count, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* INT4 quantize / dequantize (quantization.cu:104-203, 232-270, 294-428).    */
+/* Groups of `group_size` (must be 64) consecutive elements of the flat input.*/
+/* ------------------------------------------------------------------------ */
+int memopt_quantize_int4(const void* input_f16, int64_t numel, int group_size,
+                         uint8_t* packed, float* scales, void* stream);
+/* numel = number of fp16 outputs; numel / group_size groups are written.     */
+int memopt_dequantize_int4(const uint8_t* packed, const float* scales,
+                           int64_t numel, int group_size,
+                           void* output_f16, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* evict_tokens (kv_cache.cu:640-1156): per (sequence, head) Ada-KV eviction  */
+/* with the reference's exact 32-step fp32 bisection threshold, sink boost,   */
+/* partial zeroing of evicted rows and per-block vote/unlink.                 */
+/* scores: fp32 [num_seqs, num_heads, seq_len]; block_tables int32           */
+/* [num_seqs, max_blocks_per_seq] (mutated); is_block_free int32              */
+/* [total_pool_blocks] (mutated); key/value pool fp16 in reference layout.    */
+/* Optional compaction outputs (nullable): retained_idx int32                 */
+/* [num_seqs, num_heads, seq_len] — ascending indices of the kept tokens,     */
+/* padded with -1 — and retained_count int32 [num_seqs, num_heads].          */
+/* seq_len <= 32768 (the reference stops at 4096).                            */
+/* ------------------------------------------------------------------------ */
+int memopt_evict_tokens(const float* scores, int num_seqs, int num_heads, int seq_len,
+                        int32_t* block_tables, int max_blocks_per_seq,
+                        int32_t* is_block_free, int total_pool_blocks,
+                        void* key_pool, void* value_pool,
+                        int pool_num_blocks, int block_size, int head_dim,
+                        float retain_ratio, int num_sink_tokens,
+                        int32_t* retained_idx, int32_t* retained_count,
+                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* evict_cache (kv_cache.cu:379-559): per (physical block, head) keep the     */
+/* max(1, (int)(r*block_size)) highest scores, zero the full head rows of the */
+/* rest.  scores fp32 [num_blocks, block_size, num_heads].                    */
+/* ------------------------------------------------------------------------ */
+int memopt_evict_cache(const float* scores, int num_blocks, int block_size,
+                       int num_heads, int head_dim,
+                       void* key_pool, void* value_pool,
+                       float retain_ratio, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* dynamic_sparse_attention (attention.cu:98-521).                            */
+/* out[b,q,h,:] = softmax(q.K^T / sqrt(head_dim)) V over the tokens           */
+/* [max(0, ctx_b - W), ctx_b) of every logical page whose block-table entry   */
+/* is >= 0 (and < num_blocks); no causal mask; W = max_seq_len when           */
+/* window_size <= 0 or > max_seq_len; rows with no visible token are 0.       */
+/* query/out fp16 [batch, q_len, num_heads, head_dim]; head_dim in {64,128};  */
+/* block_size in {16,32}.  `workspace` holds split-K partials and tickets:    */
+/* size it with memopt_paged_attention_workspace_size(); its first            */
+/* memopt_paged_attention_ticket_bytes() bytes must be zero before the first  */
+/* use and every completed call leaves them zero again.                       */
+/* ------------------------------------------------------------------------ */
+size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads,
+                                             int head_dim, int max_blocks_per_seq,
+                                             int block_size, int max_seq_len,
+                                             int window_size);
+/* Bytes at the start of the workspace that hold tickets (must start zeroed). */
+size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads);
+
+/* fp16 pool, reference layout [num_blocks, block_size, num_heads, head_dim]. */
+int memopt_paged_attention_f16(const void* query, const void* key_pool,
+                               const void* value_pool,
+                               const int32_t* block_tables,
+                               const int32_t* context_lens,
+                               int batch, int q_len, int num_heads, int head_dim,
+                               int max_blocks_per_seq, int64_t num_blocks,
+                               int block_size, int max_seq_len, int window_size,
+                               void* out, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* INT4 pool written by memopt_write_cache_int4; K/V element value is
+ * (code - 8) * float(scale_fp16), dequantised inside the kernel. */
+int memopt_paged_attention_int4(const void* query,
+                                const uint8_t* key_codes, const void* key_scales,
+                                const uint8_t* value_codes, const void* value_scales,
+                                const int32_t* block_tables,
+                                const int32_t* context_lens,
+                                int batch, int q_len, int num_heads, int head_dim,
+                                int max_blocks_per_seq, int64_t num_blocks,
+                                int block_size, int max_seq_len, int window_size,
+                                void* out, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif /* MEMOPT_B200_H */

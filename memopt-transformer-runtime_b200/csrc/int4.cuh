@@ -1,0 +1,57 @@
+// int4.cuh — group-64 symmetric INT4 arithmetic shared by the standalone
+// quantizer and the fused write_cache.
+//
+// Per group (reference src/csrc/quantization.cu:129-202):
+//   absmax = max |x|            (fmaxf semantics: NaN inputs are ignored)
+//   scale  = absmax > 0 ? absmax / 7.0f : 1.0f       (IEEE fp32 division)
+//   q      = clamp((int)roundf(x / scale) + 8, 0, 15) (roundf: ties away)
+//   byte i = q[2i] | q[2i+1] << 4                      (low nibble = even)
+// A group of 64 fp16 values is handled by 8 consecutive lanes, 8 values
+// (16 bytes) each; lanes 8k..8k+7 must all be present for the shuffles.
+#pragma once
+#include "common.cuh"
+
+namespace memopt {
+
+__device__ __forceinline__ void unpack_half8(const uint4& v, float f[8]) {
+  const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h2[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Max of |x| over the 8-lane group containing this lane.
+__device__ __forceinline__ float group8_absmax(const float f[8]) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  return m;
+}
+
+__device__ __forceinline__ float int4_scale_from_absmax(float absmax) {
+  return (absmax > 0.f) ? (absmax / 7.0f) : 1.0f;
+}
+
+// One code, bit-exact with the reference.  The C-style float->int conversion
+// is cvt.rzi.s32.f32 (saturating, NaN -> 0), exactly as in the reference.
+__device__ __forceinline__ uint32_t int4_code(float x, float scale) {
+  int iq = static_cast<int>(roundf(x / scale)) + 8;
+  return static_cast<uint32_t>(min(max(iq, 0), 15));
+}
+
+// Eight consecutive codes packed into one little-endian word: nibble j holds
+// element j, so byte k = q[2k] | q[2k+1] << 4 as in the reference.
+__device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
+  return w;
+}
+
+}  // namespace memopt
