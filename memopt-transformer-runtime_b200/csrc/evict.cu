@@ -1,0 +1,364 @@
+// evict.cu — Ada-KV eviction over the paged pool.
+//
+// evict_tokens: replaces evict_tokens_kernel (reference
+// src/csrc/kv_cache.cu:640-1015).  Semantics reproduced exactly:
+//   * scores of tokens t < num_sink_tokens are replaced by 1e38f (:723-726);
+//   * keep = max(1, min(L, (int)ceilf(r * (float)L)))            (:754-755);
+//   * min/max start at +1e38f / -1e38f and use fminf/fmaxf       (:758-803);
+//   * if min >= max: thr = min - 1.0f, else 32 bisection steps
+//     mid = lo + (hi - lo) * 0.5f (contracted to one fma, as nvcc does by
+//     default), count(s >= mid) >= keep ? lo = mid : hi = mid; thr = lo;
+//   * token t is evicted iff s < thr; of an evicted row only the elements
+//     d = (t % 32) + 32k are zeroed in K and V (:937-973);
+//   * the per-block vote counts only evicted tokens with t % 32 == 0 (:978),
+//     so it can reach block_size only when block_size == 1 (:993-1014).
+// The reference runs one 128-thread CTA per (seq, head) with the scores in
+// shared memory and three barriers per bisection step; here a 1024-thread
+// CTA keeps the scores in registers (<= 32 per thread), each step costs one
+// barrier (double-buffered warp partials), and the kept tokens are also
+// stream-compacted into an ascending index list.
+//
+// evict_cache: replaces evict_cache_kernel (kv_cache.cu:379-483): per
+// (physical block, head) the threshold is the keep-th largest score found by
+// repeated arg-max (values <= -1e38f or NaN never win), keep =
+// max(1, (int)(r * block_size)); rows with score < threshold are zeroed.
+#include "common.cuh"
+
+namespace memopt {
+namespace {
+
+constexpr int kEvictThreads = 1024;
+constexpr int kEvictWarps = kEvictThreads / 32;
+constexpr int kMaxEvictLen = kEvictThreads * 32;
+
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kEvictThreads, 1)
+evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_heads, int seq_len,
+                    int32_t* __restrict__ block_tables, int max_blocks_per_seq,
+                    int32_t* __restrict__ is_block_free, int total_pool_blocks,
+                    __half* __restrict__ kpool, __half* __restrict__ vpool, int block_size,
+                    int head_dim, float retain_ratio, int num_sinks,
+                    int32_t* __restrict__ retained_idx, int32_t* __restrict__ retained_count) {
+  const int seq = blockIdx.x;
+  const int head = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int L = seq_len;
+
+  __shared__ float red_f[2][kEvictWarps];
+  __shared__ int red_i[2][kEvictWarps];
+  __shared__ int warp_tot[kEvictWarps];
+
+  // ---- load (thread owns tokens [tid*VPT, tid*VPT+VPT)) -------------------
+  const float* src = scores + (static_cast<int64_t>(seq) * num_heads + head) * L;
+  float v[VPT];
+  const int t0 = tid * VPT;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int t = t0 + i;
+    float s = 0.f;
+    if (t < L) s = __ldg(src + t);
+    if (t < num_sinks) s = 1e38f;
+    v[i] = s;
+  }
+
+  // ---- min / max ---------------------------------------------------------
+  float lmin = 1e38f, lmax = -1e38f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    if (t0 + i < L) {
+      lmin = fminf(lmin, v[i]);
+      lmax = fmaxf(lmax, v[i]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
+    lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+  }
+  if (lane == 0) {
+    red_f[0][warp] = lmin;
+    red_f[1][warp] = lmax;
+  }
+  __syncthreads();
+  float gmin = lane < kEvictWarps ? red_f[0][lane] : 1e38f;
+  float gmax = lane < kEvictWarps ? red_f[1][lane] : -1e38f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    gmin = fminf(gmin, __shfl_xor_sync(0xffffffffu, gmin, o));
+    gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
+  }
+
+  // ---- threshold ---------------------------------------------------------
+  const int keep = max(1, min(L, static_cast<int>(ceilf(retain_ratio * static_cast<float>(L)))));
+  float thr;
+  if (gmin >= gmax) {
+    thr = gmin - 1.0f;
+  } else {
+    float lo = gmin, hi = gmax;
+#pragma unroll 1
+    for (int it = 0; it < 32; ++it) {
+      const float mid = __fmaf_rn(hi - lo, 0.5f, lo);
+      int c = 0;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) c += (t0 + i < L && v[i] >= mid) ? 1 : 0;
+      c = warp_sum_i(c);
+      const int buf = it & 1;
+      if (lane == 0) red_i[buf][warp] = c;
+      __syncthreads();
+      int tot = lane < kEvictWarps ? red_i[buf][lane] : 0;
+      tot = warp_sum_i(tot);
+      if (tot >= keep) lo = mid; else hi = mid;
+    }
+    thr = lo;
+  }
+
+  // ---- zero evicted rows (partial pattern) ---------------------------------
+  const int64_t hd = static_cast<int64_t>(head_dim);
+  const int64_t table_size = static_cast<int64_t>(num_seqs) * max_blocks_per_seq;
+  int kept = 0;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int t = t0 + i;
+    if (t >= L) continue;
+    const bool evicted = v[i] < thr;
+    kept += evicted ? 0 : 1;
+    if (!evicted) continue;
+    const int lb = t / block_size;
+    const int pos = t - lb * block_size;
+    const int64_t flat = static_cast<int64_t>(seq) * max_blocks_per_seq + lb;
+    if (flat >= table_size) continue;
+    const int phys = block_tables[flat];
+    if (phys < 0 || phys >= total_pool_blocks) continue;
+    const int64_t base = ((static_cast<int64_t>(phys) * block_size + pos) * num_heads + head) * hd;
+    for (int d = t & 31; d < head_dim; d += 32) {
+      kpool[base + d] = __float2half_rn(0.f);
+      vpool[base + d] = __float2half_rn(0.f);
+    }
+  }
+  if (block_size == 1) {
+    // Only here can a block's vote reach block_size: token t == lb, counted
+    // when t % 32 == 0.  Votes follow every zeroing of this CTA.
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int t = t0 + i;
+      if (t >= L || (t & 31) != 0 || !(v[i] < thr)) continue;
+      const int64_t flat = static_cast<int64_t>(seq) * max_blocks_per_seq + t;
+      if (flat >= table_size) continue;
+      const int phys = block_tables[flat];
+      if (phys < 0 || phys >= total_pool_blocks) continue;
+      const int prev = atomicAdd(is_block_free + phys, 1);
+      if (prev + 1 == num_heads) block_tables[flat] = -1;
+    }
+  }
+
+  // ---- stream compaction of kept token indices ---------------------------
+  if (retained_idx != nullptr || retained_count != nullptr) {
+    int incl = kept;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    const int wt = lane < kEvictWarps ? warp_tot[lane] : 0;
+    int wincl = wt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wincl, o);
+      if (lane >= o) wincl += n;
+    }
+    const int warp_off = __shfl_sync(0xffffffffu, wincl - wt, warp);
+    const int total = __shfl_sync(0xffffffffu, wincl, 31);
+    int out = warp_off + incl - kept;
+    const int64_t pair = static_cast<int64_t>(seq) * num_heads + head;
+    if (retained_idx != nullptr) {
+      int32_t* dst = retained_idx + pair * L;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int t = t0 + i;
+        if (t < L && !(v[i] < thr)) dst[out++] = t;
+      }
+      for (int t = total + tid; t < L; t += kEvictThreads) dst[t] = -1;
+    }
+    if (retained_count != nullptr && tid == 0) retained_count[pair] = total;
+  }
+}
+
+// One thread per (physical block, head); heads fastest for coalesced reads.
+template <int BS>
+__global__ void __launch_bounds__(256)
+evict_cache_kernel(const float* __restrict__ scores, int num_blocks, int num_heads, int head_dim,
+                   __half* __restrict__ kpool, __half* __restrict__ vpool, float retain_ratio) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(num_blocks) * num_heads) return;
+  const int64_t blk = idx / num_heads;
+  const int head = static_cast<int>(idx - blk * num_heads);
+  float s[BS], w[BS];
+#pragma unroll
+  for (int p = 0; p < BS; ++p) {
+    s[p] = __ldg(scores + (blk * BS + p) * num_heads + head);
+    w[p] = s[p];
+  }
+  int keep = max(1, static_cast<int>(retain_ratio * static_cast<float>(BS)));
+  keep = min(keep, BS);
+  float thr = -1e38f;
+  for (int k = 0; k < keep; ++k) {
+    float best = -1e38f;
+    int best_pos = -1;
+#pragma unroll
+    for (int p = 0; p < BS; ++p) {
+      if (w[p] > best) {
+        best = w[p];
+        best_pos = p;
+      }
+    }
+    thr = best;
+#pragma unroll
+    for (int p = 0; p < BS; ++p)
+      if (p == best_pos) w[p] = -1e38f;
+  }
+  const int64_t hd = head_dim;
+  const bool vec = (head_dim % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(kpool) | reinterpret_cast<uintptr_t>(vpool)) & 15u) == 0;
+#pragma unroll
+  for (int p = 0; p < BS; ++p) {
+    if (!(s[p] < thr)) continue;
+    const int64_t base = ((blk * BS + p) * num_heads + head) * hd;
+    if (vec) {
+      uint4* kd = reinterpret_cast<uint4*>(kpool + base);
+      uint4* vd = reinterpret_cast<uint4*>(vpool + base);
+      for (int c = 0; c < head_dim / 8; ++c) {
+        kd[c] = make_uint4(0, 0, 0, 0);
+        vd[c] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      for (int d = 0; d < head_dim; ++d) {
+        kpool[base + d] = __float2half_rn(0.f);
+        vpool[base + d] = __float2half_rn(0.f);
+      }
+    }
+  }
+}
+
+// Any block size, no scratch: the repeated arg-max picks scores in
+// descending order (ties by position), with scores <= -1e38f or NaN acting as
+// -1e38f.  The keep-th pick is therefore the element whose rank
+//   #{q : w'[q] > w'[p]} + #{q < p : w'[q] == w'[p]}
+// equals keep-1, where w' is that normalised score.
+__global__ void __launch_bounds__(256)
+evict_cache_generic_kernel(const float* __restrict__ scores, int num_blocks, int block_size,
+                           int num_heads, int head_dim, __half* __restrict__ kpool,
+                           __half* __restrict__ vpool, float retain_ratio) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(num_blocks) * num_heads) return;
+  const int64_t blk = idx / num_heads;
+  const int head = static_cast<int>(idx - blk * num_heads);
+  auto at = [&](int p) {
+    const float x = scores[(blk * block_size + p) * num_heads + head];
+    return (x > -1e38f) ? x : -1e38f;
+  };
+  int keep = max(1, static_cast<int>(retain_ratio * static_cast<float>(block_size)));
+  keep = min(keep, block_size);
+  float thr = -1e38f;
+  for (int p = 0; p < block_size; ++p) {
+    const float wp = at(p);
+    int rank = 0;
+    for (int q = 0; q < block_size; ++q) {
+      const float wq = at(q);
+      rank += (wq > wp) || (q < p && wq == wp);
+    }
+    if (rank == keep - 1) {
+      thr = wp;
+      break;
+    }
+  }
+  for (int p = 0; p < block_size; ++p) {
+    if (!(scores[(blk * block_size + p) * num_heads + head] < thr)) continue;
+    const int64_t base = ((blk * block_size + p) * num_heads + head) * static_cast<int64_t>(head_dim);
+    for (int d = 0; d < head_dim; ++d) {
+      kpool[base + d] = __float2half_rn(0.f);
+      vpool[base + d] = __float2half_rn(0.f);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace memopt
+
+using namespace memopt;
+
+extern "C" int memopt_evict_tokens(const float* scores, int num_seqs, int num_heads, int seq_len,
+                                   int32_t* block_tables, int max_blocks_per_seq,
+                                   int32_t* is_block_free, int total_pool_blocks, void* key_pool,
+                                   void* value_pool, int pool_num_blocks, int block_size,
+                                   int head_dim, float retain_ratio, int num_sink_tokens,
+                                   int32_t* retained_idx, int32_t* retained_count, void* stream) {
+  if (!(retain_ratio > 0.f && retain_ratio <= 1.f))
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_tokens: retain_ratio must be in (0, 1]");
+  if (num_seqs < 0 || num_heads <= 0 || seq_len < 0 || max_blocks_per_seq < 0 ||
+      total_pool_blocks < 0 || block_size <= 0 || head_dim <= 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_tokens: invalid geometry");
+  if (total_pool_blocks > pool_num_blocks)
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_tokens: is_block_free size > pool.num_blocks");
+  if (seq_len > kMaxEvictLen)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "evict_tokens: seq_len exceeds 32768");
+  if (num_seqs == 0 || seq_len == 0) return MEMOPT_OK;
+  if (!scores || !block_tables || !is_block_free || !key_pool || !value_pool)
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_tokens: null pointer");
+  const int sinks = num_sink_tokens < 0 ? 0 : (num_sink_tokens > seq_len ? seq_len : num_sink_tokens);
+  const dim3 grid(num_seqs, num_heads);
+  cudaStream_t s = as_stream(stream);
+  const int vpt = (seq_len + kEvictThreads - 1) / kEvictThreads;
+#define MEMOPT_EVICT_LAUNCH(V)                                                                    \
+  evict_tokens_kernel<V><<<grid, kEvictThreads, 0, s>>>(                                        \
+      scores, num_seqs, num_heads, seq_len, block_tables, max_blocks_per_seq, is_block_free,     \
+      total_pool_blocks, reinterpret_cast<__half*>(key_pool), reinterpret_cast<__half*>(value_pool), \
+      block_size, head_dim, retain_ratio, sinks, retained_idx, retained_count)
+  if (vpt <= 1) MEMOPT_EVICT_LAUNCH(1);
+  else if (vpt <= 2) MEMOPT_EVICT_LAUNCH(2);
+  else if (vpt <= 4) MEMOPT_EVICT_LAUNCH(4);
+  else if (vpt <= 8) MEMOPT_EVICT_LAUNCH(8);
+  else if (vpt <= 16) MEMOPT_EVICT_LAUNCH(16);
+  else MEMOPT_EVICT_LAUNCH(32);
+#undef MEMOPT_EVICT_LAUNCH
+  MEMOPT_LAUNCH_CHECK("evict_tokens launch");
+  return MEMOPT_OK;
+}
+
+extern "C" int memopt_evict_cache(const float* scores, int num_blocks, int block_size,
+                                  int num_heads, int head_dim, void* key_pool, void* value_pool,
+                                  float retain_ratio, void* stream) {
+  if (!(retain_ratio > 0.f && retain_ratio <= 1.f))
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_cache: retain_ratio must be in (0, 1]");
+  if (num_blocks < 0 || block_size <= 0 || num_heads <= 0 || head_dim <= 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_cache: invalid geometry");
+  if (num_blocks == 0) return MEMOPT_OK;
+  if (!scores || !key_pool || !value_pool) return fail(MEMOPT_ERR_INVALID_ARG, "evict_cache: null pointer");
+  const int64_t n = static_cast<int64_t>(num_blocks) * num_heads;
+  const int grid = static_cast<int>((n + 255) / 256);
+  cudaStream_t s = as_stream(stream);
+  __half* k = reinterpret_cast<__half*>(key_pool);
+  __half* v = reinterpret_cast<__half*>(value_pool);
+  if (block_size == 16) {
+    evict_cache_kernel<16><<<grid, 256, 0, s>>>(scores, num_blocks, num_heads, head_dim, k, v, retain_ratio);
+  } else if (block_size == 32) {
+    evict_cache_kernel<32><<<grid, 256, 0, s>>>(scores, num_blocks, num_heads, head_dim, k, v, retain_ratio);
+  } else if (block_size == 8) {
+    evict_cache_kernel<8><<<grid, 256, 0, s>>>(scores, num_blocks, num_heads, head_dim, k, v, retain_ratio);
+  } else {
+    evict_cache_generic_kernel<<<grid, 256, 0, s>>>(scores, num_blocks, block_size, num_heads, head_dim,
+                                                    k, v, retain_ratio);
+  }
+  MEMOPT_LAUNCH_CHECK("evict_cache launch");
+  return MEMOPT_OK;
+}

@@ -1,0 +1,221 @@
+// write_cache.cu — scatter of new K/V tokens into the paged pool.
+//
+// Replaces write_cache_kernel (reference src/csrc/kv_cache.cu:228-260): the
+// reference moves one 2-byte element per thread with one CTA per token.  Here
+// one warp owns a token row and moves it with 16-byte vector accesses (a token
+// row of the reference layout [block, pos, head, dim] is contiguous in both
+// the input and the pool), several loads in flight per lane.
+//
+// The INT4 variant quantises while it writes (no reference counterpart for
+// the fusion; the per-group arithmetic follows quantization.cu:129-202) into
+// the head-major INT4 page format:
+//   codes  [num_blocks, num_heads, block_size, head_dim/2]  uint8
+//   scales [num_blocks, num_heads, block_size, head_dim/64] fp16
+#include "int4.cuh"
+
+namespace memopt {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ bool slot_ok(int32_t slot, int64_t num_slots) {
+  return slot >= 0 && static_cast<int64_t>(slot) < num_slots;
+}
+
+// Token rows of `chunks` 16-byte pieces; one warp per token.
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+write_cache_f16_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
+                       const int32_t* __restrict__ slots, int64_t num_tokens, int chunks,
+                       uint4* __restrict__ kpool, uint4* __restrict__ vpool, int64_t num_slots,
+                       int32_t* __restrict__ bad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  for (int64_t t = warp; t < num_tokens; t += nwarps) {
+    const int32_t slot = __ldg(slots + t);
+    if (!slot_ok(slot, num_slots)) {
+      if (lane == 0 && bad) atomicAdd(bad, 1);
+      continue;
+    }
+    const uint4* ksrc = keys + t * chunks;
+    const uint4* vsrc = values + t * chunks;
+    uint4* kdst = kpool + static_cast<int64_t>(slot) * chunks;
+    uint4* vdst = vpool + static_cast<int64_t>(slot) * chunks;
+    for (int c0 = lane; c0 < chunks; c0 += 32 * kUnroll) {
+      uint4 kv[kUnroll], vv[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32;
+        if (c < chunks) {
+          kv[u] = ld_stream_v4(ksrc + c);
+          vv[u] = ld_stream_v4(vsrc + c);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32;
+        if (c < chunks) {
+          kdst[c] = kv[u];
+          vdst[c] = vv[u];
+        }
+      }
+    }
+  }
+}
+
+// Generic element-wise scatter for rows that are not a multiple of 16 bytes
+// or not 16-byte aligned.
+__global__ void write_cache_f16_scalar_kernel(const __half* __restrict__ keys,
+                                              const __half* __restrict__ values,
+                                              const int32_t* __restrict__ slots,
+                                              int64_t num_tokens, int row,
+                                              __half* __restrict__ kpool,
+                                              __half* __restrict__ vpool, int64_t num_slots,
+                                              int32_t* __restrict__ bad) {
+  for (int64_t t = blockIdx.x; t < num_tokens; t += gridDim.x) {
+    const int32_t slot = slots[t];
+    if (!slot_ok(slot, num_slots)) {
+      if (threadIdx.x == 0 && bad) atomicAdd(bad, 1);
+      continue;
+    }
+    for (int i = threadIdx.x; i < row; i += blockDim.x) {
+      kpool[static_cast<int64_t>(slot) * row + i] = keys[t * row + i];
+      vpool[static_cast<int64_t>(slot) * row + i] = values[t * row + i];
+    }
+  }
+}
+
+// One warp per token; 8 lanes per 64-element group, 4 groups per warp step.
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
+                        const int32_t* __restrict__ slots, int64_t num_tokens, int num_heads,
+                        int head_dim, int block_size, int64_t num_slots,
+                        uint32_t* __restrict__ kcodes, __half* __restrict__ kscales,
+                        uint32_t* __restrict__ vcodes, __half* __restrict__ vscales,
+                        int32_t* __restrict__ bad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  const int gpr = head_dim / 64;                // groups per (token, head)
+  const int chunks = num_heads * head_dim / 8;  // 16-byte chunks per token row
+  for (int64_t t = warp; t < num_tokens; t += nwarps) {
+    const int32_t slot = __ldg(slots + t);
+    if (!slot_ok(slot, num_slots)) {
+      if (lane == 0 && bad) atomicAdd(bad, 1);
+      continue;
+    }
+    const int64_t blk = slot / block_size;
+    const int pos = slot - static_cast<int32_t>(blk * block_size);
+    const uint4* ksrc = keys + t * chunks;
+    const uint4* vsrc = values + t * chunks;
+    // chunks is a multiple of 8 (head_dim % 64 == 0), so every warp step
+    // covers whole groups and all lanes take the same trip count.
+    for (int c0 = 0; c0 < chunks; c0 += 32 * 2) {
+      uint4 kv[2], vv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < chunks) {
+          kv[u] = ld_stream_v4(ksrc + c);
+          vv[u] = ld_stream_v4(vsrc + c);
+        } else {
+          kv[u] = make_uint4(0, 0, 0, 0);
+          vv[u] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + u * 32 + lane;
+        float fk[8], fv[8];
+        unpack_half8(kv[u], fk);
+        unpack_half8(vv[u], fv);
+        const float sk = int4_scale_from_absmax(group8_absmax(fk));
+        const float sv = int4_scale_from_absmax(group8_absmax(fv));
+        if (c < chunks) {
+          const int g = c >> 3;  // group within the token row
+          const int h = g / gpr;
+          const int gi = g - h * gpr;
+          const int64_t row = (blk * num_heads + h) * block_size + pos;  // (blk, h, pos)
+          const int64_t word = row * (head_dim / 8) + gi * 8 + (c & 7);
+          kcodes[word] = int4_pack8(fk, sk);
+          vcodes[word] = int4_pack8(fv, sv);
+          if ((c & 7) == 0) {
+            kscales[row * gpr + gi] = __float2half_rn(sk);
+            vscales[row * gpr + gi] = __float2half_rn(sv);
+          }
+        }
+      }
+    }
+  }
+}
+
+int grid_for_tokens(int64_t num_tokens) {
+  const int64_t want = (num_tokens + kWarpsPerCta - 1) / kWarpsPerCta;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace memopt
+
+using namespace memopt;
+
+extern "C" int memopt_write_cache_f16(const void* keys, const void* values,
+                                      const int32_t* slot_mapping, int64_t num_tokens,
+                                      int num_heads, int head_dim, void* key_pool,
+                                      void* value_pool, int64_t num_blocks, int block_size,
+                                      int32_t* bad_slot_count, void* stream) {
+  if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || num_blocks < 0 || block_size <= 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "write_cache: invalid geometry");
+  if (num_tokens == 0) return MEMOPT_OK;
+  if (!keys || !values || !slot_mapping || !key_pool || !value_pool)
+    return fail(MEMOPT_ERR_INVALID_ARG, "write_cache: null pointer");
+  const int64_t num_slots = num_blocks * block_size;
+  const int row = num_heads * head_dim;
+  cudaStream_t s = as_stream(stream);
+  if (row % 8 == 0 && aligned16(keys) && aligned16(values) && aligned16(key_pool) &&
+      aligned16(value_pool)) {
+    write_cache_f16_kernel<<<grid_for_tokens(num_tokens), kWarpsPerCta * 32, 0, s>>>(
+        reinterpret_cast<const uint4*>(keys), reinterpret_cast<const uint4*>(values), slot_mapping,
+        num_tokens, row / 8, reinterpret_cast<uint4*>(key_pool), reinterpret_cast<uint4*>(value_pool),
+        num_slots, bad_slot_count);
+  } else {
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    write_cache_f16_scalar_kernel<<<static_cast<int>(num_tokens < cap ? num_tokens : cap), 256, 0, s>>>(
+        reinterpret_cast<const __half*>(keys), reinterpret_cast<const __half*>(values), slot_mapping,
+        num_tokens, row, reinterpret_cast<__half*>(key_pool), reinterpret_cast<__half*>(value_pool),
+        num_slots, bad_slot_count);
+  }
+  MEMOPT_LAUNCH_CHECK("write_cache_f16 launch");
+  return MEMOPT_OK;
+}
+
+extern "C" int memopt_write_cache_int4(const void* keys, const void* values,
+                                       const int32_t* slot_mapping, int64_t num_tokens,
+                                       int num_heads, int head_dim, uint8_t* key_codes,
+                                       void* key_scales, uint8_t* value_codes,
+                                       void* value_scales, int64_t num_blocks, int block_size,
+                                       int32_t* bad_slot_count, void* stream) {
+  if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || num_blocks < 0 || block_size <= 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: invalid geometry");
+  if (head_dim % 64 != 0)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "write_cache_int4: head_dim must be a multiple of 64");
+  if (num_tokens == 0) return MEMOPT_OK;
+  if (!keys || !values || !slot_mapping || !key_codes || !key_scales || !value_codes || !value_scales)
+    return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: null pointer");
+  if (!aligned16(keys) || !aligned16(values) || (reinterpret_cast<uintptr_t>(key_codes) & 3u) ||
+      (reinterpret_cast<uintptr_t>(value_codes) & 3u) || (reinterpret_cast<uintptr_t>(key_scales) & 1u) ||
+      (reinterpret_cast<uintptr_t>(value_scales) & 1u))
+    return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: misaligned pointer");
+  write_cache_int4_kernel<<<grid_for_tokens(num_tokens), kWarpsPerCta * 32, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint4*>(keys), reinterpret_cast<const uint4*>(values), slot_mapping,
+      num_tokens, num_heads, head_dim, block_size, num_blocks * block_size,
+      reinterpret_cast<uint32_t*>(key_codes), reinterpret_cast<__half*>(key_scales),
+      reinterpret_cast<uint32_t*>(value_codes), reinterpret_cast<__half*>(value_scales),
+      bad_slot_count);
+  MEMOPT_LAUNCH_CHECK("write_cache_int4 launch");
+  return MEMOPT_OK;
+}
