@@ -1,0 +1,259 @@
+// decode.cu — host side of dynamic_sparse_attention (paged decode path).
+//
+// Replaces the host dispatch of attention.cu:371-521: argument checks, window
+// clamp (attention.cu:453-455), scale 1/sqrtf(D) (:460), and dispatch on
+// (block_size, head_dim) in {16,32} x {64,128} (:494-507), but launches on the
+// caller's stream (the reference used the legacy default stream).
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "decode_kernel.cuh"
+
+namespace memopt {
+namespace {
+
+using decode::Cfg;
+using decode::Params;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D view of an fp16 pool [NB*BS rows][H][D]: box = one head, BS rows.
+int make_pool_map(CUtensorMap* map, const void* base, int64_t rows, int H, int D, int BS) {
+  auto fn = encode_fn();
+  if (!fn) return fail(MEMOPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(D), 1, static_cast<cuuint32_t>(BS)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MEMOPT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+  return MEMOPT_OK;
+}
+
+int clamp_window(int window_size, int max_seq_len) {
+  return (window_size <= 0 || window_size > max_seq_len) ? max_seq_len : window_size;
+}
+
+struct Split {
+  int chunk_pages = 32;
+  int n_chunks = 1;
+};
+
+// Chooses the page-chunk size so that the item count fills every warp slot of
+// the machine several times over (the tail wave stays small) while each item
+// still streams <= 32 pages.
+Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window) {
+  Split s;
+  const int64_t wpages =
+      window > 0 ? (static_cast<int64_t>(window) + block_size - 1) / block_size + 1 : 0;
+  int max_pages = static_cast<int>(wpages < max_blocks_per_seq ? wpages : max_blocks_per_seq);
+  if (max_pages < 1) max_pages = 1;
+  const int64_t warp_slots = static_cast<int64_t>(sm_count()) * 2 * 4;
+  const int64_t target = warp_slots * 4;
+  int64_t n = (target + pairs - 1) / pairs;
+  const int min_chunks = (max_pages + 31) / 32;
+  // Keep at least 4 pages per item so partials stay a small share of traffic.
+  const int max_chunks = max_pages >= 4 ? max_pages / 4 : 1;
+  if (n > max_chunks) n = max_chunks;
+  if (n < min_chunks) n = min_chunks;
+  if (n < 1) n = 1;
+  s.chunk_pages = static_cast<int>((max_pages + n - 1) / n);
+  s.n_chunks = (max_pages + s.chunk_pages - 1) / s.chunk_pages;
+  return s;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct WsLayout {
+  size_t tickets = 0, ml = 0, po = 0, total = 0;
+};
+
+WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
+  WsLayout w;
+  if (n_chunks <= 1) return w;
+  w.tickets = 0;
+  w.ml = align256(pairs * sizeof(int32_t));
+  w.po = w.ml + align256(pairs * n_chunks * sizeof(float2));
+  w.total = w.po + align256(static_cast<size_t>(pairs) * n_chunks * D * sizeof(float));
+  return w;
+}
+
+template <int D, int BS, bool INT4>
+int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int32_t* err,
+           cudaStream_t s) {
+  using C = Cfg<D, BS, INT4>;
+  auto kern = decode::paged_decode_kernel<D, BS, INT4>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t ctas_needed = (p.total_items + C::NW - 1) / C::NW;
+  const int per_sm = (227 * 1024) / C::SMEM >= 2 ? 2 : 1;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  kern<<<grid, C::NW * 32, C::SMEM, s>>>(p, km, vm, err);
+  MEMOPT_LAUNCH_CHECK("paged_decode_kernel launch");
+  return MEMOPT_OK;
+}
+
+int unsupported(int BS, int D) {
+  return fail(MEMOPT_ERR_UNSUPPORTED,
+              "dynamic_sparse_attention: unsupported (block_size=" + std::to_string(BS) +
+                  ", head_dim=" + std::to_string(D) +
+                  "). Supported combinations: block_size in {16,32}, head_dim in {64,128}.");
+}
+
+template <bool INT4>
+int dispatch(const Params& p, int D, int BS, const CUtensorMap& km, const CUtensorMap& vm,
+             int32_t* err, cudaStream_t s) {
+  if (D == 128 && BS == 16) return launch<128, 16, INT4>(p, km, vm, err, s);
+  if (D == 128 && BS == 32) return launch<128, 32, INT4>(p, km, vm, err, s);
+  if (D == 64 && BS == 16) return launch<64, 16, INT4>(p, km, vm, err, s);
+  if (D == 64 && BS == 32) return launch<64, 32, INT4>(p, km, vm, err, s);
+  return unsupported(BS, D);
+}
+
+int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t* ctx, int batch,
+                 int q_len, int H, int D, int MB, int64_t NB, int BS, int max_seq_len, int window,
+                 void* out, void* ws, size_t ws_bytes) {
+  if (batch < 0 || q_len < 0 || H < 0 || D < 0 || MB < 0 || NB < 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: negative size");
+  if (!((BS == 16 || BS == 32) && (D == 64 || D == 128))) return unsupported(BS, D);
+  if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: query/out must be 16-byte aligned");
+  p.q = reinterpret_cast<const __half*>(query);
+  p.out = reinterpret_cast<__half*>(out);
+  p.bt = bt;
+  p.ctx = ctx;
+  p.B = batch;
+  p.QL = q_len;
+  p.H = H;
+  p.MB = MB;
+  p.NB = NB;
+  p.window = clamp_window(window, max_seq_len);
+  p.qscale = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  const int64_t pairs = static_cast<int64_t>(batch) * q_len * H;
+  const Split sp = choose_split(pairs, MB, BS, p.window);
+  p.chunk_pages = sp.chunk_pages;
+  p.n_chunks = sp.n_chunks;
+  p.total_items = pairs * sp.n_chunks;
+  const WsLayout w = ws_layout(pairs, sp.n_chunks, D);
+  p.tickets = nullptr;
+  p.ml = nullptr;
+  p.po = nullptr;
+  if (w.total > 0) {
+    if (ws == nullptr || ws_bytes < w.total)
+      return fail(MEMOPT_ERR_WORKSPACE, "dynamic_sparse_attention: workspace too small (need " +
+                                            std::to_string(w.total) + " bytes)");
+    uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+    p.tickets = reinterpret_cast<int32_t*>(base + w.tickets);
+    p.ml = reinterpret_cast<float2*>(base + w.ml);
+    p.po = reinterpret_cast<float*>(base + w.po);
+  }
+  return MEMOPT_OK;
+}
+
+int zero_output(void* out, int batch, int q_len, int H, int D, void* stream) {
+  // No page can be visible: every output row is 0 (attention.cu:334).
+  cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(batch) * q_len * H * D * 2,
+                                  as_stream(stream));
+  return e == cudaSuccess ? MEMOPT_OK : cuda_fail(e, "dynamic_sparse_attention: zero output");
+}
+
+}  // namespace
+}  // namespace memopt
+
+using namespace memopt;
+
+extern "C" size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads,
+                                                        int head_dim, int max_blocks_per_seq,
+                                                        int block_size, int max_seq_len,
+                                                        int window_size) {
+  if (batch <= 0 || q_len <= 0 || num_heads <= 0 || head_dim <= 0 || block_size <= 0) return 0;
+  const int64_t pairs = static_cast<int64_t>(batch) * q_len * num_heads;
+  const Split sp =
+      choose_split(pairs, max_blocks_per_seq, block_size, clamp_window(window_size, max_seq_len));
+  return ws_layout(pairs, sp.n_chunks, head_dim).total;
+}
+
+extern "C" size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads) {
+  if (batch <= 0 || q_len <= 0 || num_heads <= 0) return 0;
+  return align256(static_cast<size_t>(batch) * q_len * num_heads * sizeof(int32_t));
+}
+
+extern "C" int memopt_paged_attention_f16(const void* query, const void* key_pool,
+                                          const void* value_pool, const int32_t* block_tables,
+                                          const int32_t* context_lens, int batch, int q_len,
+                                          int num_heads, int head_dim, int max_blocks_per_seq,
+                                          int64_t num_blocks, int block_size, int max_seq_len,
+                                          int window_size, void* out, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  Params p{};
+  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, head_dim,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, out,
+                        workspace, workspace_bytes);
+  if (st != MEMOPT_OK) return st;
+  if (p.total_items == 0) return MEMOPT_OK;
+  if (num_blocks == 0 || max_blocks_per_seq == 0)
+    return zero_output(out, batch, q_len, num_heads, head_dim, stream);
+  if ((reinterpret_cast<uintptr_t>(key_pool) | reinterpret_cast<uintptr_t>(value_pool)) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: pools must be 16-byte aligned");
+  if (num_blocks * block_size > 0x7fffffffLL)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: pool has more than 2^31 token rows");
+  alignas(64) CUtensorMap km, vm;
+  st = make_pool_map(&km, key_pool, num_blocks * block_size, num_heads, head_dim, block_size);
+  if (st != MEMOPT_OK) return st;
+  st = make_pool_map(&vm, value_pool, num_blocks * block_size, num_heads, head_dim, block_size);
+  if (st != MEMOPT_OK) return st;
+  return dispatch<false>(p, head_dim, block_size, km, vm, nullptr, as_stream(stream));
+}
+
+extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* key_codes,
+                                           const void* key_scales, const uint8_t* value_codes,
+                                           const void* value_scales, const int32_t* block_tables,
+                                           const int32_t* context_lens, int batch, int q_len,
+                                           int num_heads, int head_dim, int max_blocks_per_seq,
+                                           int64_t num_blocks, int block_size, int max_seq_len,
+                                           int window_size, void* out, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+  Params p{};
+  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, head_dim,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, out,
+                        workspace, workspace_bytes);
+  if (st != MEMOPT_OK) return st;
+  if (p.total_items == 0) return MEMOPT_OK;
+  if (num_blocks == 0 || max_blocks_per_seq == 0)
+    return zero_output(out, batch, q_len, num_heads, head_dim, stream);
+  if ((reinterpret_cast<uintptr_t>(key_codes) | reinterpret_cast<uintptr_t>(value_codes) |
+       reinterpret_cast<uintptr_t>(key_scales) | reinterpret_cast<uintptr_t>(value_scales)) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: pools must be 16-byte aligned");
+  p.kcodes = key_codes;
+  p.vcodes = value_codes;
+  p.kscales = reinterpret_cast<const __half*>(key_scales);
+  p.vscales = reinterpret_cast<const __half*>(value_scales);
+  alignas(64) CUtensorMap dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  return dispatch<true>(p, head_dim, block_size, dummy, dummy, nullptr, as_stream(stream));
+}

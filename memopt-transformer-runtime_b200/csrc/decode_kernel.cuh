@@ -1,0 +1,390 @@
+// decode_kernel.cuh — paged, block-skipping, split-K flash-decode for sm_100a.
+//
+// Semantics follow sparse_flash_attention_kernel (reference
+// src/csrc/attention.cu:98-339): for query row (b, q, h) the visible tokens
+// are [max(0, ctx_b - W), ctx_b) of every logical page whose block-table
+// entry is >= 0; no causal mask; out = sum_t softmax_t * V_t, or 0 when no
+// token is visible.  Pages whose entry is >= num_blocks are skipped as well
+// (the reference would read out of bounds there).
+//
+// Execution model (independent of the reference's one-CTA-per-row loop):
+//   * work item = (query row, chunk of <= 32 consecutive logical pages);
+//     each WARP processes items grid-strided, with no CTA-wide barriers;
+//   * every warp owns a ring of NS shared-memory stages; lane 0 streams the
+//     K/V pages of its items (crossing item boundaries) into the ring with
+//     the TMA engine (3-D tensor map for the fp16 pool, 1-D bulk copies for
+//     the contiguous INT4 pages) and mbarrier completion;
+//   * a lane owns 8 head dims; a page is consumed as rows of LPR = D/8 lanes,
+//     dot products are finished by a transpose-reduction (one value per lane
+//     after log2(LPR) butterfly rounds), the online softmax runs in the log2
+//     domain (q pre-scaled by log2(e)/sqrt(D)) with exp2f;
+//   * items of a row write (m, l, o[D]) partials; the last item to finish
+//     (atomic ticket) merges them in chunk order, so results are
+//     deterministic, and resets the ticket for the next call.
+#pragma once
+#include "common.cuh"
+
+namespace memopt {
+namespace decode {
+
+struct Params {
+  const __half* q;   // [B, QL, H, D]
+  __half* out;       // [B, QL, H, D]
+  const int32_t* bt;   // [B, MB]
+  const int32_t* ctx;  // [B]
+  // INT4 pool (head-major pages)
+  const uint8_t* kcodes;
+  const __half* kscales;
+  const uint8_t* vcodes;
+  const __half* vscales;
+  // split-K workspace
+  int32_t* tickets;  // [pairs]
+  float2* ml;        // [pairs * n_chunks]
+  float* po;         // [pairs * n_chunks * D]
+  int B, QL, H, MB;
+  int64_t NB;
+  int window;    // already clamped as in attention.cu:453-455
+  float qscale;  // log2(e) / sqrt(D)
+  int chunk_pages;  // <= 32
+  int n_chunks;
+  int64_t total_items;
+};
+
+template <int D, int BS, bool INT4>
+struct Cfg {
+  static constexpr int LPR = D / 8;     // lanes per page row
+  static constexpr int RPI = 32 / LPR;  // rows per warp instruction
+  static constexpr int TPL = BS / RPI;  // rows (tokens) per lane per page
+  static constexpr int DUP = LPR / TPL; // lanes holding the same score
+  static constexpr int K_BYTES = INT4 ? BS * D / 2 : BS * D * 2;
+  static constexpr int S_BYTES = INT4 ? BS * (D / 64) * 2 : 0;
+  static constexpr int STAGE_RAW = 2 * K_BYTES + 2 * S_BYTES;
+  static constexpr int STAGE = (STAGE_RAW + 127) / 128 * 128;
+  static constexpr int NS_RAW = 24576 / STAGE;
+  static constexpr int NS = NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW);
+  static constexpr int NW = 4;            // warps per CTA
+  static constexpr int BAR_BYTES = 1024;  // mbarriers
+  static constexpr int SMEM = BAR_BYTES + NW * NS * STAGE;
+  static_assert(TPL >= 1 && DUP >= 1, "unsupported geometry");
+  static_assert(NW * NS * 8 <= BAR_BYTES, "barrier area too small");
+};
+
+// Float value (c - 8) of nibble j of w, via the 2^23 magic-number trick.
+__device__ __forceinline__ float nib(uint32_t w, int j) {
+  return __int_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)) - 8388616.0f;
+}
+
+template <int D, int BS, bool INT4>
+__global__ void __launch_bounds__(Cfg<D, BS, INT4>::NW * 32)
+paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
+                    const __grid_constant__ CUtensorMap vmap, int32_t* __restrict__ err) {
+  using C = Cfg<D, BS, INT4>;
+  constexpr int NS = C::NS;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + wid * NS;
+  uint8_t* stages = smem + C::BAR_BYTES + wid * NS * C::STAGE;
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t st0 = smem_u32(stages);
+
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(bar0 + 8 * s, 1);
+    fence_mbar_init();
+    if (!INT4) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+    }
+  }
+  __syncwarp();
+
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * C::NW;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * C::NW + wid;
+
+  // Decodes an item and ballots the valid pages of its chunk (warp-uniform).
+  auto load_item = [&](int64_t item, uint32_t& mask, int& phys_lane, int& h, int& c_lo,
+                       int& win_start, int& ctx) {
+    const int64_t pair = item / p.n_chunks;
+    const int chunk = static_cast<int>(item - pair * p.n_chunks);
+    h = static_cast<int>(pair % p.H);
+    const int b = static_cast<int>(pair / (static_cast<int64_t>(p.H) * p.QL));
+    ctx = __ldg(p.ctx + b);
+    win_start = (p.window < ctx) ? (ctx - p.window) : 0;
+    int p_hi = 0;
+    if (ctx > 0) p_hi = min((ctx + BS - 1) / BS, p.MB);
+    const int p_lo = win_start / BS;
+    c_lo = p_lo + chunk * p.chunk_pages;
+    const int c_hi = min(c_lo + p.chunk_pages, p_hi);
+    const int page = c_lo + lane;
+    phys_lane = -1;
+    if (page < c_hi) phys_lane = __ldg(p.bt + static_cast<int64_t>(b) * p.MB + page);
+    const bool ok = page < c_hi && phys_lane >= 0 && static_cast<int64_t>(phys_lane) < p.NB;
+    mask = __ballot_sync(0xffffffffu, ok);
+  };
+
+  auto issue = [&](uint32_t seq, int phys, int h) {
+    const int s = static_cast<int>(seq % NS);
+    const uint32_t bar = bar0 + 8 * s;
+    const uint32_t dst = st0 + s * C::STAGE;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, C::STAGE_RAW);
+    if (!INT4) {
+      tma_load_3d(dst, &kmap, 0, h, phys * BS, bar);
+      tma_load_3d(dst + C::K_BYTES, &vmap, 0, h, phys * BS, bar);
+    } else {
+      const int64_t row = static_cast<int64_t>(phys) * p.H + h;
+      bulk_g2s(dst, p.kcodes + row * C::K_BYTES, C::K_BYTES, bar);
+      bulk_g2s(dst + C::K_BYTES, p.vcodes + row * C::K_BYTES, C::K_BYTES, bar);
+      bulk_g2s(dst + 2 * C::K_BYTES, reinterpret_cast<const uint8_t*>(p.kscales) + row * C::S_BYTES,
+               C::S_BYTES, bar);
+      bulk_g2s(dst + 2 * C::K_BYTES + C::S_BYTES,
+               reinterpret_cast<const uint8_t*>(p.vscales) + row * C::S_BYTES, C::S_BYTES, bar);
+    }
+  };
+
+  // ---------------- producer cursor (warp-uniform) ----------------------
+  int64_t p_item = first - nwarps;  // advanced before first use
+  uint32_t p_mask = 0;
+  int p_phys = -1;  // this lane's page entry for the producer's item
+  int p_h = 0;
+  uint32_t p_seq = 0;
+  bool p_done = false;
+
+  // Issues the next page of the warp's page stream (if any).
+  auto produce = [&]() {
+    while (!p_done && p_mask == 0) {
+      p_item += nwarps;
+      if (p_item >= p.total_items) {
+        p_done = true;
+        break;
+      }
+      int c_lo, ws, cx;
+      load_item(p_item, p_mask, p_phys, p_h, c_lo, ws, cx);
+    }
+    if (p_done) return;
+    const int j = __ffs(p_mask) - 1;
+    p_mask &= p_mask - 1;
+    const int phys = __shfl_sync(0xffffffffu, p_phys, j);
+    if (lane == 0) issue(p_seq, phys, p_h);
+    ++p_seq;
+  };
+
+  for (int s = 0; s < NS; ++s) produce();
+
+  // ---------------- consumer -------------------------------------------
+  const int r = lane / C::LPR;   // row within a warp instruction
+  const int cl = lane % C::LPR;  // 8-dim column chunk
+  uint32_t c_seq = 0;
+  bool failed = false;
+
+  for (int64_t item = first; item < p.total_items && !failed; item += nwarps) {
+    uint32_t mask;
+    int phys_lane, h, c_lo, win_start, ctx;
+    load_item(item, mask, phys_lane, h, c_lo, win_start, ctx);
+    const int64_t pair = item / p.n_chunks;
+
+    float q[8];
+    {
+      const uint4 qv = *reinterpret_cast<const uint4*>(p.q + pair * D + cl * 8);
+      const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(q2[i]);
+        q[2 * i] = f.x * p.qscale;
+        q[2 * i + 1] = f.y * p.qscale;
+      }
+    }
+    float m = -INFINITY, l = 0.f;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+
+    while (mask != 0) {
+      const int jpage = __ffs(mask) - 1;
+      mask &= mask - 1;
+      const int page = c_lo + jpage;
+      const int s = static_cast<int>(c_seq % NS);
+      const uint32_t parity = (c_seq / NS) & 1u;
+      // Warp-uniform bounded wait (a completed phase stays observable).
+      uint32_t polls = 0;
+      bool ready = mbar_try_wait(bar0 + 8 * s, parity);
+      while (!__all_sync(0xffffffffu, ready) && ++polls < kMaxPolls) {
+        if (!ready) ready = mbar_try_wait(bar0 + 8 * s, parity);
+      }
+      if (!__all_sync(0xffffffffu, ready)) {
+        failed = true;
+        break;
+      }
+      const uint8_t* stg = stages + s * C::STAGE;
+
+      // ---- scores: lane partials for TPL rows, then transpose-reduce ----
+      float val[C::TPL];
+#pragma unroll
+      for (int i = 0; i < C::TPL; ++i) {
+        const int t = i * C::RPI + r;
+        if (!INT4) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(stg + t * D * 2 + cl * 16);
+          const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(k2[e]);
+            acc = fmaf(q[2 * e], f.x, acc);
+            acc = fmaf(q[2 * e + 1], f.y, acc);
+          }
+          val[i] = acc;
+        } else {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(stg + t * (D / 2) + cl * 4);
+          const float ks = __half2float(*reinterpret_cast<const __half*>(
+              stg + 2 * C::K_BYTES + (t * (D / 64) + cl / 8) * 2));
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(q[e], nib(w, e), acc);
+          val[i] = acc * ks;
+        }
+      }
+      int idx = 0;
+      {
+        int n = C::TPL;
+#pragma unroll
+        for (int mk = C::LPR / 2; mk >= 1; mk >>= 1) {
+          if (n > 1) {
+            const int half = n / 2;
+            const bool up = (lane & mk) != 0;
+#pragma unroll
+            for (int i = 0; i < (C::TPL + 1) / 2; ++i) {
+              if (i < half) {
+                const float send = up ? val[i] : val[i + half];
+                const float keepv = up ? val[i + half] : val[i];
+                val[i] = keepv + __shfl_xor_sync(0xffffffffu, send, mk);
+              }
+            }
+            if (up) idx += half;
+            n = half;
+          } else {
+            val[0] += __shfl_xor_sync(0xffffffffu, val[0], mk);
+          }
+        }
+      }
+      const int tok = page * BS + idx * C::RPI + r;
+      const float s2 = (tok >= win_start && tok < ctx) ? val[0] : -INFINITY;
+      float mp = s2;
+#pragma unroll
+      for (int mk = 16; mk >= 1; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
+      const float m_new = fmaxf(m, mp);
+      if (m_new != -INFINITY) {
+        const float alpha = exp2f(m - m_new);
+        const float pr = exp2f(s2 - m_new);
+        const bool dup = (lane & (C::DUP - 1)) != 0;
+        l = l * alpha + (dup ? 0.f : pr);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] *= alpha;
+        m = m_new;
+        // ---- P.V ----
+#pragma unroll
+        for (int i = 0; i < C::TPL; ++i) {
+          const int t = i * C::RPI + r;
+          float pi = __shfl_sync(0xffffffffu, pr, r * C::LPR + i * C::DUP);
+          if (!INT4) {
+            const uint4 vv = *reinterpret_cast<const uint4*>(stg + C::K_BYTES + t * D * 2 + cl * 16);
+            const __half2* v2 = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(v2[e]);
+              o[2 * e] = fmaf(pi, f.x, o[2 * e]);
+              o[2 * e + 1] = fmaf(pi, f.y, o[2 * e + 1]);
+            }
+          } else {
+            const uint32_t w =
+                *reinterpret_cast<const uint32_t*>(stg + C::K_BYTES + t * (D / 2) + cl * 4);
+            const float vs = __half2float(*reinterpret_cast<const __half*>(
+                stg + 2 * C::K_BYTES + C::S_BYTES + (t * (D / 64) + cl / 8) * 2));
+            pi *= vs;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, nib(w, e), o[e]);
+          }
+        }
+      }
+      __syncwarp();
+      ++c_seq;
+      produce();
+    }
+    if (failed) break;
+
+    // ---- finish the item: reduce o over row groups, l over lanes ----------
+#pragma unroll
+    for (int mk = C::LPR; mk < 32; mk <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] += __shfl_xor_sync(0xffffffffu, o[j], mk);
+    }
+#pragma unroll
+    for (int mk = 16; mk >= 1; mk >>= 1) l += __shfl_xor_sync(0xffffffffu, l, mk);
+
+    if (p.n_chunks == 1) {
+      if (r == 0) {
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        uint4 ov;
+        __half2* o2 = reinterpret_cast<__half2*>(&ov);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o2[e] = __floats2half2_rn(o[2 * e] * inv, o[2 * e + 1] * inv);
+        *reinterpret_cast<uint4*>(p.out + pair * D + cl * 8) = ov;
+      }
+      continue;
+    }
+    if (r == 0) {
+      float4* dst = reinterpret_cast<float4*>(p.po + item * D + cl * 8);
+      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    }
+    if (lane == 0) p.ml[item] = make_float2(m, l);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = (atomicAdd(p.tickets + pair, 1) == p.n_chunks - 1);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) continue;
+    __threadfence();
+    // ---- merge the row's partials in chunk order ----
+    const int64_t base = pair * p.n_chunks;
+    float M = -INFINITY;
+    for (int c = lane; c < p.n_chunks; c += 32) M = fmaxf(M, __ldcg(&p.ml[base + c].x));
+#pragma unroll
+    for (int mk = 16; mk >= 1; mk >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, mk));
+    constexpr int DPL = D / 32;  // dims per lane in the merge
+    float acc[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+    float L = 0.f;
+    if (M != -INFINITY) {
+      for (int c = 0; c < p.n_chunks; ++c) {
+        const float2 mlc = __ldcg(&p.ml[base + c]);
+        const float w = exp2f(mlc.x - M);
+        L = fmaf(w, mlc.y, L);
+        const float* src = p.po + (base + c) * D + lane * DPL;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(w, __ldcg(src + j), acc[j]);
+      }
+    }
+    const float inv = (L > 0.f) ? 1.f / L : 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; j += 2) {
+      *reinterpret_cast<__half2*>(p.out + pair * D + lane * DPL + j) =
+          __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
+    }
+    if (lane == 0) p.tickets[pair] = 0;
+  }
+
+  if (failed) {
+    if (lane == 0 && err) atomicExch(err, 1);
+    // Drain the copies this warp still has in flight before leaving.
+    for (; c_seq < p_seq; ++c_seq) {
+      const int s = static_cast<int>(c_seq % NS);
+      uint32_t polls = 0;
+      while (!mbar_try_wait(bar0 + 8 * s, (c_seq / NS) & 1u) && ++polls < kMaxPolls) {
+      }
+    }
+  }
+}
+
+}  // namespace decode
+}  // namespace memopt
