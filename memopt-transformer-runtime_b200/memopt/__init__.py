@@ -20,14 +20,14 @@ _here = _os.path.dirname(_os.path.dirname(_os.path.abspath(__file__)))
 if _here not in _sys.path:
     _sys.path.insert(0, _here)
 
+import torch as _torch  # noqa: E402  (loads libc10/libtorch for memopt_C)
+
 try:
     import memopt_C  # noqa: F401
 
     _C_AVAILABLE = True
 except ImportError as _e:  # pragma: no cover - exercised only on broken installs
     _C_AVAILABLE = False
-    import torch as _torch
-
     if _torch.cuda.is_available():
         raise ImportError(
             "memopt: the CUDA extension memopt_C could not be loaded on a CUDA machine "

@@ -1,0 +1,145 @@
+"""ctypes/numpy front end of the CPU oracle (memopt_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: used by tests/, ``__graft_entry__.smoke()`` and the
+CPU-baseline leg of bench.py as the checker.  Arrays are numpy; fp16 data is
+passed as ``np.float16``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "memopt_oracle.c")
+LIB = os.path.join(HERE, "liboracle.so")
+CFLAGS = ["-O2", "-fopenmp", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared"]
+
+
+def build() -> str:
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
+        tmp = LIB + ".tmp"
+        subprocess.run(["gcc", *CFLAGS, SRC, "-o", tmp, "-lm"], check=True)
+        os.replace(tmp, LIB)
+    return LIB
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        _lib = C.CDLL(LIB)
+        _lib.oracle_f16_to_f32.restype = C.c_float
+        _lib.oracle_f16_to_f32.argtypes = [C.c_uint16]
+        _lib.oracle_f32_to_f16.restype = C.c_uint16
+        _lib.oracle_f32_to_f16.argtypes = [C.c_float]
+    return _lib
+
+
+def _p(a: np.ndarray) -> C.c_void_p:
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return C.c_void_p(a.ctypes.data)
+
+
+I64, I32, F32 = C.c_int64, C.c_int, C.c_float
+_c = np.ascontiguousarray
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return int(lib().oracle_f32_to_f16(C.c_float(x)))
+
+
+def f16_bits_to_f32(b: int) -> float:
+    return float(lib().oracle_f16_to_f32(C.c_uint16(b)))
+
+
+def quantize_int4(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Reference quantize_kv_cache_int4: packed (shape[..., D/2]) and fp32 scales."""
+    x = _c(x, dtype=np.float16)
+    n = x.size
+    packed = np.zeros(x.shape[:-1] + (x.shape[-1] // 2,), np.uint8)
+    scales = np.zeros(n // 64, np.float32)
+    lib().oracle_quantize_int4(_p(x), I64(n), _p(packed), _p(scales))
+    return packed, scales
+
+
+def dequantize_int4(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    packed = _c(packed, dtype=np.uint8)
+    scales = _c(scales, dtype=np.float32)
+    out = np.zeros(packed.shape[:-1] + (packed.shape[-1] * 2,), np.float16)
+    lib().oracle_dequantize_int4(_p(packed), _p(scales), I64(out.size), _p(out))
+    return out
+
+
+def write_cache_f16(keys, values, slots, kpool, vpool) -> None:
+    """In place on kpool/vpool [NB, BS, H, D] fp16 (C-contiguous numpy)."""
+    T, H, D = keys.shape
+    NB, BS = kpool.shape[0], kpool.shape[1]
+    keys, values, slots = _c(keys, np.float16), _c(values, np.float16), _c(slots, np.int32)
+    lib().oracle_write_cache_f16(_p(keys), _p(values), _p(slots), I64(T), I32(H), I32(D),
+                                 _p(kpool), _p(vpool), I64(NB), I32(BS))
+
+
+def write_cache_int4(keys, values, slots, kcodes, kscales, vcodes, vscales) -> None:
+    """In place on INT4 pages: codes [NB, H, BS, D/2] u8, scales [NB, H, BS, D/64] fp16."""
+    T, H, D = keys.shape
+    NB, BS = kcodes.shape[0], kcodes.shape[2]
+    keys, values, slots = _c(keys, np.float16), _c(values, np.float16), _c(slots, np.int32)
+    lib().oracle_write_cache_int4(_p(keys), _p(values), _p(slots), I64(T), I32(H), I32(D),
+                                  _p(kcodes), _p(kscales), _p(vcodes), _p(vscales), I64(NB), I32(BS))
+
+
+def evict_tokens(scores, block_tables, is_block_free, kpool, vpool, retain_ratio, num_sink_tokens=4):
+    """In place on block_tables / is_block_free / pools.  Returns (idx, cnt, thr)."""
+    scores = _c(scores, np.float32)
+    S, H, L = scores.shape
+    MB = block_tables.shape[1]
+    NBF = is_block_free.shape[0]
+    BS, D = kpool.shape[1], kpool.shape[3]
+    idx = np.full((S, H, L), -1, np.int32)
+    cnt = np.zeros((S, H), np.int32)
+    thr = np.zeros((S, H), np.float32)
+    lib().oracle_evict_tokens(_p(scores), I32(S), I32(H), I32(L), _p(block_tables), I32(MB),
+                              _p(is_block_free), I32(NBF), _p(kpool), _p(vpool), I32(BS), I32(D),
+                              F32(retain_ratio), I32(num_sink_tokens), _p(idx), _p(cnt), _p(thr))
+    return idx, cnt, thr
+
+
+def evict_cache(scores, kpool, vpool, retain_ratio) -> None:
+    scores = _c(scores, np.float32)
+    NB, BS, H = scores.shape
+    D = kpool.shape[3]
+    lib().oracle_evict_cache(_p(scores), I32(NB), I32(BS), I32(H), I32(D), _p(kpool), _p(vpool),
+                             F32(retain_ratio))
+
+
+def paged_attention_f16(q, kpool, vpool, block_tables, context_lens, max_seq_len, window_size):
+    """fp64 output [B, QL, H, D]."""
+    q = _c(q, np.float16)
+    B, QL, H, D = q.shape
+    NB, BS = kpool.shape[0], kpool.shape[1]
+    bt, cl = _c(block_tables, np.int32), _c(context_lens, np.int32)
+    out = np.zeros((B, QL, H, D), np.float64)
+    lib().oracle_paged_attention_f16(_p(q), _p(_c(kpool)), _p(_c(vpool)), _p(bt), _p(cl), I32(B),
+                                     I32(QL), I32(H), I32(D), I32(bt.shape[1]), I64(NB), I32(BS),
+                                     I32(max_seq_len), I32(window_size), _p(out))
+    return out
+
+
+def paged_attention_int4(q, kcodes, kscales, vcodes, vscales, block_tables, context_lens,
+                         max_seq_len, window_size):
+    q = _c(q, np.float16)
+    B, QL, H, D = q.shape
+    NB, BS = kcodes.shape[0], kcodes.shape[2]
+    bt, cl = _c(block_tables, np.int32), _c(context_lens, np.int32)
+    out = np.zeros((B, QL, H, D), np.float64)
+    lib().oracle_paged_attention_int4(_p(q), _p(_c(kcodes)), _p(_c(kscales)), _p(_c(vcodes)),
+                                      _p(_c(vscales)), _p(bt), _p(cl), I32(B), I32(QL), I32(H), I32(D),
+                                      I32(bt.shape[1]), I64(NB), I32(BS), I32(max_seq_len),
+                                      I32(window_size), _p(out))
+    return out
