@@ -1,0 +1,262 @@
+"""GPU parity: every kernel, called through the C-ABI, against the CPU oracle.
+
+Bit-exact for codes, scales, written pages, block tables, vote counters and
+retained-token indices; attention within 2e-3 absolute + 1e-2 relative of the
+fp64 oracle (the tolerance stated for fp16 attention outputs).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import capi
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+DEV = "cuda"
+
+
+def np16(t):
+    return t.detach().cpu().numpy()
+
+
+# ----------------------------------------------------------------- quant
+@pytest.mark.parametrize("shape", [(64,), (4, 128), (2, 8, 64), (2, 4, 8, 64), (3, 1000, 64), (7, 32, 128)])
+@pytest.mark.parametrize("dist", ["normal", "uniform", "small", "large", "zeros", "const"])
+def test_quantize_bit_exact(shape, dist):
+    g = torch.Generator(device="cpu").manual_seed(hash((shape, dist)) & 0xFFFF)
+    if dist == "normal":
+        x = torch.randn(shape, generator=g)
+    elif dist == "uniform":
+        x = torch.rand(shape, generator=g) * 2 - 1
+    elif dist == "small":
+        x = torch.rand(shape, generator=g) * 0.2 - 0.1
+    elif dist == "large":
+        x = torch.rand(shape, generator=g) * 200 - 100
+    elif dist == "zeros":
+        x = torch.zeros(shape)
+    else:
+        x = torch.full(shape, 0.5)
+    x = x.half()
+    p, s = capi.quantize(x.to(DEV))
+    pr, sr = O.quantize_int4(x.numpy())
+    assert np.array_equal(np16(p), pr)
+    assert np.array_equal(np16(s).view(np.uint32), sr.view(np.uint32))
+    d = capi.dequantize(p, s)
+    dr = O.dequantize_int4(pr, sr)
+    assert np.array_equal(np16(d).view(np.uint16), dr.view(np.uint16))
+
+
+def test_quantize_special_values():
+    x = torch.zeros(8, 64)
+    x[0, 3] = float("inf")
+    x[1, 5] = float("nan")
+    x[2] = torch.linspace(-65504, 65504, 64)
+    x[3, :] = 6e-8  # fp16 subnormals
+    x[4, ::2] = 2.5
+    x[4, 1] = 7.0
+    x = x.half()
+    p, s = capi.quantize(x.to(DEV))
+    pr, sr = O.quantize_int4(x.numpy())
+    assert np.array_equal(np16(p), pr)
+    assert np.array_equal(np16(s).view(np.uint32), sr.view(np.uint32))
+
+
+# ------------------------------------------------------------ write_cache
+def _slots(T, NB, BS, seed, bad=0):
+    rng = np.random.default_rng(seed)
+    s = rng.choice(NB * BS, size=T, replace=False).astype(np.int32)
+    if bad:
+        s[rng.choice(T, size=bad, replace=False)] = rng.choice([-1, NB * BS, NB * BS + 7, -100], size=bad)
+    return s
+
+
+@pytest.mark.parametrize("T,H,D,NB,BS", [(1, 8, 64, 4, 16), (100, 8, 64, 20, 16), (333, 32, 128, 64, 16),
+                                          (77, 4, 128, 10, 32), (50, 3, 10, 8, 16)])
+def test_write_cache_f16_bit_exact(T, H, D, NB, BS):
+    rng = np.random.default_rng(T)
+    k = rng.standard_normal((T, H, D)).astype(np.float16)
+    v = rng.standard_normal((T, H, D)).astype(np.float16)
+    s = _slots(T, NB, BS, T, bad=min(3, T - 1))
+    kp = np.zeros((NB, BS, H, D), np.float16)
+    vp = np.zeros_like(kp)
+    O.write_cache_f16(k, v, s, kp, vp)
+    gk = torch.zeros(NB, BS, H, D, dtype=torch.float16, device=DEV)
+    gv = torch.zeros_like(gk)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    capi.write_cache_f16(torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV), torch.from_numpy(s).to(DEV),
+                         gk, gv, bad)
+    assert np.array_equal(np16(gk), kp) and np.array_equal(np16(gv), vp)
+    assert int(bad.item()) == int(((s < 0) | (s >= NB * BS)).sum())
+
+
+@pytest.mark.parametrize("T,H,D,NB,BS", [(1, 8, 64, 4, 16), (129, 8, 64, 20, 16), (300, 32, 128, 64, 16),
+                                          (77, 4, 128, 10, 32), (40, 2, 192, 8, 16)])
+def test_write_cache_int4_bit_exact(T, H, D, NB, BS):
+    rng = np.random.default_rng(T + 1)
+    k = rng.standard_normal((T, H, D)).astype(np.float16)
+    v = (rng.standard_normal((T, H, D)) * 3).astype(np.float16)
+    k[0, 0, :64] = 0  # all-zero group -> scale 1.0
+    s = _slots(T, NB, BS, T + 1, bad=min(2, T - 1))
+    kc = np.zeros((NB, H, BS, D // 2), np.uint8)
+    vc = np.zeros_like(kc)
+    ks = np.zeros((NB, H, BS, D // 64), np.float16)
+    vs = np.zeros_like(ks)
+    O.write_cache_int4(k, v, s, kc, ks, vc, vs)
+    g = {n: torch.from_numpy(a.copy()).to(DEV) for n, a in dict(kc=kc * 0, ks=ks * 0, vc=vc * 0, vs=vs * 0).items()}
+    capi.write_cache_int4(torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV), torch.from_numpy(s).to(DEV),
+                          g["kc"], g["ks"], g["vc"], g["vs"])
+    assert np.array_equal(np16(g["kc"]), kc) and np.array_equal(np16(g["vc"]), vc)
+    assert np.array_equal(np16(g["ks"]).view(np.uint16), ks.view(np.uint16))
+    assert np.array_equal(np16(g["vs"]).view(np.uint16), vs.view(np.uint16))
+    # codes agree with the standalone reference quantizer on each (token, head) row
+    ok_t = [i for i in range(T) if 0 <= s[i] < NB * BS]
+    t = ok_t[0]
+    pr, sr = O.quantize_int4(k[t])
+    blk, pos = divmod(int(s[t]), BS)
+    assert np.array_equal(kc[blk, :, pos, :], pr.reshape(H, D // 2))
+    assert np.array_equal(ks[blk, :, pos, :].astype(np.float32).reshape(-1), sr.astype(np.float16).astype(np.float32))
+
+
+# ------------------------------------------------------------ evict_tokens
+def _evict_case(S, H, L, BS, D, r, sinks, seed, dist="lognormal", extra_pages=3, holes=False):
+    rng = np.random.default_rng(seed)
+    if dist == "lognormal":
+        sc = rng.lognormal(0, 1, (S, H, L)).astype(np.float32)
+    elif dist == "ties":
+        sc = rng.integers(0, 4, (S, H, L)).astype(np.float32)
+    elif dist == "const":
+        sc = np.full((S, H, L), 2.0, np.float32)
+    else:
+        sc = rng.standard_normal((S, H, L)).astype(np.float32)
+    MB = (L + BS - 1) // BS
+    NB = S * MB + extra_pages
+    bt = rng.permutation(NB)[: S * MB].astype(np.int32).reshape(S, MB)
+    if holes:
+        bt[rng.random(bt.shape) < 0.1] = -1
+    kp = rng.standard_normal((NB, BS, H, D)).astype(np.float16)
+    vp = rng.standard_normal((NB, BS, H, D)).astype(np.float16)
+    return sc, bt, kp, vp
+
+
+@pytest.mark.parametrize("S,H,L,BS,D,r,sinks,dist,holes", [
+    (2, 4, 512, 16, 64, 0.75, 4, "lognormal", False),
+    (2, 4, 512, 16, 64, 0.75, 0, "lognormal", False),
+    (3, 2, 1000, 16, 128, 0.5, 0, "normal", True),
+    (1, 8, 4096, 16, 128, 0.75, 0, "lognormal", False),
+    (2, 2, 777, 32, 64, 0.3, 2, "ties", False),
+    (1, 2, 100, 16, 64, 1.0, 0, "normal", False),
+    (1, 2, 100, 16, 64, 0.01, 0, "normal", False),
+    (1, 2, 64, 16, 64, 0.5, 0, "const", False),
+    (1, 3, 1, 16, 64, 0.5, 0, "normal", False),
+    (2, 2, 32768, 16, 64, 0.75, 0, "lognormal", False),
+    (2, 2, 32768, 16, 64, 0.75, 4, "lognormal", False),
+    (1, 2, 300, 1, 32, 0.5, 0, "normal", False),
+])
+def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
+    sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + S, dist, holes=holes)
+    NB = kp.shape[0]
+    ibf = np.zeros(NB, np.int32)
+    gk, gv = torch.from_numpy(kp).to(DEV), torch.from_numpy(vp).to(DEV)
+    gbt, gibf = torch.from_numpy(bt).to(DEV), torch.from_numpy(ibf).to(DEV)
+    idx, cnt = capi.evict_tokens(torch.from_numpy(sc).to(DEV), gbt, gibf, gk, gv, r, sinks)
+    ridx, rcnt, _ = O.evict_tokens(sc, bt, ibf, kp, vp, r, sinks)
+    assert np.array_equal(np16(cnt), rcnt)
+    assert np.array_equal(np16(idx), ridx)
+    assert np.array_equal(np16(gbt), bt)
+    assert np.array_equal(np16(gibf), ibf)
+    assert np.array_equal(np16(gk).view(np.uint16), kp.view(np.uint16))
+    assert np.array_equal(np16(gv).view(np.uint16), vp.view(np.uint16))
+
+
+@pytest.mark.parametrize("NB,BS,H,D,r", [(10, 16, 4, 64, 0.75), (7, 32, 3, 128, 0.5), (5, 8, 2, 64, 0.9),
+                                         (6, 5, 2, 64, 0.6), (3, 16, 2, 64, 0.01)])
+def test_evict_cache_bit_exact(NB, BS, H, D, r):
+    rng = np.random.default_rng(NB * BS)
+    sc = rng.integers(0, 5, (NB, BS, H)).astype(np.float32)  # many ties
+    sc[0, 0, 0] = np.nan
+    kp = rng.standard_normal((NB, BS, H, D)).astype(np.float16)
+    vp = rng.standard_normal((NB, BS, H, D)).astype(np.float16)
+    gk, gv = torch.from_numpy(kp).to(DEV), torch.from_numpy(vp).to(DEV)
+    capi.evict_cache(torch.from_numpy(sc).to(DEV), gk, gv, r)
+    O.evict_cache(sc, kp, vp, r)
+    assert np.array_equal(np16(gk).view(np.uint16), kp.view(np.uint16))
+    assert np.array_equal(np16(gv).view(np.uint16), vp.view(np.uint16))
+
+
+# --------------------------------------------------------------- attention
+def _attn_case(B, QL, H, D, BS, ctx, MB, seed, holes=0.0, dist="normal"):
+    rng = np.random.default_rng(seed)
+    NB = B * MB + 5
+    bt = rng.permutation(NB)[: B * MB].astype(np.int32).reshape(B, MB)
+    if holes:
+        bt[rng.random(bt.shape) < holes] = -1
+        bt[0, 0] = NB + 3  # beyond the pool: skipped like -1
+    f = (lambda s: rng.standard_normal(s)) if dist == "normal" else (lambda s: rng.random(s))
+    kp = f((NB, BS, H, D)).astype(np.float16)
+    vp = f((NB, BS, H, D)).astype(np.float16)
+    q = f((B, QL, H, D)).astype(np.float16)
+    return q, kp, vp, bt, np.asarray(ctx, np.int32)
+
+
+ATTN_CASES = [
+    # B, QL, H, D, BS, ctx, MB, max_seq_len, window, holes
+    (2, 1, 8, 64, 16, [512, 512], 32, 512, 512, 0.0),
+    (3, 1, 4, 128, 16, [1, 17, 300], 20, 320, 320, 0.0),
+    (2, 1, 4, 128, 32, [1000, 64], 40, 1280, 100, 0.0),
+    (2, 3, 4, 64, 32, [300, 301], 10, 320, -1, 0.2),
+    (4, 1, 2, 128, 16, [0, 5, 4096, 4095], 256, 4096, 4096, 0.0),
+    (1, 2, 2, 64, 16, [4096], 256, 4096, 77, 0.1),
+    (2, 1, 4, 128, 16, [700, 900], 64, 1024, 0, 0.0),
+    (2, 1, 32, 128, 16, [4096, 4000], 256, 4096, 4096, 0.0),
+    (1, 1, 2, 128, 16, [40000], 2500, 40000, 40000, 0.0),
+    (2, 1, 2, 64, 16, [100, 100], 8, 128, 128, 0.0),  # ctx beyond the table
+]
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_attention_f16_vs_oracle(case):
+    B, QL, H, D, BS, ctx, MB, msl, win, holes = case
+    q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, sum(ctx) + H, holes)
+    got = capi.attention_f16(torch.from_numpy(q).to(DEV), torch.from_numpy(kp).to(DEV),
+                             torch.from_numpy(vp).to(DEV), torch.from_numpy(bt).to(DEV),
+                             torch.from_numpy(cl).to(DEV), msl, win)
+    ref = O.paged_attention_f16(q, kp, vp, bt, cl, msl, win)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_attention_int4_vs_oracle(case):
+    B, QL, H, D, BS, ctx, MB, msl, win, holes = case
+    q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, sum(ctx) + H + 1, holes)
+    NB = kp.shape[0]
+    # Fill the INT4 pages from the fp16 pool rows with the fused writer.
+    T = NB * BS
+    keys = kp.reshape(T, H, D)
+    vals = vp.reshape(T, H, D)
+    slots = np.arange(T, dtype=np.int32)
+    gkc = torch.zeros(NB, H, BS, D // 2, dtype=torch.uint8, device=DEV)
+    gvc = torch.zeros_like(gkc)
+    gks = torch.zeros(NB, H, BS, D // 64, dtype=torch.float16, device=DEV)
+    gvs = torch.zeros_like(gks)
+    capi.write_cache_int4(torch.from_numpy(keys).to(DEV), torch.from_numpy(vals).to(DEV),
+                          torch.from_numpy(slots).to(DEV), gkc, gks, gvc, gvs)
+    got = capi.attention_int4(torch.from_numpy(q).to(DEV), gkc, gks, gvc, gvs, torch.from_numpy(bt).to(DEV),
+                              torch.from_numpy(cl).to(DEV), msl, win)
+    ref = O.paged_attention_int4(q, np16(gkc), np16(gks), np16(gvc), np16(gvs), bt, cl, msl, win)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_attention_deterministic_and_workspace_reuse():
+    B, QL, H, D, BS, ctx, MB, msl, win, holes = ATTN_CASES[7]
+    q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, 11, holes)
+    args = [torch.from_numpy(a).to(DEV) for a in (q, kp, vp, bt, cl)]
+    ws, n = capi.workspace(B, QL, H, D, MB, BS, msl, win)
+    assert n > 0  # this case uses split-K
+    o1 = capi.attention_f16(*args, msl, win, ws=ws)
+    o2 = capi.attention_f16(*args, msl, win, ws=ws)
+    assert torch.equal(o1, o2)
+    tickets = capi.lib().memopt_paged_attention_ticket_bytes(B, QL, H)
+    assert int(ws[:tickets].count_nonzero().item()) == 0  # tickets left zero
