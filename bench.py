@@ -1,0 +1,426 @@
+"""Benchmark of the paged decode hot path (BASELINE config 2 at N=1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (per GPU, weak scaling): BASELINE.json configs[1] — paged fp16
+decode, batch 32, 32 heads x 128, 4096 cached tokens per sequence in 16-token
+pages with seeded random-permuted block tables, one query token per
+sequence, Q/K/V ~ N(0,1) fp16, retain_ratio 1.0, synthetic data.  A step is
+one dynamic_sparse_attention over the whole batch; the pool (2.1 GB of K/V)
+is larger than L2, so every step streams it from HBM.
+
+Metric: algorithmic HBM GB/s of the step (K+V pages + q/out + tables),
+with decode tokens/s beside it.  `e2e` is the same metric through the public
+API (memopt_C.write_cache of each new token + dynamic_sparse_attention) with
+pinned host buffers copied in and the output copied back inside the timed
+region.  `--impl reference` times the CPU restatement of the reference
+kernel (oracle/, OpenMP over all host cores) on a bounded sample of the same
+workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "memopt-transformer-runtime_b200"))
+
+B, H, D, BS, CTX = 32, 32, 128, 16, 4096
+MB = CTX // BS
+NB = B * MB  # 8192 pages
+INT4_B, INT4_CTX = 16, 16384
+METRIC = "paged decode attention HBM GB/s (% of peak) & decode tokens/s at 1/2/4/8 B200"
+
+
+def step_bytes(batch: int, ctx: int, fmt: str = "fp16") -> int:
+    """Algorithmic bytes of one decode step (each byte the step must move once)."""
+    if fmt == "fp16":
+        kv = 2 * batch * ctx * H * D * 2
+    else:
+        kv = 2 * batch * ctx * H * (D // 2) + 2 * batch * ctx * H * (D // 64) * 2
+    qo = 2 * batch * H * D * 2
+    tables = batch * (ctx // BS) * 4 + batch * 4
+    return kv + qo + tables
+
+
+def peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def make_fp16_workload(torch, seed: int, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    kp = torch.randn(NB, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    vp = torch.randn(NB, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    gc = torch.Generator().manual_seed(seed + 1)
+    bt = torch.randperm(NB, generator=gc)[: B * MB].reshape(B, MB).to(torch.int32).to(dev)
+    q = torch.randn(B, 1, H, D, device=dev, dtype=torch.float16, generator=g)
+    ctx = torch.full((B,), CTX, dtype=torch.int32, device=dev)
+    return kp, vp, bt, q, ctx
+
+
+def time_loop(torch, fn, steps: int, warmup: int, barrier, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / steps  # ms per step
+
+
+def cpu_sample(torch, kp, vp, bt, q, ctx, rows_budget_s: float, max_rows: int):
+    """Times the oracle (CPU restatement of the reference kernel) on whole
+    (sequence, head) rows; returns (GB/s, tokens/s-equivalent, rows, seconds)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    pages = bt[0].cpu().numpy()
+    kp0 = kp[torch.from_numpy(pages).long().to(kp.device)].cpu().numpy()
+    vp0 = vp[torch.from_numpy(pages).long().to(kp.device)].cpu().numpy()
+    bt0 = np.arange(MB, dtype=np.int32)[None, :]
+    q0 = q[0:1].cpu().numpy()
+    ctx0 = np.array([CTX], np.int32)
+    O.paged_attention_f16(q0[:, :, :1], kp0[:, :, :1].copy(), vp0[:, :, :1].copy(), bt0, ctx0, CTX, CTX)
+    t = time.perf_counter()
+    O.paged_attention_f16(q0, kp0, vp0, bt0, ctx0, CTX, CTX)  # one sequence, all heads
+    t_seq = time.perf_counter() - t
+    t_row = t_seq / H
+    rows = int(max(1, min(max_rows, rows_budget_s / max(t_row, 1e-9))))
+    nseq = max(1, rows // H)
+    reps = max(1, rows // (nseq * H)) if rows >= H else 0
+    if rows >= H:
+        t = time.perf_counter()
+        for _ in range(reps):
+            O.paged_attention_f16(np.repeat(q0, nseq, 0), kp0, vp0, np.repeat(bt0, nseq, 0),
+                                  np.repeat(ctx0, nseq), CTX, CTX)
+        el = time.perf_counter() - t
+        rows = reps * nseq * H
+    else:
+        t = time.perf_counter()
+        O.paged_attention_f16(q0[:, :, :rows], kp0[:, :, :rows].copy(), vp0[:, :, :rows].copy(), bt0, ctx0,
+                              CTX, CTX)
+        el = time.perf_counter() - t
+    row_bytes = step_bytes(B, CTX) / (B * H)
+    return rows * row_bytes / el / 1e9, rows / H / el, rows, el
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    import torch
+
+    dev = "cpu"
+    kp, vp, bt, q, ctx = make_fp16_workload(torch, 1234, dev)
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        gbs, toks, rows, el = cpu_sample(torch, kp, vp, bt, q, ctx, budget, B * H)
+        if i >= args.warmup:
+            vals.append((gbs, toks, rows, el))
+    gbs = statistics.median(v[0] for v in vals)
+    toks = statistics.median(v[1] for v in vals)
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(v[3] for v in vals) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "decode_tokens_per_s": round(toks, 3),
+        "config": config_dict(args.gpus),
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{vals[0][2]} (sequence, head) rows of the 4096-token workload per step, "
+                                   "oracle/memopt_oracle.c with OpenMP on all host cores"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(n: int) -> dict:
+    return {"workload": "BASELINE configs[1]: paged fp16 decode, batch 32/GPU, 32 heads x 128, ctx 4096, "
+                        "16-token pages, permuted block tables",
+            "batch_per_gpu": B, "global_batch": B * n, "seq_len": CTX, "heads": H, "head_dim": D,
+            "block_size": BS, "pages_per_gpu": NB,
+            "l2": "inputs larger than L2: 2.15 GB of K/V per GPU streamed every step",
+            "parallelism": f"dp{n} (sequences sharded, one pool per GPU, no data-path collective)"}
+
+
+def run_ours(args) -> None:
+    import torch
+
+    ws_n, rank, local = dist_env()
+    dist = None
+    if ws_n > 1:
+        import torch.distributed as dist  # noqa: F811
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    import memopt_C
+    from memopt import _capi
+
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    kp, vp, bt, q, ctx = make_fp16_workload(torch, 1234 + rank, dev)
+    out = torch.empty_like(q)
+    wsb = _capi.workspace_size(B, 1, H, D, MB, BS, CTX, CTX)
+    wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+    def step():
+        _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, CTX, CTX, wsp, wsb, sp)
+
+    # ---- device-resident decode (value) --------------------------------------
+    with Clocks(local) as clk:
+        ms = time_loop(torch, step, args.steps, args.warmup, barrier, stream)
+    ms = max_over_ranks(ms)
+    sbytes = step_bytes(B, CTX)
+    value = sbytes * ws_n / (ms * 1e-3) / 1e9
+    tokens = B * ws_n / (ms * 1e-3)
+    peak, peak_kind = peaks()
+    kernel_gbs = sbytes / (ms * 1e-3) / 1e9  # one kernel launch per step
+
+    # ---- end to end through the public API (host buffers) --------------------
+    hq = torch.randn(B, 1, H, D, dtype=torch.float16).pin_memory()
+    hk = torch.randn(B, H, D, dtype=torch.float16).pin_memory()
+    hv = torch.randn(B, H, D, dtype=torch.float16).pin_memory()
+    bt_cpu = bt.cpu()
+    hslots = (bt_cpu[:, MB - 1] * BS + (BS - 1)).to(torch.int32).pin_memory()  # token CTX-1 of each seq
+    hbt = bt_cpu.pin_memory()
+    hctx = ctx.cpu().pin_memory()
+    hout = torch.empty(B, 1, H, D, dtype=torch.float16).pin_memory()
+    memopt_C.init_pool(NB, BS, H, D)
+    pk, pv = memopt_C.get_pool_tensors()
+    pk.copy_(kp)
+    pv.copy_(vp)
+    del kp, vp
+    dq = torch.empty_like(hq, device=dev)
+    dk = torch.empty_like(hk, device=dev)
+    dv = torch.empty_like(hv, device=dev)
+    ds = torch.empty_like(hslots, device=dev)
+    dbt = torch.empty_like(hbt, device=dev)
+    dctx = torch.empty_like(hctx, device=dev)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ds.copy_(hslots, non_blocking=True)
+        dbt.copy_(hbt, non_blocking=True)
+        dctx.copy_(hctx, non_blocking=True)
+        memopt_C.write_cache(dk, dv, dbt, ds)
+        o = memopt_C.dynamic_sparse_attention(dq, pk, pv, dbt, dctx, CTX, CTX)
+        hout.copy_(o, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 500))
+    ms_e2e = max_over_ranks(time_loop(torch, e2e_step, e2e_steps, args.warmup, barrier, stream))
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hslots, hbt, hctx))
+    d2h = hout.numel() * hout.element_size()
+    e2e = sbytes * ws_n / (ms_e2e * 1e-3) / 1e9
+
+    # ---- INT4 decode as a secondary line ---------------
+    extra = {}
+    if not args.no_int4:
+        extra = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)
+
+    # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
+    cpu = None
+    if ws_n == 1 and not args.no_cpu:
+        kp2, vp2 = pk, pv
+        gbs, toks, rows, el = cpu_sample(torch, kp2, vp2, bt, q, ctx, 12.0, B * H)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{rows} (sequence, head) rows of the 4096-token workload in {el:.1f} s, "
+                         "oracle/memopt_oracle.c (fp64, OpenMP on all host cores)",
+               "decode_tokens_per_s": round(toks, 3)}
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("paged_decode_f16_cfg2_bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws_n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) K/V/q, permuted block tables)",
+        "decode_tokens_per_s": round(tokens, 1),
+        "pct_of_hbm_peak": round(100 * kernel_gbs / peak, 2),
+        "config": config_dict(ws_n),
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(kernel_gbs / peak, 4), "traffic": traffic,
+                     "kernel": "paged_decode_kernel<128,16,false>", "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": sbytes},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(ms_e2e, 5), "steps": e2e_steps,
+                "path": "memopt_C.write_cache + memopt_C.dynamic_sparse_attention, pinned host buffers"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "extra": extra,
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """INT4 pool written by the fused write_cache, then
+    decode with fused dequant.  Reported as secondary numbers."""
+    b, ctx_len = INT4_B, INT4_CTX
+    mb = ctx_len // BS
+    nb = b * mb
+    memopt_C.init_pool(nb, BS, H, D, kv_format="int4")
+    kc, ks, vc, vs = memopt_C.get_int4_pool_tensors()
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(7 + rank)).to(torch.int32)
+    bt = perm[: b * mb].reshape(b, mb).to(dev)
+    # Token t of sequence s goes to page bt[s, t // BS], slot t % BS.
+    chunk = 32768
+    T = b * ctx_len
+    slots_all = (bt.reshape(-1).repeat_interleave(BS) * BS +
+                 torch.arange(BS, device=dev, dtype=torch.int32).repeat(b * mb)).to(torch.int32)
+    kbuf = torch.empty(chunk, H, D, dtype=torch.float16, device=dev)
+    vbuf = torch.empty_like(kbuf)
+    write_ms = []
+    for c0 in range(0, T, chunk):
+        kbuf.normal_(generator=g)
+        vbuf.normal_(generator=g)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        memopt_C.write_cache(kbuf, vbuf, bt, slots_all[c0:c0 + chunk])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        write_ms.append(e0.elapsed_time(e1))
+    wms = statistics.median(write_ms[1:] if len(write_ms) > 1 else write_ms)
+    wbytes_chunk = 2 * chunk * H * D * 2 + 2 * chunk * H * (D // 2) + 2 * chunk * H * (D // 64) * 2 + chunk * 4
+    q = torch.randn(b, 1, H, D, dtype=torch.float16, device=dev, generator=g)
+    ctx = torch.full((b,), ctx_len, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    wsb = _capi.workspace_size(b, 1, H, D, mb, BS, ctx_len, ctx_len)
+    wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+    def step():
+        _capi.paged_attention_int4(q, kc, ks, vc, vs, bt, ctx, out, ctx_len, ctx_len, wsp, wsb, sp)
+
+    ms = max_over_ranks(time_loop(torch, step, max(args.steps, 20), args.warmup, barrier, stream))
+    sbytes = step_bytes(b, ctx_len, "int4")
+    peak, _ = peaks()
+    return {"int4_decode": {"workload": "BASELINE configs[2]: batch 16/GPU, ctx 16384, INT4 g64 pages",
+                            "value": round(sbytes * ws_n / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                            "ms_per_step": round(ms, 5),
+                            "frac_of_hbm_peak": round(sbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                            "decode_tokens_per_s": round(b * ws_n / (ms * 1e-3), 1),
+                            "algorithmic_bytes_per_launch": sbytes},
+            "int4_write_cache": {"value": round(wbytes_chunk / (wms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                 "frac_of_hbm_peak": round(wbytes_chunk / (wms * 1e-3) / 1e9 / peak, 4),
+                                 "tokens_per_launch": chunk, "ms_per_launch": round(wms, 5)}}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,56 @@
+"""ctypes binding of libmemopt_b200.so (the C-ABI in include/memopt_b200.h).
+
+This is the binding a host without PyTorch extensions would use; tensors are
+passed as raw device pointers.  bench.py times the kernels through it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "libmemopt_b200.so")
+P, I, I64, F, SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
+_lib = None
+
+
+class MemoptError(RuntimeError):
+    pass
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise MemoptError(f"{_LIB_PATH} is missing; run memopt-transformer-runtime_b200/build.py")
+        _lib = C.CDLL(_LIB_PATH)
+        _lib.memopt_last_error.restype = C.c_char_p
+        _lib.memopt_paged_attention_workspace_size.restype = SZ
+        _lib.memopt_paged_attention_ticket_bytes.restype = SZ
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise MemoptError(f"{what}: {lib().memopt_last_error().decode()} (status {status})")
+
+
+def paged_attention_f16(q, kpool, vpool, bt, ctx, out, msl, win, ws, ws_bytes, stream):
+    B, QL, H, D = q.shape
+    check(lib().memopt_paged_attention_f16(
+        P(q.data_ptr()), P(kpool.data_ptr()), P(vpool.data_ptr()), P(bt.data_ptr()), P(ctx.data_ptr()),
+        I(B), I(QL), I(H), I(D), I(bt.shape[1]), I64(kpool.shape[0]), I(kpool.shape[1]), I(msl), I(win),
+        P(out.data_ptr()), P(ws.data_ptr() if ws is not None else 0), SZ(ws_bytes), P(stream)),
+        "memopt_paged_attention_f16")
+
+
+def paged_attention_int4(q, kc, ks, vc, vs, bt, ctx, out, msl, win, ws, ws_bytes, stream):
+    B, QL, H, D = q.shape
+    check(lib().memopt_paged_attention_int4(
+        P(q.data_ptr()), P(kc.data_ptr()), P(ks.data_ptr()), P(vc.data_ptr()), P(vs.data_ptr()),
+        P(bt.data_ptr()), P(ctx.data_ptr()), I(B), I(QL), I(H), I(D), I(bt.shape[1]), I64(kc.shape[0]),
+        I(kc.shape[2]), I(msl), I(win), P(out.data_ptr()), P(ws.data_ptr() if ws is not None else 0),
+        SZ(ws_bytes), P(stream)), "memopt_paged_attention_int4")
+
+
+def workspace_size(B, QL, H, D, MB, BS, msl, win) -> int:
+    return int(lib().memopt_paged_attention_workspace_size(B, QL, H, D, MB, BS, msl, win))
