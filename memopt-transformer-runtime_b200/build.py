@@ -77,6 +77,11 @@ def build_ext(verbose: bool = False) -> str:
     src = os.path.join(CSRC, "memopt_C.cpp")
     if not _newer(EXT, [src, LIB, os.path.join(INCLUDE, "memopt_b200.h"), __file__]):
         return EXT
+    # The image's /opt/gcc wrapper (picked up by torch's default CXX) produces
+    # extensions that crash when a TORCH_CHECK message carries a number;
+    # the system compiler does not.
+    if os.path.exists("/usr/bin/g++"):
+        os.environ["CXX"] = "/usr/bin/g++"
     from torch.utils import cpp_extension
 
     bdir = os.path.join(PKG, "_build", "memopt_C")

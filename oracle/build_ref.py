@@ -32,6 +32,11 @@ def build(ref_root: str | None = None, verbose: bool = False) -> str | None:
     if os.path.exists(SO) and all(os.path.getmtime(SO) >= os.path.getmtime(s) for s in srcs):
         return SO
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    # The image's /opt/gcc wrapper (picked up by torch's default CXX) produces
+    # extensions that crash when a TORCH_CHECK message carries a number;
+    # the system compiler does not.
+    if os.path.exists("/usr/bin/g++"):
+        os.environ["CXX"] = "/usr/bin/g++"
     from torch.utils import cpp_extension
 
     bdir = os.path.join(OUT, "build")

@@ -25,6 +25,7 @@ def setup_pool(seq_len):
     nbps = math.ceil(seq_len / BS)
     memopt_C.init_pool(B * nbps + 2, BS, H, D)
     rows = [[memopt_C.allocate_block() for _ in range(nbps)] for _ in range(B)]
+    assert min(min(r) for r in rows) >= 0, "pool exhausted (idempotent init_pool kept a used free-list)"
     slots = [rows[b][t // BS] * BS + t % BS for b in range(B) for t in range(seq_len)]
     return (torch.tensor(slots, dtype=torch.int32, device="cuda"),
             torch.tensor(rows, dtype=torch.int32, device="cuda"))
@@ -123,8 +124,9 @@ def test_dynamic_attention_paged_path_runs(fmt):
     torch.manual_seed(0)
     S = 64
     mod = memopt.DynamicAttention(512, 8, strict=True).cuda()
-    memopt_C.init_pool(B * S // BS + 2, BS, 8, 64, kv_format=fmt)
+    memopt_C.init_pool(B * S // BS + 7, BS, 8, 64, kv_format=fmt)  # fresh geometry: fresh free-list
     rows = [[memopt_C.allocate_block() for _ in range(S // BS)] for _ in range(B)]
+    assert min(min(r) for r in rows) >= 0
     slots = torch.tensor([rows[b][t // BS] * BS + t % BS for b in range(B) for t in range(S)],
                          dtype=torch.int32, device="cuda")
     bt = torch.tensor(rows, dtype=torch.int32, device="cuda")
