@@ -23,6 +23,7 @@
 //     deterministic, and resets the ticket for the next call.
 #pragma once
 #include "common.cuh"
+#include "int4_mma.cuh"
 
 namespace memopt {
 namespace decode {
@@ -69,10 +70,6 @@ struct Cfg {
   static_assert(NW * NS * 8 <= BAR_BYTES, "barrier area too small");
 };
 
-// Float value (c - 8) of nibble j of w, via the 2^23 magic-number trick.
-__device__ __forceinline__ float nib(uint32_t w, int j) {
-  return __int_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)) - 8388616.0f;
-}
 
 template <int D, int BS, bool INT4>
 __global__ void __launch_bounds__(Cfg<D, BS, INT4>::NW * 32)
@@ -172,8 +169,14 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   for (int s = 0; s < NS; ++s) produce();
 
   // ---------------- consumer -------------------------------------------
-  const int r = lane / C::LPR;   // row within a warp instruction
-  const int cl = lane % C::LPR;  // 8-dim column chunk
+  const int r = lane / C::LPR;   // fp16: row within a warp instruction
+  const int cl = lane % C::LPR;  // fp16: 8-dim column chunk
+  const int mg = lane >> 2;      // int4 (mma fragments): group id
+  const int mt4 = lane & 3;      // int4 (mma fragments): thread in group
+  constexpr int G = D / 64;      // int4 scale groups per row
+  constexpr int NKM = D / 16;    // int4: k-steps of the score mma
+  constexpr int NT = D / 8;      // int4: n-tiles of the P.V mma
+  constexpr int MT = BS / 16;    // int4: 16-token m-tiles per page
   uint32_t c_seq = 0;
   bool failed = false;
 
@@ -184,7 +187,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     const int64_t pair = item / p.n_chunks;
 
     float q[8];
-    {
+    uint32_t qb[INT4 ? NKM : 1][2];
+    if constexpr (!INT4) {
       const uint4 qv = *reinterpret_cast<const uint4*>(p.q + pair * D + cl * 8);
       const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
 #pragma unroll
@@ -193,11 +197,28 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         q[2 * i] = f.x * p.qscale;
         q[2 * i + 1] = f.y * p.qscale;
       }
+    } else {
+      // B operand of the score mma: column g holds the q dims of group g.
+      const __half* qrow = p.q + pair * D;
+#pragma unroll
+      for (int m = 0; m < NKM; ++m) {
+        const int word = (D / 32) * mt4 + m / 2;
+        const int d0 = 8 * word + 2 * (m % 2);
+        const bool use = mg == word / 8;
+        const __half z = __ushort_as_half(0);
+        const __half2 lo = use ? __halves2half2(qrow[d0], qrow[d0 + 4]) : __halves2half2(z, z);
+        const __half2 hi = use ? __halves2half2(qrow[d0 + 1], qrow[d0 + 5]) : __halves2half2(z, z);
+        qb[m][0] = *reinterpret_cast<const uint32_t*>(&lo);
+        qb[m][1] = *reinterpret_cast<const uint32_t*>(&hi);
+      }
     }
     float m = -INFINITY, l = 0.f;
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    float acc[INT4 ? NT : 1][2];
+#pragma unroll
+    for (int j = 0; j < (INT4 ? NT : 1); ++j) acc[j][0] = acc[j][1] = 0.f;
 
     while (mask != 0) {
       const int jpage = __ffs(mask) - 1;
@@ -216,76 +237,64 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         break;
       }
       const uint8_t* stg = stages + s * C::STAGE;
-
-      // ---- scores: lane partials for TPL rows, then transpose-reduce ----
-      float val[C::TPL];
-#pragma unroll
-      for (int i = 0; i < C::TPL; ++i) {
-        const int t = i * C::RPI + r;
-        if (!INT4) {
-          const uint4 kv = *reinterpret_cast<const uint4*>(stg + t * D * 2 + cl * 16);
-          const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
-          float acc = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(k2[e]);
-            acc = fmaf(q[2 * e], f.x, acc);
-            acc = fmaf(q[2 * e + 1], f.y, acc);
-          }
-          val[i] = acc;
-        } else {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(stg + t * (D / 2) + cl * 4);
-          const float ks = __half2float(*reinterpret_cast<const __half*>(
-              stg + 2 * C::K_BYTES + (t * (D / 64) + cl / 8) * 2));
-          float acc = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(q[e], nib(w, e), acc);
-          val[i] = acc * ks;
-        }
-      }
-      int idx = 0;
-      {
-        int n = C::TPL;
-#pragma unroll
-        for (int mk = C::LPR / 2; mk >= 1; mk >>= 1) {
-          if (n > 1) {
-            const int half = n / 2;
-            const bool up = (lane & mk) != 0;
-#pragma unroll
-            for (int i = 0; i < (C::TPL + 1) / 2; ++i) {
-              if (i < half) {
-                const float send = up ? val[i] : val[i + half];
-                const float keepv = up ? val[i + half] : val[i];
-                val[i] = keepv + __shfl_xor_sync(0xffffffffu, send, mk);
-              }
-            }
-            if (up) idx += half;
-            n = half;
-          } else {
-            val[0] += __shfl_xor_sync(0xffffffffu, val[0], mk);
-          }
-        }
-      }
-      const int tok = page * BS + idx * C::RPI + r;
-      const float s2 = (tok >= win_start && tok < ctx) ? val[0] : -INFINITY;
-      float mp = s2;
-#pragma unroll
-      for (int mk = 16; mk >= 1; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
-      const float m_new = fmaxf(m, mp);
-      if (m_new != -INFINITY) {
-        const float alpha = exp2f(m - m_new);
-        const float pr = exp2f(s2 - m_new);
-        const bool dup = (lane & (C::DUP - 1)) != 0;
-        l = l * alpha + (dup ? 0.f : pr);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] *= alpha;
-        m = m_new;
-        // ---- P.V ----
+      if constexpr (!INT4) {
+        // ---- scores: lane partials for TPL rows, then transpose-reduce ----
+        float val[C::TPL];
 #pragma unroll
         for (int i = 0; i < C::TPL; ++i) {
           const int t = i * C::RPI + r;
-          float pi = __shfl_sync(0xffffffffu, pr, r * C::LPR + i * C::DUP);
-          if (!INT4) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(stg + t * D * 2 + cl * 16);
+          const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+          float a = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(k2[e]);
+            a = fmaf(q[2 * e], f.x, a);
+            a = fmaf(q[2 * e + 1], f.y, a);
+          }
+          val[i] = a;
+        }
+        int idx = 0;
+        {
+          int n = C::TPL;
+#pragma unroll
+          for (int mk = C::LPR / 2; mk >= 1; mk >>= 1) {
+            if (n > 1) {
+              const int half = n / 2;
+              const bool up = (lane & mk) != 0;
+#pragma unroll
+              for (int i = 0; i < (C::TPL + 1) / 2; ++i) {
+                if (i < half) {
+                  const float send = up ? val[i] : val[i + half];
+                  const float keepv = up ? val[i + half] : val[i];
+                  val[i] = keepv + __shfl_xor_sync(0xffffffffu, send, mk);
+                }
+              }
+              if (up) idx += half;
+              n = half;
+            } else {
+              val[0] += __shfl_xor_sync(0xffffffffu, val[0], mk);
+            }
+          }
+        }
+        const int tok = page * BS + idx * C::RPI + r;
+        const float s2 = (tok >= win_start && tok < ctx) ? val[0] : -INFINITY;
+        float mp = s2;
+#pragma unroll
+        for (int mk = 16; mk >= 1; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
+        const float m_new = fmaxf(m, mp);
+        if (m_new != -INFINITY) {
+          const float alpha = exp2f(m - m_new);
+          const float pr = exp2f(s2 - m_new);
+          const bool dup = (lane & (C::DUP - 1)) != 0;
+          l = l * alpha + (dup ? 0.f : pr);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] *= alpha;
+          m = m_new;
+#pragma unroll
+          for (int i = 0; i < C::TPL; ++i) {
+            const int t = i * C::RPI + r;
+            const float pi = __shfl_sync(0xffffffffu, pr, r * C::LPR + i * C::DUP);
             const uint4 vv = *reinterpret_cast<const uint4*>(stg + C::K_BYTES + t * D * 2 + cl * 16);
             const __half2* v2 = reinterpret_cast<const __half2*>(&vv);
 #pragma unroll
@@ -294,14 +303,117 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               o[2 * e] = fmaf(pi, f.x, o[2 * e]);
               o[2 * e + 1] = fmaf(pi, f.y, o[2 * e + 1]);
             }
-          } else {
-            const uint32_t w =
-                *reinterpret_cast<const uint32_t*>(stg + C::K_BYTES + t * (D / 2) + cl * 4);
-            const float vs = __half2float(*reinterpret_cast<const __half*>(
-                stg + 2 * C::K_BYTES + C::S_BYTES + (t * (D / 64) + cl / 8) * 2));
-            pi *= vs;
+          }
+        }
+      } else {
+        using namespace int4mma;
+        const __half* ksc = reinterpret_cast<const __half*>(stg + 2 * C::K_BYTES);
+        const __half* vsc = reinterpret_cast<const __half*>(stg + 2 * C::K_BYTES + C::S_BYTES);
+        float slo[MT], shi[MT];
+        // ---- scores on the tensor pipe, one m-tile (16 tokens) at a time ----
 #pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = fmaf(pi, nib(w, e), o[e]);
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint8_t* kr = stg + mt * 16 * (D / 2);
+          uint32_t w0[D / 32], w1[D / 32];
+          if constexpr (D == 128) {
+            const uint4 x0 = *reinterpret_cast<const uint4*>(kr + mg * (D / 2) + mt4 * 16);
+            const uint4 x1 = *reinterpret_cast<const uint4*>(kr + (mg + 8) * (D / 2) + mt4 * 16);
+            w0[0] = x0.x; w0[1] = x0.y; w0[2] = x0.z; w0[3] = x0.w;
+            w1[0] = x1.x; w1[1] = x1.y; w1[2] = x1.z; w1[3] = x1.w;
+          } else {
+            const uint2 x0 = *reinterpret_cast<const uint2*>(kr + mg * (D / 2) + mt4 * 8);
+            const uint2 x1 = *reinterpret_cast<const uint2*>(kr + (mg + 8) * (D / 2) + mt4 * 8);
+            w0[0] = x0.x; w0[1] = x0.y;
+            w1[0] = x1.x; w1[1] = x1.y;
+          }
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < D / 32; ++i) {
+            uint32_t a[4];
+            a[0] = nib_pair<0>(w0[i]); a[1] = nib_pair<0>(w1[i]);
+            a[2] = nib_pair<1>(w0[i]); a[3] = nib_pair<1>(w1[i]);
+            mma16816(c, a, qb[2 * i][0], qb[2 * i][1]);
+            a[0] = nib_pair<2>(w0[i]); a[1] = nib_pair<2>(w1[i]);
+            a[2] = nib_pair<3>(w0[i]); a[3] = nib_pair<3>(w1[i]);
+            mma16816(c, a, qb[2 * i + 1][0], qb[2 * i + 1][1]);
+          }
+          // Lanes with mt4 == 0 hold (group0, group1) partials of tokens mg, mg+8.
+          const int rl = mt * 16 + mg;
+          float a_lo = __half2float(ksc[rl * G]) * c[0];
+          float a_hi = __half2float(ksc[(rl + 8) * G]) * c[2];
+          if constexpr (G > 1) {
+            a_lo = fmaf(__half2float(ksc[rl * G + 1]), c[1], a_lo);
+            a_hi = fmaf(__half2float(ksc[(rl + 8) * G + 1]), c[3], a_hi);
+          }
+          a_lo = __shfl_sync(0xffffffffu, a_lo * p.qscale, lane & ~3);
+          a_hi = __shfl_sync(0xffffffffu, a_hi * p.qscale, lane & ~3);
+          const int tl = page * BS + rl;
+          slo[mt] = (tl >= win_start && tl < ctx) ? a_lo : -INFINITY;
+          shi[mt] = (tl + 8 >= win_start && tl + 8 < ctx) ? a_hi : -INFINITY;
+        }
+        float mp = -INFINITY;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mp = fmaxf(mp, fmaxf(slo[mt], shi[mt]));
+#pragma unroll
+        for (int mk = 16; mk >= 4; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
+        const float m_new = fmaxf(m, mp);
+        if (m_new != -INFINITY) {
+          const float alpha = exp2f(m - m_new);
+          m = m_new;
+          float psum = 0.f;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            slo[mt] = exp2f(slo[mt] - m_new);
+            shi[mt] = exp2f(shi[mt] - m_new);
+            psum += slo[mt] + shi[mt];
+          }
+          l = l * alpha + (mt4 == 0 ? psum : 0.f);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            acc[j][0] *= alpha;
+            acc[j][1] *= alpha;
+          }
+          // ---- P.V on the tensor pipe ----
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint8_t* vr = stg + C::K_BYTES + mt * 16 * (D / 2);
+            uint32_t wa[4], wb[4];
+            float pp[4];
+            const int gs = mg < G ? mg : G - 1;  // scale group of A row mg (rows >= G unused)
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl) {
+              const int row = (mt4 >> 1) + 2 * (4 * (mt4 & 1) + sl);  // conflict-free token order
+              if constexpr (D == 128) {
+                const uint32_t ua = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * (mg + 8 * (mt4 & 1)));
+                const uint32_t ub = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * (mg + 8 * (1 - (mt4 & 1))));
+                wa[sl] = (mt4 & 1) ? ub : ua;
+                wb[sl] = (mt4 & 1) ? ua : ub;
+              } else {
+                wa[sl] = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * mg);
+                wb[sl] = wa[sl];
+              }
+              const float plo = __shfl_sync(0xffffffffu, slo[mt], 4 * (row & 7));
+              const float phi = __shfl_sync(0xffffffffu, shi[mt], 4 * (row & 7));
+              pp[sl] = ((mt4 & 1) ? phi : plo) * __half2float(vsc[(mt * 16 + row) * G + gs]);
+            }
+            uint32_t a[4];
+            a[0] = pack_half2(pp[0], pp[1]);
+            a[1] = 0u;
+            a[2] = pack_half2(pp[2], pp[3]);
+            a[3] = 0u;
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+              const uint32_t* w = (j < 8) ? wa : wb;
+              const uint32_t sel = static_cast<uint32_t>((j % 8) / 2) | (static_cast<uint32_t>(4 + (j % 8) / 2) << 8);
+              const uint32_t x01 = __byte_perm(w[0], w[1], sel);
+              const uint32_t x23 = __byte_perm(w[2], w[3], sel);
+              const uint32_t b0 = (j % 2) ? nib_pair<1>(x01) : nib_pair<0>(x01);
+              const uint32_t b1 = (j % 2) ? nib_pair<1>(x23) : nib_pair<0>(x23);
+              float c[4] = {acc[j][0], acc[j][1], 0.f, 0.f};
+              mma16816(c, a, b0, b1);
+              acc[j][0] = c[0];
+              acc[j][1] = c[1];
+            }
           }
         }
       }
@@ -311,30 +423,58 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     }
     if (failed) break;
 
-    // ---- finish the item: reduce o over row groups, l over lanes ----------
-#pragma unroll
-    for (int mk = C::LPR; mk < 32; mk <<= 1) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] += __shfl_xor_sync(0xffffffffu, o[j], mk);
-    }
+    // ---- finish the item -------------------------------------------------
 #pragma unroll
     for (int mk = 16; mk >= 1; mk >>= 1) l += __shfl_xor_sync(0xffffffffu, l, mk);
+    // Each writing lane owns DPW contiguous output dims starting at dbase.
+    constexpr int DPW = INT4 ? 16 : 8;
+    float ov[DPW];
+    int dbase = 0;
+    bool writer = false;
+    if constexpr (!INT4) {
+#pragma unroll
+      for (int mk = C::LPR; mk < 32; mk <<= 1) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += __shfl_xor_sync(0xffffffffu, o[j], mk);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ov[j] = o[j];
+      dbase = cl * 8;
+      writer = r == 0;
+    } else {
+      // Lane (g < G, t) holds dims 64g + 16t + [0, 16): acc[8g + jj][c] is
+      // dim 64g + 8(2t + c) + jj.
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          float v = acc[jj][c];
+          if constexpr (G > 1) v = (mg == 1) ? acc[8 + jj][c] : v;
+          ov[c * 8 + jj] = v;
+        }
+      }
+      dbase = 64 * mg + 16 * mt4;
+      writer = mg < G;
+    }
 
     if (p.n_chunks == 1) {
-      if (r == 0) {
+      if (writer) {
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
-        uint4 ov;
-        __half2* o2 = reinterpret_cast<__half2*>(&ov);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o2[e] = __floats2half2_rn(o[2 * e] * inv, o[2 * e + 1] * inv);
-        *reinterpret_cast<uint4*>(p.out + pair * D + cl * 8) = ov;
+        for (int e = 0; e < DPW; e += 8) {
+          uint4 hv;
+          __half2* h2 = reinterpret_cast<__half2*>(&hv);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(ov[e + 2 * k] * inv, ov[e + 2 * k + 1] * inv);
+          *reinterpret_cast<uint4*>(p.out + pair * D + dbase + e) = hv;
+        }
       }
       continue;
     }
-    if (r == 0) {
-      float4* dst = reinterpret_cast<float4*>(p.po + item * D + cl * 8);
-      dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-      dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+    if (writer) {
+      float4* dst = reinterpret_cast<float4*>(p.po + item * D + dbase);
+#pragma unroll
+      for (int e = 0; e < DPW / 4; ++e) dst[e] = make_float4(ov[4 * e], ov[4 * e + 1], ov[4 * e + 2], ov[4 * e + 3]);
     }
     if (lane == 0) p.ml[item] = make_float2(m, l);
     __threadfence();
@@ -351,9 +491,9 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
     for (int mk = 16; mk >= 1; mk >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, mk));
     constexpr int DPL = D / 32;  // dims per lane in the merge
-    float acc[DPL];
+    float macc[DPL];
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+    for (int j = 0; j < DPL; ++j) macc[j] = 0.f;
     float L = 0.f;
     if (M != -INFINITY) {
       for (int c = 0; c < p.n_chunks; ++c) {
@@ -362,14 +502,14 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         L = fmaf(w, mlc.y, L);
         const float* src = p.po + (base + c) * D + lane * DPL;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) acc[j] = fmaf(w, __ldcg(src + j), acc[j]);
+        for (int j = 0; j < DPL; ++j) macc[j] = fmaf(w, __ldcg(src + j), macc[j]);
       }
     }
     const float inv = (L > 0.f) ? 1.f / L : 0.f;
 #pragma unroll
     for (int j = 0; j < DPL; j += 2) {
       *reinterpret_cast<__half2*>(p.out + pair * D + lane * DPL + j) =
-          __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
+          __floats2half2_rn(macc[j] * inv, macc[j + 1] * inv);
     }
     if (lane == 0) p.tickets[pair] = 0;
   }

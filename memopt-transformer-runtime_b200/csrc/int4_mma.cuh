@@ -1,0 +1,49 @@
+// int4_mma.cuh — INT4 page consumption on the tensor cores (mma.sync
+// m16n8k16, fp16 operands, fp32 accumulation) for the paged decode kernel.
+//
+// The decode of one query row is not a dense contraction, but doing its two
+// skinny products on the tensor pipe removes most of the per-element ALU work
+// that makes a CUDA-core INT4 loop issue-bound:
+//   * scores: S[tok] = sum_d (code-8)[tok][d] * q[d] for the 16 tokens of an
+//     m-tile.  A = codes (16 tokens x 16 dims per mma), B = q with column 0
+//     holding the dims of scale group 0 and column 1 those of group 1, so one
+//     mma yields both per-group partial dots; the fp32 per-(token, group)
+//     scales are applied after the mma.  Products are exact: (code-8) and q
+//     are fp16 values, (code-8) a small integer.
+//   * P.V: O[d] += sum_tok P'[tok] (code-8)[tok][d] with A row 0 = p*scale of
+//     group 0 and row 1 = p*scale of group 1 (fp16), B = V codes.
+// Nibbles become fp16 with the 0x6400 exponent trick: the half with bits
+// 0x6400 | n is 1024 + n exactly; subtracting 1032 gives n - 8 exactly.
+// Reduction dims (k) may be permuted freely as long as both operands use
+// the same permutation; the permutations below make every shared-memory
+// access conflict-free.
+#pragma once
+#include "common.cuh"
+
+namespace memopt {
+namespace int4mma {
+
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Half2 (n_lo - 8, n_hi - 8) from the nibbles at bits [4k, 4k+4) and
+// [16+4k, 16+4k+4) of x.
+template <int K>
+__device__ __forceinline__ uint32_t nib_pair(uint32_t x) {
+  uint32_t h = ((x >> (4 * K)) & 0x000F000Fu) | 0x64006400u;
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6408)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+}  // namespace int4mma
+}  // namespace memopt
