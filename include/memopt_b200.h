@@ -179,6 +179,26 @@ int memopt_paged_attention_f16(const void* query, const void* key_pool,
                                void* out, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/* No counterpart in the reference.  Same as memopt_paged_attention_f16, but
+ * for callers that cannot allocate device memory at call time (hosts with
+ * their own allocator-free runtime, or steps where allocator calls are not
+ * allowed): the split-K scratch is a fixed 8 MiB array inside this library's
+ * device image (held on every GPU that loads the library until exit), so the
+ * call allocates nothing.  Calls needing more scratch than
+ * memopt_paged_attention_noalloc_max_bytes() return MEMOPT_ERR_WORKSPACE.
+ * The first call on a device looks up the array's address (make it before
+ * any stream capture).  All calls share the array: calls that overlap on the
+ * GPU race.  The ticket region is cleared at the start of every call. */
+size_t memopt_paged_attention_noalloc_max_bytes(void);
+int memopt_paged_attention_f16_noalloc(const void* query, const void* key_pool,
+                                       const void* value_pool,
+                                       const int32_t* block_tables,
+                                       const int32_t* context_lens,
+                                       int batch, int q_len, int num_heads, int head_dim,
+                                       int max_blocks_per_seq, int64_t num_blocks,
+                                       int block_size, int max_seq_len, int window_size,
+                                       void* out, void* stream);
+
 /* INT4 pool written by memopt_write_cache_int4; K/V element value is
  * (code - 8) * float(scale_fp16), dequantised inside the kernel. */
 int memopt_paged_attention_int4(const void* query,
