@@ -405,6 +405,30 @@ def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_
                                  "tokens_per_launch": chunk, "ms_per_launch": round(wms, 5)}}
 
 
+def run_only(args) -> None:
+    """One kernel family in isolation (for ncu captures and quick timing)."""
+    import torch
+
+    import memopt_C
+    from memopt import _capi
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    if args.only == "fp16":
+        kp, vp, bt, q, ctx = make_fp16_workload(torch, 1234, dev)
+        out = torch.empty_like(q)
+        wsb = _capi.workspace_size(B, 1, H, D, MB, BS, CTX, CTX)
+        wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+        ms = time_loop(torch, lambda: _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, CTX, CTX, wsp, wsb, sp),
+                       args.steps, args.warmup, lambda: None, stream)
+        res = {"kernel": "paged_decode f16 cfg2", "ms": ms, "GB/s": step_bytes(B, CTX) / ms / 1e6}
+    else:
+        res = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
+    print(json.dumps(res), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -413,10 +437,13 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
+    ap.add_argument("--only", choices=["fp16", "int4"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -110,7 +110,9 @@ int launch(const Params& p, const CUtensorMap& km, const CUtensorMap& vm, int32_
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int64_t ctas_needed = (p.total_items + C::NW - 1) / C::NW;
-  const int per_sm = (227 * 1024) / C::SMEM >= 2 ? 2 : 1;
+  int per_sm = (227 * 1024) / C::SMEM;
+  if (per_sm > C::MIN_BLOCKS) per_sm = C::MIN_BLOCKS;
+  if (per_sm < 1) per_sm = 1;
   const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
   const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
   kern<<<grid, C::NW * 32, C::SMEM, s>>>(p, km, vm, err);

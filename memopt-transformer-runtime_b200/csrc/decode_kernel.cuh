@@ -61,9 +61,14 @@ struct Cfg {
   static constexpr int S_BYTES = INT4 ? BS * (D / 64) * 2 : 0;
   static constexpr int STAGE_RAW = 2 * K_BYTES + 2 * S_BYTES;
   static constexpr int STAGE = (STAGE_RAW + 127) / 128 * 128;
-  static constexpr int NS_RAW = 24576 / STAGE;
+  // fp16 pages are large: 3 stages of 8 KB per warp, 2 CTAs (8 warps) per SM.
+  // INT4 pages are small and their consumer is issue-latency bound: ~12 KB of
+  // stages per warp and 4 CTAs (16 warps) per SM at <= 128 registers.
+  static constexpr int WARP_BUDGET = INT4 ? 12288 : 24576;
+  static constexpr int NS_RAW = WARP_BUDGET / STAGE;
   static constexpr int NS = NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW);
   static constexpr int NW = 4;            // warps per CTA
+  static constexpr int MIN_BLOCKS = INT4 ? 4 : 2;
   static constexpr int BAR_BYTES = 1024;  // mbarriers
   static constexpr int SMEM = BAR_BYTES + NW * NS * STAGE;
   static_assert(TPL >= 1 && DUP >= 1, "unsupported geometry");
@@ -72,7 +77,7 @@ struct Cfg {
 
 
 template <int D, int BS, bool INT4>
-__global__ void __launch_bounds__(Cfg<D, BS, INT4>::NW * 32)
+__global__ void __launch_bounds__(Cfg<D, BS, INT4>::NW * 32, Cfg<D, BS, INT4>::MIN_BLOCKS)
 paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap, int32_t* __restrict__ err) {
   using C = Cfg<D, BS, INT4>;
@@ -327,16 +332,21 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             w1[0] = x1.x; w1[1] = x1.y;
           }
           float c[4] = {0.f, 0.f, 0.f, 0.f};
+          float c2[4] = {0.f, 0.f, 0.f, 0.f};  // second chain: halves the mma dependency depth
 #pragma unroll
           for (int i = 0; i < D / 32; ++i) {
+            // Pair k of a word is (elem k, elem k+4); pairs 2,3 come from w >> 8.
             uint32_t a[4];
-            a[0] = nib_pair<0>(w0[i]); a[1] = nib_pair<0>(w1[i]);
-            a[2] = nib_pair<1>(w0[i]); a[3] = nib_pair<1>(w1[i]);
+            a[0] = lo_pair(w0[i]); a[1] = lo_pair(w1[i]);
+            a[2] = hi_pair(w0[i]); a[3] = hi_pair(w1[i]);
             mma16816(c, a, qb[2 * i][0], qb[2 * i][1]);
-            a[0] = nib_pair<2>(w0[i]); a[1] = nib_pair<2>(w1[i]);
-            a[2] = nib_pair<3>(w0[i]); a[3] = nib_pair<3>(w1[i]);
-            mma16816(c, a, qb[2 * i + 1][0], qb[2 * i + 1][1]);
+            const uint32_t u0 = w0[i] >> 8, u1 = w1[i] >> 8;
+            a[0] = lo_pair(u0); a[1] = lo_pair(u1);
+            a[2] = hi_pair(u0); a[3] = hi_pair(u1);
+            mma16816(c2, a, qb[2 * i + 1][0], qb[2 * i + 1][1]);
           }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c[e] += c2[e];
           // Lanes with mt4 == 0 hold (group0, group1) partials of tokens mg, mg+8.
           const int rl = mt * 16 + mg;
           float a_lo = __half2float(ksc[rl * G]) * c[0];
@@ -368,10 +378,12 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             psum += slo[mt] + shi[mt];
           }
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
+          if (alpha != 1.f) {  // warp-uniform; skipped once the running max settles
 #pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            acc[j][0] *= alpha;
-            acc[j][1] *= alpha;
+            for (int j = 0; j < NT; ++j) {
+              acc[j][0] *= alpha;
+              acc[j][1] *= alpha;
+            }
           }
           // ---- P.V on the tensor pipe ----
 #pragma unroll
@@ -401,18 +413,22 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a[1] = 0u;
             a[2] = pack_half2(pp[2], pp[3]);
             a[3] = 0u;
+            // n-tiles 2jb and 2jb+1 read the low and high nibble of byte jb%4
+            // of word (mg + 8 * (jb / 4)) from the four token rows.
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-              const uint32_t* w = (j < 8) ? wa : wb;
-              const uint32_t sel = static_cast<uint32_t>((j % 8) / 2) | (static_cast<uint32_t>(4 + (j % 8) / 2) << 8);
+            for (int jb = 0; jb < NT / 2; ++jb) {
+              const uint32_t* w = (jb < 4) ? wa : wb;
+              const uint32_t sel = static_cast<uint32_t>(jb % 4) | (static_cast<uint32_t>(4 + jb % 4) << 8);
               const uint32_t x01 = __byte_perm(w[0], w[1], sel);
               const uint32_t x23 = __byte_perm(w[2], w[3], sel);
-              const uint32_t b0 = (j % 2) ? nib_pair<1>(x01) : nib_pair<0>(x01);
-              const uint32_t b1 = (j % 2) ? nib_pair<1>(x23) : nib_pair<0>(x23);
-              float c[4] = {acc[j][0], acc[j][1], 0.f, 0.f};
-              mma16816(c, a, b0, b1);
-              acc[j][0] = c[0];
-              acc[j][1] = c[1];
+              float c0[4] = {acc[2 * jb][0], acc[2 * jb][1], 0.f, 0.f};
+              mma16816(c0, a, lo_pair(x01), lo_pair(x23));
+              float c1[4] = {acc[2 * jb + 1][0], acc[2 * jb + 1][1], 0.f, 0.f};
+              mma16816(c1, a, hi_pair(x01), hi_pair(x23));
+              acc[2 * jb][0] = c0[0];
+              acc[2 * jb][1] = c0[1];
+              acc[2 * jb + 1][0] = c1[0];
+              acc[2 * jb + 1][1] = c1[1];
             }
           }
         }

@@ -31,12 +31,20 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Half2 (n_lo - 8, n_hi - 8) from the nibbles at bits [4k, 4k+4) and
-// [16+4k, 16+4k+4) of x.
-template <int K>
-__device__ __forceinline__ uint32_t nib_pair(uint32_t x) {
-  uint32_t h = ((x >> (4 * K)) & 0x000F000Fu) | 0x64006400u;
+// Half2 (n_a - 8, n_b - 8) of the nibbles at bits [0,4) and [16,20) of x.
+__device__ __forceinline__ uint32_t lo_pair(uint32_t x) {
+  uint32_t h = (x & 0x000F000Fu) | 0x64006400u;  // 1024 + n, exactly
   const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6408)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// Half2 (n_a - 8, n_b - 8) of the nibbles at bits [4,8) and [20,24) of x:
+// the half 0x6400 | n << 4 is 1024 + 16 n, and (1024 + 16 n) / 16 - 72 = n - 8
+// with a single exact fma.
+__device__ __forceinline__ uint32_t hi_pair(uint32_t x) {
+  uint32_t h = (x & 0x00F000F0u) | 0x64006400u;
+  const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x2C00)),
+                            __half2half2(__ushort_as_half(0xD480)));
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 
