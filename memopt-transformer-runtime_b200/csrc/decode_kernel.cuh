@@ -66,7 +66,10 @@ struct Cfg {
   // stages per warp and 4 CTAs (16 warps) per SM at <= 128 registers.
   static constexpr int WARP_BUDGET = INT4 ? 12288 : 24576;
   static constexpr int NS_RAW = WARP_BUDGET / STAGE;
-  static constexpr int NS = NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW);
+  // INT4: largest power of two that fits (the ring index is then a mask;
+  // per-page integer overhead matters at 2 KB pages).  fp16: as many as fit.
+  static constexpr int NS_P2 = NS_RAW >= 16 ? 16 : NS_RAW >= 8 ? 8 : NS_RAW >= 4 ? 4 : 2;
+  static constexpr int NS = INT4 ? NS_P2 : (NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW));
   static constexpr int NW = 4;            // warps per CTA
   static constexpr int MIN_BLOCKS = INT4 ? 4 : 2;
   static constexpr int BAR_BYTES = 1024;  // mbarriers
@@ -421,14 +424,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               const uint32_t sel = static_cast<uint32_t>(jb % 4) | (static_cast<uint32_t>(4 + jb % 4) << 8);
               const uint32_t x01 = __byte_perm(w[0], w[1], sel);
               const uint32_t x23 = __byte_perm(w[2], w[3], sel);
-              float c0[4] = {acc[2 * jb][0], acc[2 * jb][1], 0.f, 0.f};
-              mma16816(c0, a, lo_pair(x01), lo_pair(x23));
-              float c1[4] = {acc[2 * jb + 1][0], acc[2 * jb + 1][1], 0.f, 0.f};
-              mma16816(c1, a, hi_pair(x01), hi_pair(x23));
-              acc[2 * jb][0] = c0[0];
-              acc[2 * jb][1] = c0[1];
-              acc[2 * jb + 1][0] = c1[0];
-              acc[2 * jb + 1][1] = c1[1];
+              mma16816_top(acc[2 * jb][0], acc[2 * jb][1], a, lo_pair(x01), lo_pair(x23));
+              mma16816_top(acc[2 * jb + 1][0], acc[2 * jb + 1][1], a, hi_pair(x01), hi_pair(x23));
             }
           }
         }

@@ -31,6 +31,18 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Same product when rows 8..15 of A are zero: only rows 0..7 of D are kept
+// (d0, d1 accumulate in place), rows 8..15 go to scratch outputs and their
+// accumulator inputs are a shared zero, so no register moves are needed.
+__device__ __forceinline__ void mma16816_top(float& d0, float& d1, const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  float x2, x3;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%10,%10};"
+      : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // Half2 (n_a - 8, n_b - 8) of the nibbles at bits [0,4) and [16,20) of x.
 __device__ __forceinline__ uint32_t lo_pair(uint32_t x) {
   uint32_t h = (x & 0x000F000Fu) | 0x64006400u;  // 1024 + n, exactly
