@@ -359,7 +359,7 @@ def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_
     mb = ctx_len // BS
     nb = b * mb
     memopt_C.init_pool(nb, BS, H, D, kv_format="int4")
-    kc, ks, vc, vs = memopt_C.get_int4_pool_tensors()
+    pages = memopt_C.get_int4_pages()
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     perm = torch.randperm(nb, generator=torch.Generator().manual_seed(7 + rank)).to(torch.int32)
     bt = perm[: b * mb].reshape(b, mb).to(dev)
@@ -389,7 +389,7 @@ def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_
     wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
 
     def step():
-        _capi.paged_attention_int4(q, kc, ks, vc, vs, bt, ctx, out, ctx_len, ctx_len, wsp, wsb, sp)
+        _capi.paged_attention_int4(q, pages, BS, bt, ctx, out, ctx_len, ctx_len, wsp, wsb, sp)
 
     ms = max_over_ranks(time_loop(torch, step, max(args.steps, 20), args.warmup, barrier, stream))
     sbytes = step_bytes(b, ctx_len, "int4")

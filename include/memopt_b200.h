@@ -94,16 +94,20 @@ int memopt_write_cache_f16(const void* keys, const void* values,
 
 /* INT4 pool with on-the-fly quantisation (new page format, no reference
  * counterpart for the fused op; the codes follow quantization.cu:129-202).
- * codes  : uint8 [num_blocks, num_heads, block_size, head_dim/2]
- * scales : fp16  [num_blocks, num_heads, block_size, head_dim/64]
- * Groups are 64 consecutive head_dim elements of one (token, head); the code
- * is computed from the fp32 scale absmax/7 (1.0 for an all-zero group) and
- * the stored scale is that fp32 scale rounded to fp16. head_dim % 64 == 0. */
+ * kv_pages: uint8 [num_blocks, num_heads, page_bytes], one contiguous page per
+ * (block, head) laid out as
+ *   K codes  [block_size][head_dim/2]   (byte i of a row = q[2i] | q[2i+1] << 4)
+ *   V codes  [block_size][head_dim/2]
+ *   K scales [block_size][head_dim/64]  fp16
+ *   V scales [block_size][head_dim/64]  fp16
+ * page_bytes = memopt_int4_page_bytes(block_size, head_dim).  Groups are 64
+ * consecutive head_dim elements of one (token, head); the code is computed
+ * from the fp32 scale absmax/7 (1.0 for an all-zero group) and the stored
+ * scale is that fp32 scale rounded to fp16.  head_dim % 64 == 0. */
+size_t memopt_int4_page_bytes(int block_size, int head_dim);
 int memopt_write_cache_int4(const void* keys, const void* values,
                             const int32_t* slot_mapping, int64_t num_tokens,
-                            int num_heads, int head_dim,
-                            uint8_t* key_codes, void* key_scales,
-                            uint8_t* value_codes, void* value_scales,
+                            int num_heads, int head_dim, uint8_t* kv_pages,
                             int64_t num_blocks, int block_size,
                             int32_t* bad_slot_count, void* stream);
 
@@ -199,11 +203,10 @@ int memopt_paged_attention_f16_noalloc(const void* query, const void* key_pool,
                                        int block_size, int max_seq_len, int window_size,
                                        void* out, void* stream);
 
-/* INT4 pool written by memopt_write_cache_int4; K/V element value is
- * (code - 8) * float(scale_fp16), dequantised inside the kernel. */
-int memopt_paged_attention_int4(const void* query,
-                                const uint8_t* key_codes, const void* key_scales,
-                                const uint8_t* value_codes, const void* value_scales,
+/* INT4 pool written by memopt_write_cache_int4 (kv_pages as described
+ * there); K/V element value is (code - 8) * float(scale_fp16), dequantised
+ * inside the kernel. */
+int memopt_paged_attention_int4(const void* query, const uint8_t* kv_pages,
                                 const int32_t* block_tables,
                                 const int32_t* context_lens,
                                 int batch, int q_len, int num_heads, int head_dim,

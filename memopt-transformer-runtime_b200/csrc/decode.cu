@@ -232,13 +232,11 @@ extern "C" int memopt_paged_attention_f16(const void* query, const void* key_poo
   return dispatch<false>(p, head_dim, block_size, km, vm, nullptr, as_stream(stream));
 }
 
-extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* key_codes,
-                                           const void* key_scales, const uint8_t* value_codes,
-                                           const void* value_scales, const int32_t* block_tables,
-                                           const int32_t* context_lens, int batch, int q_len,
-                                           int num_heads, int head_dim, int max_blocks_per_seq,
-                                           int64_t num_blocks, int block_size, int max_seq_len,
-                                           int window_size, void* out, void* workspace,
+extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* kv_pages,
+                                           const int32_t* block_tables, const int32_t* context_lens,
+                                           int batch, int q_len, int num_heads, int head_dim,
+                                           int max_blocks_per_seq, int64_t num_blocks, int block_size,
+                                           int max_seq_len, int window_size, void* out, void* workspace,
                                            size_t workspace_bytes, void* stream) {
   Params p{};
   int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, head_dim,
@@ -248,13 +246,9 @@ extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* key
   if (p.total_items == 0) return MEMOPT_OK;
   if (num_blocks == 0 || max_blocks_per_seq == 0)
     return zero_output(out, batch, q_len, num_heads, head_dim, stream);
-  if ((reinterpret_cast<uintptr_t>(key_codes) | reinterpret_cast<uintptr_t>(value_codes) |
-       reinterpret_cast<uintptr_t>(key_scales) | reinterpret_cast<uintptr_t>(value_scales)) & 15u)
-    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: pools must be 16-byte aligned");
-  p.kcodes = key_codes;
-  p.vcodes = value_codes;
-  p.kscales = reinterpret_cast<const __half*>(key_scales);
-  p.vscales = reinterpret_cast<const __half*>(value_scales);
+  if (reinterpret_cast<uintptr_t>(kv_pages) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: pages must be 16-byte aligned");
+  p.pages = kv_pages;
   alignas(64) CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   return dispatch<true>(p, head_dim, block_size, dummy, dummy, nullptr, as_stream(stream));

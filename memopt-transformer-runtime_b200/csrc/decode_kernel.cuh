@@ -33,11 +33,8 @@ struct Params {
   __half* out;       // [B, QL, H, D]
   const int32_t* bt;   // [B, MB]
   const int32_t* ctx;  // [B]
-  // INT4 pool (head-major pages)
-  const uint8_t* kcodes;
-  const __half* kscales;
-  const uint8_t* vcodes;
-  const __half* vscales;
+  // INT4 pool: one page of STAGE_RAW bytes per (block, head)
+  const uint8_t* pages;
   // split-K workspace
   int32_t* tickets;  // [pairs]
   float2* ml;        // [pairs * n_chunks]
@@ -138,12 +135,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       tma_load_3d(dst + C::K_BYTES, &vmap, 0, h, phys * BS, bar);
     } else {
       const int64_t row = static_cast<int64_t>(phys) * p.H + h;
-      bulk_g2s(dst, p.kcodes + row * C::K_BYTES, C::K_BYTES, bar);
-      bulk_g2s(dst + C::K_BYTES, p.vcodes + row * C::K_BYTES, C::K_BYTES, bar);
-      bulk_g2s(dst + 2 * C::K_BYTES, reinterpret_cast<const uint8_t*>(p.kscales) + row * C::S_BYTES,
-               C::S_BYTES, bar);
-      bulk_g2s(dst + 2 * C::K_BYTES + C::S_BYTES,
-               reinterpret_cast<const uint8_t*>(p.vscales) + row * C::S_BYTES, C::S_BYTES, bar);
+      bulk_g2s(dst, p.pages + row * C::STAGE_RAW, C::STAGE_RAW, bar);
     }
   };
 
@@ -393,28 +385,33 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           for (int mt = 0; mt < MT; ++mt) {
             const uint8_t* vr = stg + C::K_BYTES + mt * 16 * (D / 2);
             uint32_t wa[4], wb[4];
-            float pp[4];
             const int gs = mg < G ? mg : G - 1;  // scale group of A row mg (rows >= G unused)
-#pragma unroll
-            for (int sl = 0; sl < 4; ++sl) {
-              const int row = (mt4 >> 1) + 2 * (4 * (mt4 & 1) + sl);  // conflict-free token order
-              if constexpr (D == 128) {
-                const uint32_t ua = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * (mg + 8 * (mt4 & 1)));
-                const uint32_t ub = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * (mg + 8 * (1 - (mt4 & 1))));
-                wa[sl] = (mt4 & 1) ? ub : ua;
-                wb[sl] = (mt4 & 1) ? ua : ub;
-              } else {
-                wa[sl] = *reinterpret_cast<const uint32_t*>(vr + row * (D / 2) + 4 * mg);
-                wb[sl] = wa[sl];
-              }
-              const float plo = __shfl_sync(0xffffffffu, slo[mt], 4 * (row & 7));
-              const float phi = __shfl_sync(0xffffffffu, shi[mt], 4 * (row & 7));
-              pp[sl] = ((mt4 & 1) ? phi : plo) * __half2float(vsc[(mt * 16 + row) * G + gs]);
-            }
+            // p of tokens 0..7 travel in the low half, 8..15 in the high half.
+            const uint32_t pk = pack_half2(slo[mt], shi[mt]);
+            const uint32_t psel = (mt4 & 1) ? 0x7632u : 0x5410u;
             uint32_t a[4];
-            a[0] = pack_half2(pp[0], pp[1]);
+#pragma unroll
+            for (int sp = 0; sp < 2; ++sp) {
+              // Token slots 2sp, 2sp+1 of this lane (conflict-free token order).
+              const int r0 = (mt4 >> 1) + 2 * (4 * (mt4 & 1) + 2 * sp);
+              const int r1 = r0 + 2;
+              wa[2 * sp] = *reinterpret_cast<const uint32_t*>(vr + r0 * (D / 2) + 4 * mg);
+              wa[2 * sp + 1] = *reinterpret_cast<const uint32_t*>(vr + r1 * (D / 2) + 4 * mg);
+              if constexpr (D == 128) {
+                wb[2 * sp] = *reinterpret_cast<const uint32_t*>(vr + r0 * (D / 2) + 4 * (mg + 8));
+                wb[2 * sp + 1] = *reinterpret_cast<const uint32_t*>(vr + r1 * (D / 2) + 4 * (mg + 8));
+              }
+              const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * (r0 & 7));
+              const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * (r1 & 7));
+              const uint32_t p01 = __byte_perm(u0, u1, psel);
+              const uint32_t s0 = __half_as_ushort(vsc[(mt * 16 + r0) * G + gs]);
+              const uint32_t s1 = __half_as_ushort(vsc[(mt * 16 + r1) * G + gs]);
+              const uint32_t v01 = s0 | (s1 << 16);
+              const __half2 pv = __hmul2(*reinterpret_cast<const __half2*>(&p01),
+                                         *reinterpret_cast<const __half2*>(&v01));
+              a[2 * sp] = *reinterpret_cast<const uint32_t*>(&pv);
+            }
             a[1] = 0u;
-            a[2] = pack_half2(pp[2], pp[3]);
             a[3] = 0u;
             // n-tiles 2jb and 2jb+1 read the low and high nibble of byte jb%4
             // of word (mg + 8 * (jb / 4)) from the four token rows.

@@ -6,7 +6,8 @@
 //   * get_key_pool / get_value_pool, which the reference's DynamicAttention
 //     calls (src/memopt/attention.py:330-331) but the reference never exported;
 //   * an INT4 page pool (init_pool(..., kv_format="int4")) fed by write_cache
-//     with on-the-fly quantisation, read by dynamic_sparse_attention_int4;
+//     with on-the-fly quantisation, read by dynamic_sparse_attention_int4
+//     (one [K codes | V codes | K scales | V scales] page per (block, head));
 //   * optional compaction outputs of evict_tokens.
 // The pool tensors are allocated here (caching allocator, zero filled as in
 // kv_cache.cu:135-141); the free-list lives in the C library.
@@ -27,7 +28,7 @@ struct Pool {
   std::mutex mu;
   bool int4 = false;
   torch::Tensor k, v;            // fp16 [NB, BS, H, D]
-  torch::Tensor kc, ks, vc, vs;  // int4 codes [NB, H, BS, D/2], scales fp16 [NB, H, BS, D/64]
+  torch::Tensor kvp;             // int4 pages uint8 [NB, H, page_bytes]
   int nb = 0, bs = 0, h = 0, d = 0;
   bool live = false;
 };
@@ -70,7 +71,7 @@ void init_pool(int num_blocks, int block_size, int num_heads, int head_dim, cons
     return;  // idempotent (kv_cache.cu:116-122)
   // Any other call resets first, so a rejected geometry leaves no pool behind.
   p.live = false;
-  p.k = p.v = p.kc = p.ks = p.vc = p.vs = torch::Tensor();
+  p.k = p.v = p.kvp = torch::Tensor();
   memopt_pool_reset();
   check(memopt_pool_init(num_blocks, block_size, num_heads, head_dim), "init_pool");
   if (int4 && head_dim % 64 != 0) {
@@ -84,11 +85,8 @@ void init_pool(int num_blocks, int block_size, int num_heads, int head_dim, cons
     p.v = torch::zeros({num_blocks, block_size, num_heads, head_dim}, o);
   } else {
     auto ou = torch::TensorOptions().dtype(torch::kUInt8).device(dev);
-    auto oh = torch::TensorOptions().dtype(torch::kFloat16).device(dev);
-    p.kc = torch::zeros({num_blocks, num_heads, block_size, head_dim / 2}, ou);
-    p.vc = torch::zeros({num_blocks, num_heads, block_size, head_dim / 2}, ou);
-    p.ks = torch::zeros({num_blocks, num_heads, block_size, head_dim / 64}, oh);
-    p.vs = torch::zeros({num_blocks, num_heads, block_size, head_dim / 64}, oh);
+    const int64_t pb = static_cast<int64_t>(memopt_int4_page_bytes(block_size, head_dim));
+    p.kvp = torch::zeros({num_blocks, num_heads, pb}, ou);
   }
   p.nb = num_blocks;
   p.bs = block_size;
@@ -108,10 +106,27 @@ void free_block(int block_idx) { check(memopt_pool_free_block(block_idx), "free_
 
 int free_blocks_count() { return memopt_pool_free_blocks_count(); }
 
+namespace {
+// Strided views of the four regions of every INT4 page (see memopt_b200.h).
+std::vector<torch::Tensor> int4_views(const torch::Tensor& kvp, int bs, int d) {
+  const int64_t nb = kvp.size(0), h = kvp.size(1), pb = kvp.size(2), g = d / 64;
+  const int64_t codes = static_cast<int64_t>(bs) * (d / 2);
+  auto kc = kvp.as_strided({nb, h, bs, d / 2}, {h * pb, pb, d / 2, 1}, kvp.storage_offset());
+  auto vc = kvp.as_strided({nb, h, bs, d / 2}, {h * pb, pb, d / 2, 1}, kvp.storage_offset() + codes);
+  auto k16 = kvp.view(torch::kFloat16);  // [nb, h, pb / 2]
+  auto ks = k16.as_strided({nb, h, bs, g}, {h * pb / 2, pb / 2, g, 1}, k16.storage_offset() + codes);
+  auto vs = k16.as_strided({nb, h, bs, g}, {h * pb / 2, pb / 2, g, 1}, k16.storage_offset() + codes + bs * g);
+  return {kc, ks, vc, vs};
+}
+}  // namespace
+
 std::pair<torch::Tensor, torch::Tensor> get_pool_tensors() {
   require_pool("get_pool_tensors");
   auto& p = P();
-  if (p.int4) return {p.kc, p.vc};
+  if (p.int4) {
+    auto v = int4_views(p.kvp, p.bs, p.d);
+    return {v[0], v[2]};
+  }
   return {p.k, p.v};
 }
 torch::Tensor get_key_pool() { return get_pool_tensors().first; }
@@ -121,7 +136,14 @@ std::vector<torch::Tensor> get_int4_pool_tensors() {
   require_pool("get_int4_pool_tensors");
   auto& p = P();
   TORCH_CHECK(p.int4, "get_int4_pool_tensors: pool was initialised with kv_format='fp16'");
-  return {p.kc, p.ks, p.vc, p.vs};
+  return int4_views(p.kvp, p.bs, p.d);
+}
+
+torch::Tensor get_int4_pages() {
+  require_pool("get_int4_pages");
+  auto& p = P();
+  TORCH_CHECK(p.int4, "get_int4_pages: pool was initialised with kv_format='fp16'");
+  return p.kvp;
 }
 
 std::string pool_format() {
@@ -174,8 +196,7 @@ void write_cache(torch::Tensor keys, torch::Tensor values, torch::Tensor block_t
                                 D, p.k.data_ptr(), p.v.data_ptr(), p.nb, p.bs, badp, cur_stream());
   } else {
     st = memopt_write_cache_int4(keys.data_ptr(), values.data_ptr(), slot_mapping.data_ptr<int32_t>(), T, H,
-                                 D, p.kc.data_ptr<uint8_t>(), p.ks.data_ptr(), p.vc.data_ptr<uint8_t>(),
-                                 p.vs.data_ptr(), p.nb, p.bs, badp, cur_stream());
+                                 D, p.kvp.data_ptr<uint8_t>(), p.nb, p.bs, badp, cur_stream());
   }
   check(st, "write_cache");
   if (debug) {
@@ -333,40 +354,31 @@ torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_ca
   return out;
 }
 
-torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor key_codes, torch::Tensor key_scales,
-                                            torch::Tensor value_codes, torch::Tensor value_scales,
-                                            torch::Tensor block_tables, torch::Tensor context_lens,
-                                            int max_seq_len, int window_size) {
+torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor kv_pages, torch::Tensor block_tables,
+                                            torch::Tensor context_lens, int max_seq_len, int window_size) {
   attn_checks(query, block_tables, context_lens);
-  for (auto* t : {&key_codes, &value_codes}) {
-    TORCH_CHECK(t->is_cuda() && t->dim() == 4 && t->scalar_type() == torch::kUInt8 && t->is_contiguous(),
-                "int4 codes must be contiguous CUDA uint8 [num_blocks, num_heads, block_size, head_dim/2]");
-  }
-  for (auto* t : {&key_scales, &value_scales}) {
-    TORCH_CHECK(t->is_cuda() && t->dim() == 4 && t->scalar_type() == torch::kFloat16 && t->is_contiguous(),
-                "int4 scales must be contiguous CUDA fp16 [num_blocks, num_heads, block_size, head_dim/64]");
-  }
+  TORCH_CHECK(kv_pages.is_cuda() && kv_pages.dim() == 3 && kv_pages.scalar_type() == torch::kUInt8 &&
+                  kv_pages.is_contiguous(),
+              "kv_pages must be a contiguous CUDA uint8 tensor [num_blocks, num_heads, page_bytes]");
   const int B = static_cast<int>(query.size(0)), QL = static_cast<int>(query.size(1));
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
-  const int BS = static_cast<int>(key_codes.size(2));
+  TORCH_CHECK(kv_pages.size(1) == H, "kv_pages num_heads ", kv_pages.size(1), " != query num_heads ", H);
+  TORCH_CHECK(D % 64 == 0, "dynamic_sparse_attention_int4: head_dim must be a multiple of 64");
+  const int64_t per_token = D + 4 * (D / 64);
+  TORCH_CHECK(kv_pages.size(2) % per_token == 0, "kv_pages page_bytes ", kv_pages.size(2),
+              " is not a whole number of tokens for head_dim ", D);
+  const int BS = static_cast<int>(kv_pages.size(2) / per_token);
   const int MB = static_cast<int>(block_tables.size(1));
-  TORCH_CHECK(key_codes.size(1) == H && key_codes.size(3) * 2 == D, "key_codes shape mismatch with query");
-  TORCH_CHECK(value_codes.sizes() == key_codes.sizes(), "value_codes shape mismatch");
-  TORCH_CHECK(key_scales.size(0) == key_codes.size(0) && key_scales.size(1) == H && key_scales.size(2) == BS &&
-                  key_scales.size(3) * 64 == D,
-              "key_scales shape mismatch");
-  TORCH_CHECK(value_scales.sizes() == key_scales.sizes(), "value_scales shape mismatch");
   auto out = torch::empty_like(query);
   if (B == 0 || QL == 0 || H == 0 || D == 0) return out;
   const at::cuda::CUDAGuard g(query.device());
   auto q = aligned_contig(query);
   size_t wsb = 0;
   auto ws = attn_workspace(q, MB, BS, max_seq_len, window_size, &wsb);
-  check(memopt_paged_attention_int4(q.data_ptr(), key_codes.data_ptr<uint8_t>(), key_scales.data_ptr(),
-                                    value_codes.data_ptr<uint8_t>(), value_scales.data_ptr(),
-                                    block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(), B, QL, H,
-                                    D, MB, key_codes.size(0), BS, max_seq_len, window_size, out.data_ptr(),
-                                    wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
+  check(memopt_paged_attention_int4(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
+                                    context_lens.data_ptr<int32_t>(), B, QL, H, D, MB, kv_pages.size(0), BS,
+                                    max_seq_len, window_size, out.data_ptr(), wsb ? ws.data_ptr() : nullptr, wsb,
+                                    cur_stream()),
         "dynamic_sparse_attention_int4");
   return out;
 }
@@ -436,7 +448,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("get_key_pool", &get_key_pool, "Return the key pool tensor");
   m.def("get_value_pool", &get_value_pool, "Return the value pool tensor");
   m.def("get_int4_pool_tensors", &get_int4_pool_tensors,
-        "Return [key_codes, key_scales, value_codes, value_scales] of an int4 pool");
+        "Return strided views [key_codes, key_scales, value_codes, value_scales] of an int4 pool");
+  m.def("get_int4_pages", &get_int4_pages, "Return the int4 page tensor [num_blocks, num_heads, page_bytes]");
   m.def("pool_format", &pool_format, "'fp16' or 'int4'");
   m.def("free_blocks_count", &free_blocks_count, "Return the number of free blocks remaining in the pool");
   m.def("write_cache", &write_cache, "Scatter key/value tokens into the paged KV cache pool via slot_mapping",

@@ -8,9 +8,9 @@
 //
 // The INT4 variant quantises while it writes (no reference counterpart for
 // the fusion; the per-group arithmetic follows quantization.cu:129-202) into
-// the head-major INT4 page format:
-//   codes  [num_blocks, num_heads, block_size, head_dim/2]  uint8
-//   scales [num_blocks, num_heads, block_size, head_dim/64] fp16
+// the INT4 page format: one contiguous page per (block, head) holding
+// [K codes | V codes | K scales | V scales], so a decode step moves each page
+// with a single bulk copy.
 #include "int4.cuh"
 
 namespace memopt {
@@ -91,14 +91,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
 write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
                         const int32_t* __restrict__ slots, int64_t num_tokens, int num_heads,
                         int head_dim, int block_size, int64_t num_slots,
-                        uint32_t* __restrict__ kcodes, __half* __restrict__ kscales,
-                        uint32_t* __restrict__ vcodes, __half* __restrict__ vscales,
-                        int32_t* __restrict__ bad) {
+                        uint8_t* __restrict__ pages, int64_t page_bytes, int32_t* __restrict__ bad) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
   const int gpr = head_dim / 64;                // groups per (token, head)
   const int chunks = num_heads * head_dim / 8;  // 16-byte chunks per token row
+  const int64_t codes_bytes = static_cast<int64_t>(block_size) * (head_dim / 2);
+  const int64_t scale_bytes = static_cast<int64_t>(block_size) * gpr * 2;
   for (int64_t t = warp; t < num_tokens; t += nwarps) {
     const int32_t slot = __ldg(slots + t);
     if (!slot_ok(slot, num_slots)) {
@@ -136,13 +136,15 @@ write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict_
           const int g = c >> 3;  // group within the token row
           const int h = g / gpr;
           const int gi = g - h * gpr;
-          const int64_t row = (blk * num_heads + h) * block_size + pos;  // (blk, h, pos)
-          const int64_t word = row * (head_dim / 8) + gi * 8 + (c & 7);
-          kcodes[word] = int4_pack8(fk, sk);
-          vcodes[word] = int4_pack8(fv, sv);
+          uint8_t* page = pages + (blk * num_heads + h) * page_bytes;
+          const int64_t code_off = static_cast<int64_t>(pos) * (head_dim / 2) + gi * 32 + (c & 7) * 4;
+          *reinterpret_cast<uint32_t*>(page + code_off) = int4_pack8(fk, sk);
+          *reinterpret_cast<uint32_t*>(page + codes_bytes + code_off) = int4_pack8(fv, sv);
           if ((c & 7) == 0) {
-            kscales[row * gpr + gi] = __float2half_rn(sk);
-            vscales[row * gpr + gi] = __float2half_rn(sv);
+            __half* ks = reinterpret_cast<__half*>(page + 2 * codes_bytes);
+            __half* vs = reinterpret_cast<__half*>(page + 2 * codes_bytes + scale_bytes);
+            ks[pos * gpr + gi] = __float2half_rn(sk);
+            vs[pos * gpr + gi] = __float2half_rn(sv);
           }
         }
       }
@@ -193,29 +195,29 @@ extern "C" int memopt_write_cache_f16(const void* keys, const void* values,
   return MEMOPT_OK;
 }
 
+extern "C" size_t memopt_int4_page_bytes(int block_size, int head_dim) {
+  if (block_size <= 0 || head_dim <= 0 || head_dim % 64 != 0) return 0;
+  return static_cast<size_t>(block_size) * head_dim + static_cast<size_t>(block_size) * (head_dim / 64) * 4;
+}
+
 extern "C" int memopt_write_cache_int4(const void* keys, const void* values,
                                        const int32_t* slot_mapping, int64_t num_tokens,
-                                       int num_heads, int head_dim, uint8_t* key_codes,
-                                       void* key_scales, uint8_t* value_codes,
-                                       void* value_scales, int64_t num_blocks, int block_size,
+                                       int num_heads, int head_dim, uint8_t* kv_pages,
+                                       int64_t num_blocks, int block_size,
                                        int32_t* bad_slot_count, void* stream) {
   if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || num_blocks < 0 || block_size <= 0)
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: invalid geometry");
   if (head_dim % 64 != 0)
     return fail(MEMOPT_ERR_UNSUPPORTED, "write_cache_int4: head_dim must be a multiple of 64");
   if (num_tokens == 0) return MEMOPT_OK;
-  if (!keys || !values || !slot_mapping || !key_codes || !key_scales || !value_codes || !value_scales)
+  if (!keys || !values || !slot_mapping || !kv_pages)
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: null pointer");
-  if (!aligned16(keys) || !aligned16(values) || (reinterpret_cast<uintptr_t>(key_codes) & 3u) ||
-      (reinterpret_cast<uintptr_t>(value_codes) & 3u) || (reinterpret_cast<uintptr_t>(key_scales) & 1u) ||
-      (reinterpret_cast<uintptr_t>(value_scales) & 1u))
+  if (!aligned16(keys) || !aligned16(values) || !aligned16(kv_pages))
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: misaligned pointer");
   write_cache_int4_kernel<<<grid_for_tokens(num_tokens), kWarpsPerCta * 32, 0, as_stream(stream)>>>(
       reinterpret_cast<const uint4*>(keys), reinterpret_cast<const uint4*>(values), slot_mapping,
-      num_tokens, num_heads, head_dim, block_size, num_blocks * block_size,
-      reinterpret_cast<uint32_t*>(key_codes), reinterpret_cast<__half*>(key_scales),
-      reinterpret_cast<uint32_t*>(value_codes), reinterpret_cast<__half*>(value_scales),
-      bad_slot_count);
+      num_tokens, num_heads, head_dim, block_size, num_blocks * block_size, kv_pages,
+      static_cast<int64_t>(memopt_int4_page_bytes(block_size, head_dim)), bad_slot_count);
   MEMOPT_LAUNCH_CHECK("write_cache_int4 launch");
   return MEMOPT_OK;
 }

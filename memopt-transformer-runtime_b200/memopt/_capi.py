@@ -43,13 +43,12 @@ def paged_attention_f16(q, kpool, vpool, bt, ctx, out, msl, win, ws, ws_bytes, s
         "memopt_paged_attention_f16")
 
 
-def paged_attention_int4(q, kc, ks, vc, vs, bt, ctx, out, msl, win, ws, ws_bytes, stream):
+def paged_attention_int4(q, pages, block_size, bt, ctx, out, msl, win, ws, ws_bytes, stream):
     B, QL, H, D = q.shape
     check(lib().memopt_paged_attention_int4(
-        P(q.data_ptr()), P(kc.data_ptr()), P(ks.data_ptr()), P(vc.data_ptr()), P(vs.data_ptr()),
-        P(bt.data_ptr()), P(ctx.data_ptr()), I(B), I(QL), I(H), I(D), I(bt.shape[1]), I64(kc.shape[0]),
-        I(kc.shape[2]), I(msl), I(win), P(out.data_ptr()), P(ws.data_ptr() if ws is not None else 0),
-        SZ(ws_bytes), P(stream)), "memopt_paged_attention_int4")
+        P(q.data_ptr()), P(pages.data_ptr()), P(bt.data_ptr()), P(ctx.data_ptr()), I(B), I(QL), I(H), I(D),
+        I(bt.shape[1]), I64(pages.shape[0]), I(block_size), I(msl), I(win), P(out.data_ptr()),
+        P(ws.data_ptr() if ws is not None else 0), SZ(ws_bytes), P(stream)), "memopt_paged_attention_int4")
 
 
 def workspace_size(B, QL, H, D, MB, BS, msl, win) -> int:

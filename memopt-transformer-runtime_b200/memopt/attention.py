@@ -140,9 +140,9 @@ class DynamicAttention(nn.Module):
         q16 = q.to(torch.float16).reshape(B, seq_len, H, D).contiguous()
         window = self._effective_window(seq_len)
         if _memopt_C.pool_format() == "int4":
-            kc, ks, vc, vs = _memopt_C.get_int4_pool_tensors()
+            pages = _memopt_C.get_int4_pages()
             out = _memopt_C.dynamic_sparse_attention_int4(
-                q16, kc, ks, vc, vs, block_tables, context_lens, seq_len, window
+                q16, pages, block_tables, context_lens, seq_len, window
             )
         else:
             key_cache = _memopt_C.get_key_pool()

@@ -140,28 +140,32 @@ void oracle_write_cache_f16(const uint16_t* keys, const uint16_t* values, const 
   }
 }
 
-/* INT4 pages: codes [NB, H, BS, D/2], scales fp16 [NB, H, BS, D/64]. */
+/* INT4 pages: one page per (block, head) of
+ * [K codes BS*D/2 | V codes BS*D/2 | K scales BS*(D/64) fp16 | V scales]. */
+static int64_t int4_page_bytes(int BS, int D) { return (int64_t)BS * D + (int64_t)BS * (D / 64) * 4; }
+
 void oracle_write_cache_int4(const uint16_t* keys, const uint16_t* values, const int32_t* slots,
-                             int64_t T, int H, int D, uint8_t* kcodes, uint16_t* kscales,
-                             uint8_t* vcodes, uint16_t* vscales, int64_t NB, int BS) {
+                             int64_t T, int H, int D, uint8_t* pages, int64_t NB, int BS) {
   const int gpr = D / 64;
+  const int64_t pb = int4_page_bytes(BS, D), codes = (int64_t)BS * (D / 2);
   for (int64_t t = 0; t < T; ++t) {
     const int32_t s = slots[t];
     if (s < 0 || (int64_t)s >= NB * BS) continue;
     const int64_t blk = s / BS;
     const int pos = s % BS;
     for (int h = 0; h < H; ++h) {
-      const int64_t r = (blk * H + h) * BS + pos;
+      uint8_t* page = pages + (blk * H + h) * pb;
       for (int g = 0; g < gpr; ++g) {
         for (int kv = 0; kv < 2; ++kv) {
           const uint16_t* src = (kv ? values : keys) + (t * H + h) * D + g * 64;
           float v[64];
           for (int i = 0; i < 64; ++i) v[i] = oracle_f16_to_f32(src[i]);
           const float sc = int4_scale(v, 64);
-          uint8_t* codes = (kv ? vcodes : kcodes) + r * (D / 2) + g * 32;
+          uint8_t* c = page + kv * codes + (int64_t)pos * (D / 2) + g * 32;
           for (int i = 0; i < 32; ++i)
-            codes[i] = (uint8_t)(int4_code(v[2 * i], sc) | (int4_code(v[2 * i + 1], sc) << 4));
-          (kv ? vscales : kscales)[r * gpr + g] = oracle_f32_to_f16(sc);
+            c[i] = (uint8_t)(int4_code(v[2 * i], sc) | (int4_code(v[2 * i + 1], sc) << 4));
+          const uint16_t hs = oracle_f32_to_f16(sc);
+          memcpy(page + 2 * codes + (int64_t)kv * BS * gpr * 2 + ((int64_t)pos * gpr + g) * 2, &hs, 2);
         }
       }
     }
@@ -283,8 +287,7 @@ void oracle_evict_cache(const float* scores, int NB, int BS, int H, int D, uint1
 typedef struct {
   int fmt;
   const uint16_t *kp, *vp;
-  const uint8_t *kc, *vc;
-  const uint16_t *ks, *vs;
+  const uint8_t* pages;
   int H, D, BS;
 } kv_src;
 
@@ -293,12 +296,16 @@ static void fetch_row(const kv_src* s, int kv, int64_t phys, int pos, int h, dou
     const uint16_t* p = (kv ? s->vp : s->kp) + ((phys * s->BS + pos) * s->H + h) * s->D;
     for (int d = 0; d < s->D; ++d) out[d] = oracle_f16_to_f32(p[d]);
   } else {
-    const int64_t r = (phys * s->H + h) * s->BS + pos;
-    const uint8_t* c = (kv ? s->vc : s->kc) + r * (s->D / 2);
-    const uint16_t* sc = (kv ? s->vs : s->ks) + r * (s->D / 64);
+    const int64_t pb = int4_page_bytes(s->BS, s->D), codes = (int64_t)s->BS * (s->D / 2);
+    const int G = s->D / 64;
+    const uint8_t* page = s->pages + (phys * s->H + h) * pb;
+    const uint8_t* c = page + kv * codes + (int64_t)pos * (s->D / 2);
+    const uint8_t* sc = page + 2 * codes + (int64_t)kv * s->BS * G * 2 + (int64_t)pos * G * 2;
     for (int d = 0; d < s->D; ++d) {
       const int code = (d & 1) ? (c[d / 2] >> 4) : (c[d / 2] & 0xF);
-      out[d] = (double)(code - 8) * (double)oracle_f16_to_f32(sc[d / 64]);
+      uint16_t hs;
+      memcpy(&hs, sc + (d / 64) * 2, 2);
+      out[d] = (double)(code - 8) * (double)oracle_f16_to_f32(hs);
     }
   }
 }
@@ -349,14 +356,13 @@ void oracle_paged_attention_f16(const uint16_t* q, const uint16_t* kpool, const 
                                 const int32_t* bt, const int32_t* ctx, int B, int QL, int H, int D,
                                 int MB, int64_t NB, int BS, int max_seq_len, int window,
                                 double* out) {
-  kv_src s = {0, kpool, vpool, 0, 0, 0, 0, H, D, BS};
+  kv_src s = {0, kpool, vpool, 0, H, D, BS};
   attention_core(q, &s, bt, ctx, B, QL, MB, NB, max_seq_len, window, out);
 }
 
-void oracle_paged_attention_int4(const uint16_t* q, const uint8_t* kcodes, const uint16_t* kscales,
-                                 const uint8_t* vcodes, const uint16_t* vscales, const int32_t* bt,
+void oracle_paged_attention_int4(const uint16_t* q, const uint8_t* pages, const int32_t* bt,
                                  const int32_t* ctx, int B, int QL, int H, int D, int MB, int64_t NB,
                                  int BS, int max_seq_len, int window, double* out) {
-  kv_src s = {1, 0, 0, kcodes, vcodes, kscales, vscales, H, D, BS};
+  kv_src s = {1, 0, 0, pages, H, D, BS};
   attention_core(q, &s, bt, ctx, B, QL, MB, NB, max_seq_len, window, out);
 }

@@ -85,13 +85,29 @@ def write_cache_f16(keys, values, slots, kpool, vpool) -> None:
                                  _p(kpool), _p(vpool), I64(NB), I32(BS))
 
 
-def write_cache_int4(keys, values, slots, kcodes, kscales, vcodes, vscales) -> None:
-    """In place on INT4 pages: codes [NB, H, BS, D/2] u8, scales [NB, H, BS, D/64] fp16."""
+def int4_page_bytes(block_size: int, head_dim: int) -> int:
+    return block_size * head_dim + block_size * (head_dim // 64) * 4
+
+
+def write_cache_int4(keys, values, slots, pages, block_size) -> None:
+    """In place on INT4 pages uint8 [NB, H, page_bytes]."""
     T, H, D = keys.shape
-    NB, BS = kcodes.shape[0], kcodes.shape[2]
+    NB = pages.shape[0]
     keys, values, slots = _c(keys, np.float16), _c(values, np.float16), _c(slots, np.int32)
-    lib().oracle_write_cache_int4(_p(keys), _p(values), _p(slots), I64(T), I32(H), I32(D),
-                                  _p(kcodes), _p(kscales), _p(vcodes), _p(vscales), I64(NB), I32(BS))
+    lib().oracle_write_cache_int4(_p(keys), _p(values), _p(slots), I64(T), I32(H), I32(D), _p(pages),
+                                  I64(NB), I32(block_size))
+
+
+def int4_views(pages, block_size, head_dim):
+    """(k_codes, k_scales, v_codes, v_scales) numpy views of the INT4 pages."""
+    NB, H, PB = pages.shape
+    BS, D, G = block_size, head_dim, head_dim // 64
+    cb = BS * D // 2
+    kc = pages[:, :, :cb].reshape(NB, H, BS, D // 2)
+    vc = pages[:, :, cb:2 * cb].reshape(NB, H, BS, D // 2)
+    ks = np.ascontiguousarray(pages[:, :, 2 * cb:2 * cb + BS * G * 2]).view(np.float16).reshape(NB, H, BS, G)
+    vs = np.ascontiguousarray(pages[:, :, 2 * cb + BS * G * 2:]).view(np.float16).reshape(NB, H, BS, G)
+    return kc, ks, vc, vs
 
 
 def evict_tokens(scores, block_tables, is_block_free, kpool, vpool, retain_ratio, num_sink_tokens=4):
@@ -131,15 +147,13 @@ def paged_attention_f16(q, kpool, vpool, block_tables, context_lens, max_seq_len
     return out
 
 
-def paged_attention_int4(q, kcodes, kscales, vcodes, vscales, block_tables, context_lens,
-                         max_seq_len, window_size):
+def paged_attention_int4(q, pages, block_tables, context_lens, max_seq_len, window_size, block_size):
     q = _c(q, np.float16)
     B, QL, H, D = q.shape
-    NB, BS = kcodes.shape[0], kcodes.shape[2]
+    NB = pages.shape[0]
     bt, cl = _c(block_tables, np.int32), _c(context_lens, np.int32)
     out = np.zeros((B, QL, H, D), np.float64)
-    lib().oracle_paged_attention_int4(_p(q), _p(_c(kcodes)), _p(_c(kscales)), _p(_c(vcodes)),
-                                      _p(_c(vscales)), _p(bt), _p(cl), I32(B), I32(QL), I32(H), I32(D),
-                                      I32(bt.shape[1]), I64(NB), I32(BS), I32(max_seq_len),
+    lib().oracle_paged_attention_int4(_p(q), _p(_c(pages)), _p(bt), _p(cl), I32(B), I32(QL), I32(H), I32(D),
+                                      I32(bt.shape[1]), I64(NB), I32(block_size), I32(max_seq_len),
                                       I32(window_size), _p(out))
     return out

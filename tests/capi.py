@@ -44,11 +44,10 @@ def write_cache_f16(keys, values, slots, kpool, vpool, bad=None):
                                     ptr(vpool), I64(kpool.shape[0]), I(kpool.shape[1]), ptr(bad), stream()))
 
 
-def write_cache_int4(keys, values, slots, kc, ks, vc, vs, bad=None):
+def write_cache_int4(keys, values, slots, pages, block_size, bad=None):
     T, H, D = keys.shape
-    ok(lib().memopt_write_cache_int4(ptr(keys), ptr(values), ptr(slots), I64(T), I(H), I(D), ptr(kc),
-                                     ptr(ks), ptr(vc), ptr(vs), I64(kc.shape[0]), I(kc.shape[2]), ptr(bad),
-                                     stream()))
+    ok(lib().memopt_write_cache_int4(ptr(keys), ptr(values), ptr(slots), I64(T), I(H), I(D), ptr(pages),
+                                     I64(pages.shape[0]), I(block_size), ptr(bad), stream()))
 
 
 def quantize(x):
@@ -103,15 +102,20 @@ def attention_f16(q, kpool, vpool, bt, ctx, msl, win, ws=None):
     return out
 
 
-def attention_int4(q, kc, ks, vc, vs, bt, ctx, msl, win, ws=None):
+def attention_int4(q, pages, block_size, bt, ctx, msl, win, ws=None):
     B, QL, H, D = q.shape
     MB = bt.shape[1]
     out = torch.empty_like(q)
     if ws is None:
-        ws, n = workspace(B, QL, H, D, MB, kc.shape[2], msl, win)
+        ws, n = workspace(B, QL, H, D, MB, block_size, msl, win)
     else:
         n = ws.numel()
-    ok(lib().memopt_paged_attention_int4(ptr(q), ptr(kc), ptr(ks), ptr(vc), ptr(vs), ptr(bt), ptr(ctx), I(B),
-                                         I(QL), I(H), I(D), I(MB), I64(kc.shape[0]), I(kc.shape[2]), I(msl),
-                                         I(win), ptr(out), ptr(ws), SZ(n), stream()))
+    ok(lib().memopt_paged_attention_int4(ptr(q), ptr(pages), ptr(bt), ptr(ctx), I(B), I(QL), I(H), I(D), I(MB),
+                                         I64(pages.shape[0]), I(block_size), I(msl), I(win), ptr(out), ptr(ws),
+                                         SZ(n), stream()))
     return out
+
+
+def int4_page_bytes(block_size, head_dim):
+    lib().memopt_int4_page_bytes.restype = SZ
+    return int(lib().memopt_int4_page_bytes(I(block_size), I(head_dim)))

@@ -100,24 +100,25 @@ def test_write_cache_int4_bit_exact(T, H, D, NB, BS):
     v = (rng.standard_normal((T, H, D)) * 3).astype(np.float16)
     k[0, 0, :64] = 0  # all-zero group -> scale 1.0
     s = _slots(T, NB, BS, T + 1, bad=min(2, T - 1))
-    kc = np.zeros((NB, H, BS, D // 2), np.uint8)
-    vc = np.zeros_like(kc)
-    ks = np.zeros((NB, H, BS, D // 64), np.float16)
-    vs = np.zeros_like(ks)
-    O.write_cache_int4(k, v, s, kc, ks, vc, vs)
-    g = {n: torch.from_numpy(a.copy()).to(DEV) for n, a in dict(kc=kc * 0, ks=ks * 0, vc=vc * 0, vs=vs * 0).items()}
+    PB = O.int4_page_bytes(BS, D)
+    assert PB == capi.int4_page_bytes(BS, D)
+    pages = np.zeros((NB, H, PB), np.uint8)
+    O.write_cache_int4(k, v, s, pages, BS)
+    g = torch.zeros(NB, H, PB, dtype=torch.uint8, device=DEV)
     capi.write_cache_int4(torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV), torch.from_numpy(s).to(DEV),
-                          g["kc"], g["ks"], g["vc"], g["vs"])
-    assert np.array_equal(np16(g["kc"]), kc) and np.array_equal(np16(g["vc"]), vc)
-    assert np.array_equal(np16(g["ks"]).view(np.uint16), ks.view(np.uint16))
-    assert np.array_equal(np16(g["vs"]).view(np.uint16), vs.view(np.uint16))
-    # codes agree with the standalone reference quantizer on each (token, head) row
+                          g, BS)
+    assert np.array_equal(np16(g), pages)
+    # codes and scales agree with the standalone reference quantizer on each (token, head) row
+    kc, ks, vc, vs = O.int4_views(pages, BS, D)
     ok_t = [i for i in range(T) if 0 <= s[i] < NB * BS]
-    t = ok_t[0]
-    pr, sr = O.quantize_int4(k[t])
-    blk, pos = divmod(int(s[t]), BS)
-    assert np.array_equal(kc[blk, :, pos, :], pr.reshape(H, D // 2))
-    assert np.array_equal(ks[blk, :, pos, :].astype(np.float32).reshape(-1), sr.astype(np.float16).astype(np.float32))
+    for t in ok_t[:3]:
+        blk, pos = divmod(int(s[t]), BS)
+        pr, sr = O.quantize_int4(k[t])
+        assert np.array_equal(kc[blk, :, pos, :], pr.reshape(H, D // 2))
+        assert np.array_equal(ks[blk, :, pos, :].reshape(-1).view(np.uint16), sr.astype(np.float16).view(np.uint16))
+        pr, sr = O.quantize_int4(v[t])
+        assert np.array_equal(vc[blk, :, pos, :], pr.reshape(H, D // 2))
+        assert np.array_equal(vs[blk, :, pos, :].reshape(-1).view(np.uint16), sr.astype(np.float16).view(np.uint16))
 
 
 # ------------------------------------------------------------ evict_tokens
@@ -237,15 +238,12 @@ def test_attention_int4_vs_oracle(case):
     keys = kp.reshape(T, H, D)
     vals = vp.reshape(T, H, D)
     slots = np.arange(T, dtype=np.int32)
-    gkc = torch.zeros(NB, H, BS, D // 2, dtype=torch.uint8, device=DEV)
-    gvc = torch.zeros_like(gkc)
-    gks = torch.zeros(NB, H, BS, D // 64, dtype=torch.float16, device=DEV)
-    gvs = torch.zeros_like(gks)
+    pages = torch.zeros(NB, H, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
     capi.write_cache_int4(torch.from_numpy(keys).to(DEV), torch.from_numpy(vals).to(DEV),
-                          torch.from_numpy(slots).to(DEV), gkc, gks, gvc, gvs)
-    got = capi.attention_int4(torch.from_numpy(q).to(DEV), gkc, gks, gvc, gvs, torch.from_numpy(bt).to(DEV),
+                          torch.from_numpy(slots).to(DEV), pages, BS)
+    got = capi.attention_int4(torch.from_numpy(q).to(DEV), pages, BS, torch.from_numpy(bt).to(DEV),
                               torch.from_numpy(cl).to(DEV), msl, win)
-    ref = O.paged_attention_int4(q, np16(gkc), np16(gks), np16(gvc), np16(gvs), bt, cl, msl, win)
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS)
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
 
 

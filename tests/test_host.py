@@ -100,7 +100,7 @@ def test_memopt_c_module_surface():
                  "free_blocks_count", "write_cache", "evict_cache", "evict_tokens",
                  "dynamic_sparse_attention", "quantize_kv_cache_int4", "dequantize_kv_cache_int4",
                  "get_key_pool", "get_value_pool", "dynamic_sparse_attention_int4",
-                 "get_int4_pool_tensors"]:
+                 "get_int4_pool_tensors", "get_int4_pages"]:
         assert hasattr(memopt_C, name), name
     assert "MemOpt C++ Backend Initialized" in memopt_C.get_hello()
 
