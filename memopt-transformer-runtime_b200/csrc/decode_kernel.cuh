@@ -176,7 +176,6 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   constexpr int G = D / 64;      // int4 scale groups per row
   constexpr int NKM = D / 16;    // int4: k-steps of the score mma
   constexpr int NT = D / 8;      // int4: n-tiles of the P.V mma
-  constexpr int MT = BS / 16;    // int4: 16-token m-tiles per page
   uint32_t c_seq = 0;
   bool failed = false;
 
@@ -220,24 +219,28 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
     for (int j = 0; j < (INT4 ? NT : 1); ++j) acc[j][0] = acc[j][1] = 0.f;
 
-    while (mask != 0) {
-      const int jpage = __ffs(mask) - 1;
-      mask &= mask - 1;
-      const int page = c_lo + jpage;
-      const int s = static_cast<int>(c_seq % NS);
-      const uint32_t parity = (c_seq / NS) & 1u;
-      // Warp-uniform bounded wait (a completed phase stays observable).
+    // Warp-uniform bounded wait for stage `seq` (a completed phase stays observable).
+    auto wait_stage = [&](uint32_t seq) -> bool {
+      const int st = static_cast<int>(seq % NS);
+      const uint32_t parity = (seq / NS) & 1u;
       uint32_t polls = 0;
-      bool ready = mbar_try_wait(bar0 + 8 * s, parity);
+      bool ready = mbar_try_wait(bar0 + 8 * st, parity);
       while (!__all_sync(0xffffffffu, ready) && ++polls < kMaxPolls) {
-        if (!ready) ready = mbar_try_wait(bar0 + 8 * s, parity);
+        if (!ready) ready = mbar_try_wait(bar0 + 8 * st, parity);
       }
-      if (!__all_sync(0xffffffffu, ready)) {
-        failed = true;
-        break;
-      }
-      const uint8_t* stg = stages + s * C::STAGE;
-      if constexpr (!INT4) {
+      return __all_sync(0xffffffffu, ready);
+    };
+
+    if constexpr (!INT4) {
+      while (mask != 0) {
+        const int jpage = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const int page = c_lo + jpage;
+        if (!wait_stage(c_seq)) {
+          failed = true;
+          break;
+        }
+        const uint8_t* stg = stages + static_cast<int>(c_seq % NS) * C::STAGE;
         // ---- scores: lane partials for TPL rows, then transpose-reduce ----
         float val[C::TPL];
 #pragma unroll
@@ -305,15 +308,43 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             }
           }
         }
-      } else {
-        using namespace int4mma;
-        const __half* ksc = reinterpret_cast<const __half*>(stg + 2 * C::K_BYTES);
-        const __half* vsc = reinterpret_cast<const __half*>(stg + 2 * C::K_BYTES + C::S_BYTES);
-        float slo[MT], shi[MT];
-        // ---- scores on the tensor pipe, one m-tile (16 tokens) at a time ----
+        __syncwarp();
+        ++c_seq;
+        produce();
+      }
+    } else {
+      using namespace int4mma;
+      // Two 16-token tiles per softmax step: both halves of a 32-token page,
+      // or two consecutive 16-token pages of the item.
+      while (mask != 0) {
+        const int ja = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const bool two_pages = (BS == 16) && (mask != 0);
+        int jb = ja;
+        if (two_pages) {
+          jb = __ffs(mask) - 1;
+          mask &= mask - 1;
+        }
+        if (!wait_stage(c_seq) || (two_pages && !wait_stage(c_seq + 1))) {
+          failed = true;
+          break;
+        }
+        const uint8_t* stg_a = stages + static_cast<int>(c_seq % NS) * C::STAGE;
+        const uint8_t* stg_b = two_pages ? stages + static_cast<int>((c_seq + 1) % NS) * C::STAGE : stg_a;
+        const bool has2 = (BS == 32) || two_pages;
+        // tile -> (stage, first row in the stage, first token position)
+        const uint8_t* tstg[2] = {stg_a, (BS == 32) ? stg_a : stg_b};
+        const int trow[2] = {0, (BS == 32) ? 16 : 0};
+        const int ttok[2] = {(c_lo + ja) * BS, (BS == 32) ? (c_lo + ja) * BS + 16 : (c_lo + jb) * BS};
+        float slo[2], shi[2];
+        // ---- scores on the tensor pipe ----
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const uint8_t* kr = stg + mt * 16 * (D / 2);
+        for (int ti = 0; ti < 2; ++ti) {
+          slo[ti] = -INFINITY;
+          shi[ti] = -INFINITY;
+          if (ti == 1 && !has2) break;
+          const uint8_t* kr = tstg[ti] + trow[ti] * (D / 2);
+          const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
           uint32_t w0[D / 32], w1[D / 32];
           if constexpr (D == 128) {
             const uint4 x0 = *reinterpret_cast<const uint4*>(kr + mg * (D / 2) + mt4 * 16);
@@ -343,35 +374,32 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
           for (int e = 0; e < 4; ++e) c[e] += c2[e];
           // Lanes with mt4 == 0 hold (group0, group1) partials of tokens mg, mg+8.
-          const int rl = mt * 16 + mg;
-          float a_lo = __half2float(ksc[rl * G]) * c[0];
-          float a_hi = __half2float(ksc[(rl + 8) * G]) * c[2];
+          float a_lo = __half2float(ksc[mg * G]) * c[0];
+          float a_hi = __half2float(ksc[(mg + 8) * G]) * c[2];
           if constexpr (G > 1) {
-            a_lo = fmaf(__half2float(ksc[rl * G + 1]), c[1], a_lo);
-            a_hi = fmaf(__half2float(ksc[(rl + 8) * G + 1]), c[3], a_hi);
+            a_lo = fmaf(__half2float(ksc[mg * G + 1]), c[1], a_lo);
+            a_hi = fmaf(__half2float(ksc[(mg + 8) * G + 1]), c[3], a_hi);
           }
           a_lo = __shfl_sync(0xffffffffu, a_lo * p.qscale, lane & ~3);
           a_hi = __shfl_sync(0xffffffffu, a_hi * p.qscale, lane & ~3);
-          const int tl = page * BS + rl;
-          slo[mt] = (tl >= win_start && tl < ctx) ? a_lo : -INFINITY;
-          shi[mt] = (tl + 8 >= win_start && tl + 8 < ctx) ? a_hi : -INFINITY;
+          const int tl = ttok[ti] + mg;
+          const bool interior = ttok[ti] >= win_start && ttok[ti] + 16 <= ctx;
+          slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
+          shi[ti] = (interior || (tl + 8 >= win_start && tl + 8 < ctx)) ? a_hi : -INFINITY;
         }
-        float mp = -INFINITY;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mp = fmaxf(mp, fmaxf(slo[mt], shi[mt]));
+        float mp = fmaxf(fmaxf(slo[0], shi[0]), fmaxf(slo[1], shi[1]));
 #pragma unroll
         for (int mk = 16; mk >= 4; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
         const float m_new = fmaxf(m, mp);
         if (m_new != -INFINITY) {
           const float alpha = exp2f(m - m_new);
           m = m_new;
-          float psum = 0.f;
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            slo[mt] = exp2f(slo[mt] - m_new);
-            shi[mt] = exp2f(shi[mt] - m_new);
-            psum += slo[mt] + shi[mt];
+          for (int ti = 0; ti < 2; ++ti) {
+            slo[ti] = exp2f(slo[ti] - m_new);
+            shi[ti] = exp2f(shi[ti] - m_new);
           }
+          const float psum = (slo[0] + shi[0]) + (slo[1] + shi[1]);
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
           if (alpha != 1.f) {  // warp-uniform; skipped once the running max settles
 #pragma unroll
@@ -382,12 +410,14 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           }
           // ---- P.V on the tensor pipe ----
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const uint8_t* vr = stg + C::K_BYTES + mt * 16 * (D / 2);
+          for (int ti = 0; ti < 2; ++ti) {
+            if (ti == 1 && !has2) break;
+            const uint8_t* vr = tstg[ti] + C::K_BYTES + trow[ti] * (D / 2);
+            const __half* vsc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES + C::S_BYTES) + trow[ti] * G;
             uint32_t wa[4], wb[4];
             const int gs = mg < G ? mg : G - 1;  // scale group of A row mg (rows >= G unused)
             // p of tokens 0..7 travel in the low half, 8..15 in the high half.
-            const uint32_t pk = pack_half2(slo[mt], shi[mt]);
+            const uint32_t pk = pack_half2(slo[ti], shi[ti]);
             const uint32_t psel = (mt4 & 1) ? 0x7632u : 0x5410u;
             uint32_t a[4];
 #pragma unroll
@@ -404,8 +434,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * (r0 & 7));
               const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * (r1 & 7));
               const uint32_t p01 = __byte_perm(u0, u1, psel);
-              const uint32_t s0 = __half_as_ushort(vsc[(mt * 16 + r0) * G + gs]);
-              const uint32_t s1 = __half_as_ushort(vsc[(mt * 16 + r1) * G + gs]);
+              const uint32_t s0 = __half_as_ushort(vsc[r0 * G + gs]);
+              const uint32_t s1 = __half_as_ushort(vsc[r1 * G + gs]);
               const uint32_t v01 = s0 | (s1 << 16);
               const __half2 pv = __hmul2(*reinterpret_cast<const __half2*>(&p01),
                                          *reinterpret_cast<const __half2*>(&v01));
@@ -416,20 +446,24 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             // n-tiles 2jb and 2jb+1 read the low and high nibble of byte jb%4
             // of word (mg + 8 * (jb / 4)) from the four token rows.
 #pragma unroll
-            for (int jb = 0; jb < NT / 2; ++jb) {
-              const uint32_t* w = (jb < 4) ? wa : wb;
-              const uint32_t sel = static_cast<uint32_t>(jb % 4) | (static_cast<uint32_t>(4 + jb % 4) << 8);
+            for (int jq = 0; jq < NT / 2; ++jq) {
+              const uint32_t* w = (jq < 4) ? wa : wb;
+              const uint32_t sel = static_cast<uint32_t>(jq % 4) | (static_cast<uint32_t>(4 + jq % 4) << 8);
               const uint32_t x01 = __byte_perm(w[0], w[1], sel);
               const uint32_t x23 = __byte_perm(w[2], w[3], sel);
-              mma16816_top(acc[2 * jb][0], acc[2 * jb][1], a, lo_pair(x01), lo_pair(x23));
-              mma16816_top(acc[2 * jb + 1][0], acc[2 * jb + 1][1], a, hi_pair(x01), hi_pair(x23));
+              mma16816_top(acc[2 * jq][0], acc[2 * jq][1], a, lo_pair(x01), lo_pair(x23));
+              mma16816_top(acc[2 * jq + 1][0], acc[2 * jq + 1][1], a, hi_pair(x01), hi_pair(x23));
             }
           }
         }
+        __syncwarp();
+        ++c_seq;
+        produce();
+        if (two_pages) {
+          ++c_seq;
+          produce();
+        }
       }
-      __syncwarp();
-      ++c_seq;
-      produce();
     }
     if (failed) break;
 
