@@ -5,6 +5,7 @@
 // (block_size, head_dim) in {16,32} x {64,128} (:494-507), but launches on the
 // caller's stream (the reference used the legacy default stream).
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -13,6 +14,13 @@
 #include "decode_kernel.cuh"
 
 namespace memopt {
+
+// prefill.cu: tcgen05 path for q_len >= kPrefillMinRows.
+int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,
+                int B, int QL, int H, int D, int MB, int64_t NB, int BS, int window_clamped, void* out,
+                cudaStream_t s);
+constexpr int kPrefillMinRows = 64;
+
 namespace {
 
 using decode::Cfg;
@@ -224,6 +232,9 @@ extern "C" int memopt_paged_attention_f16(const void* query, const void* key_poo
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: pools must be 16-byte aligned");
   if (num_blocks * block_size > 0x7fffffffLL)
     return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: pool has more than 2^31 token rows");
+  if (q_len >= kPrefillMinRows && !std::getenv("MEMOPT_DISABLE_PREFILL"))
+    return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads, head_dim,
+                       max_blocks_per_seq, num_blocks, block_size, p.window, out, as_stream(stream));
   alignas(64) CUtensorMap km, vm;
   st = make_pool_map(&km, key_pool, num_blocks * block_size, num_heads, head_dim, block_size);
   if (st != MEMOPT_OK) return st;

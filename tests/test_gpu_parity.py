@@ -258,3 +258,27 @@ def test_attention_deterministic_and_workspace_reuse():
     assert torch.equal(o1, o2)
     tickets = capi.lib().memopt_paged_attention_ticket_bytes(B, QL, H)
     assert int(ws[:tickets].count_nonzero().item()) == 0  # tickets left zero
+
+
+# --------------------------------------------- prefill (q_len >= 64: tcgen05)
+PREFILL_CASES = [
+    # B, QL, H, D, BS, ctx, MB, max_seq_len, window, holes
+    (1, 64, 1, 128, 16, [128], 8, 128, 128, 0.0),
+    (1, 128, 2, 128, 16, [256], 16, 256, 256, 0.0),
+    (2, 130, 2, 128, 16, [300, 77], 20, 320, 320, 0.0),
+    (2, 256, 4, 64, 16, [1000, 1024], 64, 1024, 1024, 0.1),
+    (1, 200, 2, 128, 32, [777], 30, 960, 300, 0.1),
+    (2, 64, 2, 64, 32, [64, 0], 4, 128, -1, 0.0),
+    (1, 512, 8, 128, 16, [4096], 256, 4096, 1000, 0.0),
+]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES)
+def test_prefill_f16_vs_oracle(case):
+    B, QL, H, D, BS, ctx, MB, msl, win, holes = case
+    q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, sum(ctx) + QL, holes)
+    got = capi.attention_f16(torch.from_numpy(q).to(DEV), torch.from_numpy(kp).to(DEV),
+                             torch.from_numpy(vp).to(DEV), torch.from_numpy(bt).to(DEV),
+                             torch.from_numpy(cl).to(DEV), msl, win)
+    ref = O.paged_attention_f16(q, kp, vp, bt, cl, msl, win)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
