@@ -308,6 +308,7 @@ def run_ours(args) -> None:
     extra = {}
     if not args.no_int4:
         extra = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)
+        extra.update(prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
 
     # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
     cpu = None
@@ -424,9 +425,47 @@ def run_only(args) -> None:
         ms = time_loop(torch, lambda: _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, CTX, CTX, wsp, wsb, sp),
                        args.steps, args.warmup, lambda: None, stream)
         res = {"kernel": "paged_decode f16 cfg2", "ms": ms, "GB/s": step_bytes(B, CTX) / ms / 1e6}
+    elif args.only == "prefill":
+        res = prefill_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     else:
         res = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     print(json.dumps(res), flush=True)
+
+
+def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """BASELINE configs[4] prefill: 4 sequences x 8192 query tokens over their
+    own 8192 cached tokens, 32 heads x 128, fp16, non-causal (reference
+    semantics), on the tcgen05 path.  FLOPs = 4 * B * H * QL * ctx * D."""
+    pb, pql = 4, 8192
+    mb = pql // BS
+    nb = pb * mb
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    kp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    vp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(5 + rank))[: pb * mb].reshape(pb, mb)
+    bt = bt.to(torch.int32).to(dev)
+    q = torch.randn(pb, pql, H, D, device=dev, dtype=torch.float16, generator=g)
+    ctx = torch.full((pb,), pql, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+
+    def step():
+        _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, pql, pql, None, 0, sp)
+
+    steps = max(3, min(args.steps, 20))
+    ms = max_over_ranks(time_loop(torch, step, steps, args.warmup, barrier, stream))
+    flops = 4.0 * pb * H * pql * pql * D
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            tpk = float(json.load(f)["bf16_tflops"])
+        kind = "measured"
+    except Exception:  # noqa: BLE001
+        tpk, kind = 1590.0, "fallback"
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"prefill": {"workload": "BASELINE configs[4] prefill: 4 x 8192 tokens, 32 heads x 128, fp16, "
+                                    "non-causal over context_lens=8192",
+                        "value": round(tf * ws_n, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+                        "frac_of_tensor_peak": round(tf / tpk, 4), "peak_kind": kind, "flops_per_launch": flops,
+                        "kernel": "prefill_kernel<128,16> (tcgen05)"}}
 
 
 def main() -> None:
@@ -437,7 +476,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
-    ap.add_argument("--only", choices=["fp16", "int4"], help="time one kernel family alone (profiling)")
+    ap.add_argument("--only", choices=["fp16", "int4", "prefill"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

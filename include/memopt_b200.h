@@ -186,7 +186,7 @@ int memopt_paged_attention_f16(const void* query, const void* key_pool,
 /* No counterpart in the reference.  Same as memopt_paged_attention_f16, but
  * for callers that cannot allocate device memory at call time (hosts with
  * their own allocator-free runtime, or steps where allocator calls are not
- * allowed): the split-K scratch is a fixed 8 MiB array inside this library's
+ * allowed): the split-K scratch is a fixed 4 MiB array inside this library's
  * device image (held on every GPU that loads the library until exit), so the
  * call allocates nothing.  Calls needing more scratch than
  * memopt_paged_attention_noalloc_max_bytes() return MEMOPT_ERR_WORKSPACE.

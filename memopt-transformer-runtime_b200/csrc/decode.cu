@@ -21,6 +21,17 @@ int prefill_f16(const void* query, const void* kpool, const void* vpool, const i
                 cudaStream_t s);
 constexpr int kPrefillMinRows = 64;
 
+// One predicate for the workspace size and the dispatch: q_len >= 64 runs on
+// the tcgen05 prefill kernel (no split-K workspace); MEMOPT_DISABLE_PREFILL=1
+// forces the decode kernel (diagnostics).
+bool use_prefill(int q_len) {
+  static const bool disabled = [] {
+    const char* e = std::getenv("MEMOPT_DISABLE_PREFILL");
+    return e != nullptr && e[0] == '1';
+  }();
+  return q_len >= kPrefillMinRows && !disabled;
+}
+
 namespace {
 
 using decode::Cfg;
@@ -66,8 +77,9 @@ struct Split {
 };
 
 // Chooses the page-chunk size so that the item count fills every warp slot of
-// the machine several times over (the tail wave stays small) while each item
-// still streams <= 32 pages.
+// the machine several times over (the tail wave stays small).  A chunk may
+// span any number of pages (the kernel walks it in 32-page sub-windows), so
+// calls with many query rows need no split-K partials at all.
 Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window) {
   Split s;
   const int64_t wpages =
@@ -77,11 +89,9 @@ Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int wi
   const int64_t warp_slots = static_cast<int64_t>(sm_count()) * 2 * 4;
   const int64_t target = warp_slots * 4;
   int64_t n = (target + pairs - 1) / pairs;
-  const int min_chunks = (max_pages + 31) / 32;
   // Keep at least 4 pages per item so partials stay a small share of traffic.
   const int max_chunks = max_pages >= 4 ? max_pages / 4 : 1;
   if (n > max_chunks) n = max_chunks;
-  if (n < min_chunks) n = min_chunks;
   if (n < 1) n = 1;
   s.chunk_pages = static_cast<int>((max_pages + n - 1) / n);
   s.n_chunks = (max_pages + s.chunk_pages - 1) / s.chunk_pages;
@@ -232,7 +242,7 @@ extern "C" int memopt_paged_attention_f16(const void* query, const void* key_poo
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: pools must be 16-byte aligned");
   if (num_blocks * block_size > 0x7fffffffLL)
     return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: pool has more than 2^31 token rows");
-  if (q_len >= kPrefillMinRows && !std::getenv("MEMOPT_DISABLE_PREFILL"))
+  if (use_prefill(q_len))
     return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads, head_dim,
                        max_blocks_per_seq, num_blocks, block_size, p.window, out, as_stream(stream));
   alignas(64) CUtensorMap km, vm;

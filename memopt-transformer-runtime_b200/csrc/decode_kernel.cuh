@@ -43,7 +43,7 @@ struct Params {
   int64_t NB;
   int window;    // already clamped as in attention.cu:453-455
   float qscale;  // log2(e) / sqrt(D)
-  int chunk_pages;  // <= 32
+  int chunk_pages;  // pages per item (walked in 32-page sub-windows)
   int n_chunks;
   int64_t total_items;
 };
@@ -103,9 +103,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * C::NW;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * C::NW + wid;
 
-  // Decodes an item and ballots the valid pages of its chunk (warp-uniform).
-  auto load_item = [&](int64_t item, uint32_t& mask, int& phys_lane, int& h, int& c_lo,
-                       int& win_start, int& ctx) {
+  // Decodes an item and ballots the valid pages of sub-window `sub` (32 pages)
+  // of its chunk; `more` tells whether the chunk has pages beyond it.
+  auto load_item = [&](int64_t item, int sub, uint32_t& mask, int& phys_lane, int& h, int& c_lo,
+                       int& win_start, int& ctx, bool& more) {
     const int64_t pair = item / p.n_chunks;
     const int chunk = static_cast<int>(item - pair * p.n_chunks);
     h = static_cast<int>(pair % p.H);
@@ -115,8 +116,11 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     int p_hi = 0;
     if (ctx > 0) p_hi = min((ctx + BS - 1) / BS, p.MB);
     const int p_lo = win_start / BS;
-    c_lo = p_lo + chunk * p.chunk_pages;
-    const int c_hi = min(c_lo + p.chunk_pages, p_hi);
+    const int k_lo = p_lo + chunk * p.chunk_pages;
+    const int k_hi = min(k_lo + p.chunk_pages, p_hi);
+    c_lo = k_lo + 32 * sub;
+    const int c_hi = min(c_lo + 32, k_hi);
+    more = c_lo + 32 < k_hi;
     const int page = c_lo + lane;
     phys_lane = -1;
     if (page < c_hi) phys_lane = __ldg(p.bt + static_cast<int64_t>(b) * p.MB + page);
@@ -141,8 +145,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 
   // ---------------- producer cursor (warp-uniform) ----------------------
   int64_t p_item = first - nwarps;  // advanced before first use
+  int p_sub = 0;
+  bool p_more = false;
   uint32_t p_mask = 0;
-  int p_phys = -1;  // this lane's page entry for the producer's item
+  int p_phys = -1;  // this lane's page entry for the producer's window
   int p_h = 0;
   uint32_t p_seq = 0;
   bool p_done = false;
@@ -150,13 +156,18 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   // Issues the next page of the warp's page stream (if any).
   auto produce = [&]() {
     while (!p_done && p_mask == 0) {
-      p_item += nwarps;
-      if (p_item >= p.total_items) {
-        p_done = true;
-        break;
+      if (p_more) {
+        ++p_sub;
+      } else {
+        p_item += nwarps;
+        p_sub = 0;
+        if (p_item >= p.total_items) {
+          p_done = true;
+          break;
+        }
       }
       int c_lo, ws, cx;
-      load_item(p_item, p_mask, p_phys, p_h, c_lo, ws, cx);
+      load_item(p_item, p_sub, p_mask, p_phys, p_h, c_lo, ws, cx, p_more);
     }
     if (p_done) return;
     const int j = __ffs(p_mask) - 1;
@@ -182,7 +193,9 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   for (int64_t item = first; item < p.total_items && !failed; item += nwarps) {
     uint32_t mask;
     int phys_lane, h, c_lo, win_start, ctx;
-    load_item(item, mask, phys_lane, h, c_lo, win_start, ctx);
+    bool more;
+    int sub = 0;
+    load_item(item, 0, mask, phys_lane, h, c_lo, win_start, ctx, more);
     const int64_t pair = item / p.n_chunks;
 
     float q[8];
@@ -231,6 +244,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       return __all_sync(0xffffffffu, ready);
     };
 
+    for (;;) {  // 32-page sub-windows of the chunk
     if constexpr (!INT4) {
       while (mask != 0) {
         const int jpage = __ffs(mask) - 1;
@@ -464,6 +478,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           produce();
         }
       }
+    }
+    if (failed || !more) break;
+    ++sub;
+    load_item(item, sub, mask, phys_lane, h, c_lo, win_start, ctx, more);
     }
     if (failed) break;
 

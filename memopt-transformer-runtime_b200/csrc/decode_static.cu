@@ -9,7 +9,7 @@
 // the library's device image, so the call itself allocates nothing.
 //
 // Limits and rules (also stated in include/memopt_b200.h):
-//   * the scratch is kStaticScratchBytes (8 MiB) per device; every GPU on
+//   * the scratch is kStaticScratchBytes (4 MiB) per device; every GPU on
 //     which the library is loaded holds it until the process exits;
 //   * a call whose split-K scratch would exceed it is rejected with
 //     MEMOPT_ERR_WORKSPACE before any work is queued;
@@ -27,7 +27,7 @@
 namespace memopt {
 namespace {
 
-constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
 
 static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
 

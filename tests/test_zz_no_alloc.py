@@ -65,7 +65,8 @@ def test_noalloc_rejects_oversized_calls():
     lib = capi.lib()
     lib.memopt_paged_attention_noalloc_max_bytes.restype = C.c_size_t
     cap = lib.memopt_paged_attention_noalloc_max_bytes()
-    B, H, D, BS, MB = 64, 32, 128, 16, 256
+    # ~4700 (sequence, head) rows split in two chunks need ~4.9 MB of partials.
+    B, H, D, BS, MB = 47, 100, 128, 16, 64
     need = lib.memopt_paged_attention_workspace_size(B, 1, H, D, MB, BS, MB * BS, MB * BS)
     assert need > cap
     q = torch.zeros(B, 1, H, D, dtype=torch.float16, device="cuda")
