@@ -50,14 +50,14 @@ constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 B (one 64-wide half)
 template <int D, int BS>
 struct Cfg {
   static constexpr int HALVES = D / 64;
-  static constexpr int PPB = 128 / BS;  // pages per 128-token block
+  static constexpr int PPB = 128 / BS;                 // pages per 128-token block
+  static constexpr int TILE = HALVES * kTileBytes;     // one 128-row tile (Q, K or V)
   static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = HALVES * kTileBytes;
-  static constexpr int K_BYTES = HALVES * kTileBytes;
-  static constexpr int BUF = 2 * K_BYTES;  // K then V
-  static constexpr int P_OFF = KV_OFF + 2 * BUF;
+  static constexpr int K_OFF = TILE;                   // K ring: 2 tiles
+  static constexpr int V_OFF = K_OFF + 2 * TILE;       // V ring: 3 tiles
+  static constexpr int P_OFF = V_OFF + 3 * TILE;       // P: 128 rows x 128 tokens fp16
   static constexpr int SMEM = P_OFF + 2 * kTileBytes + 1024;  // + alignment slack
-  static constexpr uint32_t PAGE_TX = 2u * HALVES * BS * 128u;  // K+V bytes of one page
+  static constexpr uint32_t PAGE_TX = 1u * HALVES * BS * 128u;  // bytes of one page of K (or V)
   static constexpr uint32_t IDESC_S = tc::idesc_f16(128, 128, false, false);
   static constexpr uint32_t IDESC_PV = tc::idesc_f16(128, D, false, true);
 };
@@ -70,16 +70,22 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
   return true;
 }
 
+// Warp-specialised: warps 0-3 own one query row each per thread (softmax,
+// rescale, P, epilogue); warp 4 stages Q/K/V with TMA and issues the MMAs.
+// Barriers: 0 = Q, 1..2 = K ring, 3..5 = V ring, 6 = S(j) done (commit),
+// 7 = P.V(j) done (commit), 8 = S(j) read out of TMEM (4 arrivals, one per
+// softmax warp), 9 = P(j) written and O rescaled (4 arrivals).
+constexpr int kThreads = 160;
+
 template <int D, int BS>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap qmap,
                const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                int32_t* __restrict__ err) {
   using C = Cfg<D, BS>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[5];  // q, kv0, kv1, s, o
+  __shared__ __align__(8) uint64_t bars[10];
   __shared__ uint32_t tmem_slot;
-  __shared__ uint32_t page_mask[2];
   __shared__ int fail_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -87,7 +93,9 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(base);
   const uint32_t sQ = sbase + C::Q_OFF, sP = sbase + C::P_OFF;
-  const uint32_t bar_q = smem_u32(&bars[0]), bar_s = smem_u32(&bars[3]), bar_o = smem_u32(&bars[4]);
+  auto bar_at = [&](int i) { return smem_u32(&bars[i]); };
+  const uint32_t bar_q = bar_at(0), bar_s = bar_at(6), bar_o = bar_at(7), bar_sfree = bar_at(8),
+                 bar_pready = bar_at(9);
 
   const int ctx = __ldg(p.ctx + b);
   const int ws = (p.window < ctx) ? (ctx - p.window) : 0;
@@ -96,11 +104,10 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   const int nblocks = p_hi > p_lo ? (p_hi - p_lo + C::PPB - 1) / C::PPB : 0;
 
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 8; ++i) mbar_init(bar_at(i), 1);
+    mbar_init(bar_sfree, 4);
+    mbar_init(bar_pready, 4);
     fence_mbar_init();
-    prefetch_tensormap(&qmap);
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
     fail_flag = 0;
   }
   if (warp == 0) {
@@ -112,178 +119,62 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 128;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
-  // Warp 0: stage the pages of block j into buffer j & 1 (zero-filling the
-  // skipped ones) and publish the page-validity mask.
-  auto issue_block = [&](int j) {
-    const int buf = j & 1;
-    const uint32_t bar = smem_u32(&bars[1 + buf]);
-    const uint32_t sK = sbase + C::KV_OFF + buf * C::BUF, sV = sK + C::K_BYTES;
+  // Validity of the pages of block j, one bit per page (warp-collective).
+  auto page_bits = [&](int j, int& phys) -> uint32_t {
     const int page = p_lo + j * C::PPB + lane;
-    int phys = -1;
+    phys = -1;
     if (lane < C::PPB && page < p_hi) phys = __ldg(p.bt + static_cast<int64_t>(b) * p.MB + page);
     const bool ok = lane < C::PPB && page < p_hi && phys >= 0 && static_cast<int64_t>(phys) < p.NB;
-    const uint32_t mask = __ballot_sync(0xffffffffu, ok);
-    // Zero the smem of skipped pages (lanes stride over 16-byte chunks).
-    const uint32_t bad = ~mask & ((1u << C::PPB) - 1u);
-    if (bad != 0) {
-      for (int pg = 0; pg < C::PPB; ++pg) {
-        if (!((bad >> pg) & 1u)) continue;
-        for (int hh = 0; hh < C::HALVES; ++hh) {
-          uint8_t* kdst = base + C::KV_OFF + buf * C::BUF + hh * kTileBytes + pg * BS * 128;
-          uint8_t* vdst = kdst + C::K_BYTES;
-          for (int c = lane; c < BS * 8; c += 32) {
-            reinterpret_cast<uint4*>(kdst)[c] = make_uint4(0, 0, 0, 0);
-            reinterpret_cast<uint4*>(vdst)[c] = make_uint4(0, 0, 0, 0);
-          }
-        }
-      }
-      fence_proxy_async_smem();
-    }
-    __syncwarp();
-    if (lane == 0) {
-      page_mask[buf] = mask;
-      mbar_arrive_expect_tx(bar, __popc(mask) * C::PAGE_TX);
-    }
-    __syncwarp();  // the transaction count is armed before any copy can land
-    if (ok) {  // each valid page's lane issues its own copies
-      for (int hh = 0; hh < C::HALVES; ++hh) {
-        const uint32_t off = hh * kTileBytes + lane * BS * 128;
-        tma_load_3d(sK + off, &kmap, hh * 64, h, phys * BS, bar);
-        tma_load_3d(sV + off, &vmap, hh * 64, h, phys * BS, bar);
-      }
-    }
+    return __ballot_sync(0xffffffffu, ok);
   };
 
-  if (nblocks > 0) {
-    if (warp == 0) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar_q, C::HALVES * kTileBytes);
-        for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sQ + hh * kTileBytes, &qmap, hh * 64, h, b * p.QL + qt * 128, bar_q);
-      }
-      issue_block(0);
-      if (nblocks > 1) issue_block(1);
+  if (warp == 4) {
+    // =========================== producer warp ===========================
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
     }
-    __syncthreads();
-  }
-
-  float m_run = -INFINITY, l_run = 0.f;
-  bool failed = false;
-  for (int j = 0; j < nblocks && !failed; ++j) {
-    const int buf = j & 1;
-    const uint32_t sK = sbase + C::KV_OFF + buf * C::BUF, sV = sK + C::K_BYTES;
-    // ---- S = Q K^T --------------------------------------------------------
-    if (tid == 0) {
-      bool ok = true;
-      if (j == 0) ok = wait_bar(bar_q, 0);
-      ok = ok && wait_bar(smem_u32(&bars[1 + buf]), (j >> 1) & 1);
-      if (!ok) {
-        fail_flag = 1;
-      } else {
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / 4) * kTileBytes + (kk % 4) * 32;
-          tc::mma_f16(tS, tc::sdesc_sw128(sQ + off, 16, 1024), tc::sdesc_sw128(sK + off, 16, 1024), C::IDESC_S,
-                      kk > 0);
+    // Stage the K (is_v = false) or V pages of block j, zero-filling skipped pages.
+    auto stage = [&](int j, bool is_v) {
+      const int slot = is_v ? (j % 3) : (j & 1);
+      const uint32_t bar = is_v ? bar_at(3 + slot) : bar_at(1 + slot);
+      const int off = (is_v ? C::V_OFF : C::K_OFF) + slot * C::TILE;
+      int phys;
+      const uint32_t mask = page_bits(j, phys);
+      const uint32_t bad = ~mask & ((1u << C::PPB) - 1u);
+      if (bad != 0) {
+        for (int pg = 0; pg < C::PPB; ++pg) {
+          if (!((bad >> pg) & 1u)) continue;
+          for (int hh = 0; hh < C::HALVES; ++hh) {
+            uint4* dst = reinterpret_cast<uint4*>(base + off + hh * kTileBytes + pg * BS * 128);
+            for (int c = lane; c < BS * 8; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
+          }
         }
-        tc::commit(bar_s);
+        fence_proxy_async_smem();
       }
-    }
-    __syncthreads();
-    if (fail_flag) {
-      failed = true;
-      break;
-    }
-    if (!wait_bar(bar_s, j & 1)) {
-      failed = true;
-      fail_flag = 1;
-    }
-    tc::fence_after_sync();
-    // ---- softmax of this thread's row ----------------------------------------
-    float s[128];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tc::ld32(tS + lane_base + c * 32, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-    }
-    tc::wait_ld();
-    const uint32_t mask = page_mask[buf];
-    const int tok0 = (p_lo + j * C::PPB) * BS;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 128; ++i) {
-      const int t = tok0 + i;
-      const bool valid = ((mask >> (i / BS)) & 1u) && t >= ws && t < ctx;
-      s[i] = valid ? s[i] * p.qscale : -INFINITY;
-      mx = fmaxf(mx, s[i]);
-    }
-    const float m_new = fmaxf(m_run, mx);
-    float m_use = m_run, alpha = 1.f;
-    bool rescale = false;
-    if (m_run == -INFINITY) {
-      m_use = m_new;  // nothing accumulated yet (all earlier p were 0)
-    } else if (m_new > m_run + 8.f) {
-      m_use = m_new;
-      alpha = tc::ex2(m_run - m_new);
-      rescale = true;
-    }
-    float psum = 0.f;
-    uint32_t ph[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float p0 = (m_use == -INFINITY) ? 0.f : tc::ex2(s[2 * i] - m_use);
-      const float p1 = (m_use == -INFINITY) ? 0.f : tc::ex2(s[2 * i + 1] - m_use);
-      psum += p0 + p1;
-      const __half2 hv = __floats2half2_rn(p0, p1);
-      ph[i] = *reinterpret_cast<const uint32_t*>(&hv);
-    }
-    l_run = l_run * alpha + psum;
-    m_run = m_use;
-    // PV(j-1) must have finished before P and the O rows are touched and
-    // before its K/V buffer is refilled.
-    if (j > 0 && !wait_bar(bar_o, (j - 1) & 1)) {
-      failed = true;
-      fail_flag = 1;
-    }
-    tc::fence_after_sync();
-    if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tc::ld32(tO + lane_base + c * 32, v);
-        tc::wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= alpha;
-        tc::st32(tO + lane_base + c * 32, v);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(bar, __popc(mask) * C::PAGE_TX);
+      __syncwarp();  // the transaction count is armed before any copy can land
+      if ((mask >> lane) & 1u) {
+        for (int hh = 0; hh < C::HALVES; ++hh)
+          tma_load_3d(sbase + off + hh * kTileBytes + lane * BS * 128, is_v ? &vmap : &kmap, hh * 64, h,
+                      phys * BS, bar);
       }
-      tc::wait_st();
-    }
-    if (warp == 0 && j >= 1 && j + 1 < nblocks) issue_block(j + 1);
-    // P row -> smem, K-major with 128-byte swizzle (two 64-token halves).
-    {
-      const int row = tid;
+    };
+    auto issue_s = [&](int j) {
+      const uint32_t sK = sbase + C::K_OFF + (j & 1) * C::TILE;
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        const int half = c16 / 8, chunk = c16 % 8;
-        uint8_t* dst = base + C::P_OFF + half * kTileBytes + row * 128 + ((chunk ^ (row & 7)) * 16);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(ph[4 * c16], ph[4 * c16 + 1], ph[4 * c16 + 2], ph[4 * c16 + 3]);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / 4) * kTileBytes + (kk % 4) * 32;
+        tc::mma_f16(tS, tc::sdesc_sw128(sQ + off, 16, 1024), tc::sdesc_sw128(sK + off, 16, 1024), C::IDESC_S,
+                    kk > 0);
       }
-    }
-    fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (fail_flag) {
-      failed = true;
-      break;
-    }
-    // ---- O += P V -------------------------------------------------------------
-    if (tid == 0) {
-      tc::fence_after_sync();
+      tc::commit(bar_s);
+    };
+    auto issue_pv = [&](int j) {
+      const uint32_t sV = sbase + C::V_OFF + (j % 3) * C::TILE;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
@@ -291,41 +182,183 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
                     C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
       }
       tc::commit(bar_o);
-    }
-  }
-
-  // ---- epilogue ------------------------------------------------------------------
-  const int qi = qt * 128 + tid;
-  __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D;
-  if (nblocks > 0 && !failed) {
-    if (!wait_bar(bar_o, (nblocks - 1) & 1)) failed = true;
-    tc::fence_after_sync();
-  }
-  if (nblocks > 0 && !failed) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float v[32];
-      tc::ld32(tO + lane_base + c * 32, v);
-      tc::wait_ld();
-      if (qi < p.QL) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 u;
-          __half2* h2 = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(v[8 * k + 2 * e] * inv, v[8 * k + 2 * e + 1] * inv);
-          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * k) = u;
+    };
+    bool ok = true;
+    if (nblocks > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_q, C::TILE);
+        for (int hh = 0; hh < C::HALVES; ++hh)
+          tma_load_3d(sQ + hh * kTileBytes, &qmap, hh * 64, h, b * p.QL + qt * 128, bar_q);
+      }
+      stage(0, false);
+      stage(0, true);
+      if (nblocks > 1) {
+        stage(1, false);
+        stage(1, true);
+      }
+      if (nblocks > 2) stage(2, true);
+      if (lane == 0) {
+        ok = wait_bar(bar_q, 0) && wait_bar(bar_at(1), 0);
+        if (ok) {
+          tc::fence_after_sync();
+          issue_s(0);
         }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
-  } else if (qi < p.QL) {
-    // No visible token (or a failed wait): zero row, as attention.cu:334 does for l == 0.
-    for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < nblocks && ok; ++j) {
+      if (j + 1 < nblocks) {
+        // S(j+1) needs S(j) read out of TMEM and K(j+1) staged.
+        if (lane == 0) {
+          ok = wait_bar(bar_sfree, j & 1) && wait_bar(bar_at(1 + ((j + 1) & 1)), ((j + 1) >> 1) & 1);
+          if (ok) {
+            tc::fence_after_sync();
+            issue_s(j + 1);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (j + 2 < nblocks) stage(j + 2, false);  // S(j) has completed: K slot j & 1 is free
+      }
+      // P.V(j) needs P(j) written (which implies P.V(j-1) completed) and V(j) staged.
+      if (lane == 0) {
+        ok = wait_bar(bar_pready, j & 1) && wait_bar(bar_at(3 + j % 3), (j / 3) & 1);
+        if (ok) {
+          tc::fence_after_sync();
+          issue_pv(j);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (j >= 1 && j + 2 < nblocks) stage(j + 2, true);  // P.V(j-1) done: V slot (j-1)%3 is free
+    }
+    if (!ok && lane == 0) fail_flag = 1;
+  } else {
+    // =========================== softmax warps ===========================
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblocks && ok; ++j) {
+      ok = wait_bar(bar_s, j & 1);
+      tc::fence_after_sync();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc::ld32(tS + lane_base + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+      }
+      tc::wait_ld();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree);
+      ok = __all_sync(0xffffffffu, ok);
+      int phys_unused;
+      const uint32_t mask = page_bits(j, phys_unused);
+      const int tok0 = (p_lo + j * C::PPB) * BS;
+      const bool edge = mask != ((1u << C::PPB) - 1u) || tok0 < ws || tok0 + 128 > ctx;
+      float mx = -INFINITY;
+      if (edge) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const int t = tok0 + i;
+          const bool valid = ((mask >> (i / BS)) & 1u) && t >= ws && t < ctx;
+          s[i] = valid ? s[i] * p.qscale : -INFINITY;
+          mx = fmaxf(mx, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          s[i] *= p.qscale;
+          mx = fmaxf(mx, s[i]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      float m_use = m_run, alpha = 1.f;
+      bool rescale = false;
+      if (m_run == -INFINITY) {
+        m_use = m_new;  // nothing accumulated yet (all earlier p were 0)
+      } else if (m_new > m_run + 8.f) {
+        m_use = m_new;
+        alpha = tc::ex2(m_run - m_new);
+        rescale = true;
+      }
+      const float msub = (m_use == -INFINITY) ? 0.f : m_use;  // all-masked rows: every p = ex2(-inf) = 0
+      float psum = 0.f;
+      uint32_t ph[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = tc::ex2(s[2 * i] - msub);
+        const float p1 = tc::ex2(s[2 * i + 1] - msub);
+        psum += p0 + p1;
+        const __half2 hv = __floats2half2_rn(p0, p1);
+        ph[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      l_run = l_run * alpha + psum;
+      m_run = m_use;
+      // P.V(j-1) must be done before P and the O rows are touched.
+      if (j > 0) ok = ok && wait_bar(bar_o, (j - 1) & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      tc::fence_after_sync();
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tc::ld32(tO + lane_base + c * 32, v);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tc::st32(tO + lane_base + c * 32, v);
+        }
+        tc::wait_st();
+      }
+      // P row -> smem, K-major with 128-byte swizzle (two 64-token halves).
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        const int half = c16 / 8, chunk = c16 % 8;
+        uint8_t* dst = base + C::P_OFF + half * kTileBytes + tid * 128 + ((chunk ^ (tid & 7)) * 16);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(ph[4 * c16], ph[4 * c16 + 1], ph[4 * c16 + 2], ph[4 * c16 + 3]);
+      }
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_pready);
+    }
+    // ---- epilogue ------------------------------------------------------------
+    const int qi = qt * 128 + tid;
+    __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D;
+    if (nblocks > 0 && ok) ok = wait_bar(bar_o, (nblocks - 1) & 1);
+    ok = __all_sync(0xffffffffu, ok);
+    tc::fence_after_sync();
+    if (nblocks > 0 && ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tc::ld32(tO + lane_base + c * 32, v);
+        tc::wait_ld();
+        if (qi < p.QL) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint4 u;
+            __half2* h2 = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              h2[e] = __floats2half2_rn(v[8 * k + 2 * e] * inv, v[8 * k + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * k) = u;
+          }
+        }
+      }
+    } else if (qi < p.QL) {
+      // No visible token (or a failed wait): zero row, as attention.cu:334 does for l == 0.
+      for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
+    }
+    if (!ok && lane == 0) fail_flag = 1;
   }
-  if (failed && tid == 0 && err) atomicExch(err, 2);
   tc::fence_before_sync();
   __syncthreads();
+  if (fail_flag && tid == 0 && err) atomicExch(err, 2);
   if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
@@ -378,7 +411,7 @@ int launch_prefill(const prefill::Params& p, const void* query, const void* kpoo
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
   const dim3 grid((p.QL + 127) / 128, p.H, p.B);
-  kern<<<grid, 128, C::SMEM, s>>>(p, qm, km, vm, nullptr);
+  kern<<<grid, prefill::kThreads, C::SMEM, s>>>(p, qm, km, vm, nullptr);
   MEMOPT_LAUNCH_CHECK("prefill_kernel launch");
   return MEMOPT_OK;
 }
