@@ -46,6 +46,7 @@ struct Params {
 };
 
 constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 B (one 64-wide half)
+constexpr int kBtCache = 4096;         // block-table entries cached in smem per CTA
 
 template <int D, int BS>
 struct Cfg {
@@ -54,9 +55,10 @@ struct Cfg {
   static constexpr int TILE = HALVES * kTileBytes;     // one 128-row tile (Q, K or V)
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = TILE;                   // K ring: 2 tiles
-  static constexpr int V_OFF = K_OFF + 2 * TILE;       // V ring: 3 tiles
-  static constexpr int P_OFF = V_OFF + 3 * TILE;       // P: 128 rows x 128 tokens fp16
-  static constexpr int SMEM = P_OFF + 2 * kTileBytes + 1024;  // + alignment slack
+  static constexpr int V_OFF = K_OFF + 2 * TILE;       // V ring: 2 tiles
+  static constexpr int P_OFF = V_OFF + 2 * TILE;       // P: 128 rows x 128 tokens fp16
+  static constexpr int BT_OFF = P_OFF + 2 * kTileBytes;  // block-table window (kBtCache entries)
+  static constexpr int SMEM = BT_OFF + 4 * 4096 + 1024;     // + alignment slack
   static constexpr uint32_t PAGE_TX = 1u * HALVES * BS * 128u;  // bytes of one page of K (or V)
   static constexpr uint32_t IDESC_S = tc::idesc_f16(128, 128, false, false);
   static constexpr uint32_t IDESC_PV = tc::idesc_f16(128, D, false, true);
@@ -70,12 +72,14 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
   return true;
 }
 
-// Warp-specialised: warps 0-3 own one query row each per thread (softmax,
-// rescale, P, epilogue); warp 4 stages Q/K/V with TMA and issues the MMAs.
-// Barriers: 0 = Q, 1..2 = K ring, 3..5 = V ring, 6 = S(j) done (commit),
-// 7 = P.V(j) done (commit), 8 = S(j) read out of TMEM (4 arrivals, one per
-// softmax warp), 9 = P(j) written and O rescaled (4 arrivals).
-constexpr int kThreads = 160;
+// Warp-specialised: warps 0-7 run the softmax, two threads per query row
+// (warp w handles row 32*(w%4)+lane, score columns [64*(w/4), +64) and O
+// columns [(D/2)*(w/4), +D/2)); warp 8 stages Q/K/V with TMA and issues the
+// MMAs.  Barriers: 0 = Q, 1..2 = K ring, 3..4 = V ring, 6 = S(j) done
+// (commit), 7 = P.V(j) done (commit), 8 = S(j) read out of TMEM (8 arrivals,
+// one per softmax warp), 9 = P(j) written and O rescaled (8 arrivals).
+constexpr int kThreads = 288;
+constexpr int kSoftmaxWarps = 8;
 
 template <int D, int BS>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -87,6 +91,8 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   __shared__ __align__(8) uint64_t bars[10];
   __shared__ uint32_t tmem_slot;
   __shared__ int fail_flag;
+  __shared__ float red_max[2][2][128];  // [block parity][half][row]
+  __shared__ float red_sum[2][128];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -105,8 +111,8 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
 
   if (tid == 0) {
     for (int i = 0; i < 8; ++i) mbar_init(bar_at(i), 1);
-    mbar_init(bar_sfree, 4);
-    mbar_init(bar_pready, 4);
+    mbar_init(bar_sfree, kSoftmaxWarps);
+    mbar_init(bar_pready, kSoftmaxWarps);
     fence_mbar_init();
     fail_flag = 0;
   }
@@ -120,16 +126,27 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   const uint32_t tmem = tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 128;
 
+  // The pages of this sequence's window are read once into smem (when they
+  // fit), so per-block validity checks never wait on global memory.
+  int32_t* s_bt = reinterpret_cast<int32_t*>(base + C::BT_OFF);
+  const int npages = p_hi > p_lo ? p_hi - p_lo : 0;
+  const bool bt_cached = npages <= kBtCache;
+  if (bt_cached) {
+    for (int i = tid; i < npages; i += kThreads) s_bt[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.MB + p_lo + i);
+  }
+  __syncthreads();
+
   // Validity of the pages of block j, one bit per page (warp-collective).
   auto page_bits = [&](int j, int& phys) -> uint32_t {
     const int page = p_lo + j * C::PPB + lane;
     phys = -1;
-    if (lane < C::PPB && page < p_hi) phys = __ldg(p.bt + static_cast<int64_t>(b) * p.MB + page);
+    if (lane < C::PPB && page < p_hi)
+      phys = bt_cached ? s_bt[page - p_lo] : __ldg(p.bt + static_cast<int64_t>(b) * p.MB + page);
     const bool ok = lane < C::PPB && page < p_hi && phys >= 0 && static_cast<int64_t>(phys) < p.NB;
     return __ballot_sync(0xffffffffu, ok);
   };
 
-  if (warp == 4) {
+  if (warp == kSoftmaxWarps) {
     // =========================== producer warp ===========================
     if (lane == 0) {
       prefetch_tensormap(&qmap);
@@ -138,7 +155,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     }
     // Stage the K (is_v = false) or V pages of block j, zero-filling skipped pages.
     auto stage = [&](int j, bool is_v) {
-      const int slot = is_v ? (j % 3) : (j & 1);
+      const int slot = j & 1;
       const uint32_t bar = is_v ? bar_at(3 + slot) : bar_at(1 + slot);
       const int off = (is_v ? C::V_OFF : C::K_OFF) + slot * C::TILE;
       int phys;
@@ -174,7 +191,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       tc::commit(bar_s);
     };
     auto issue_pv = [&](int j) {
-      const uint32_t sV = sbase + C::V_OFF + (j % 3) * C::TILE;
+      const uint32_t sV = sbase + C::V_OFF + (j & 1) * C::TILE;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
@@ -196,7 +213,6 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         stage(1, false);
         stage(1, true);
       }
-      if (nblocks > 2) stage(2, true);
       if (lane == 0) {
         ok = wait_bar(bar_q, 0) && wait_bar(bar_at(1), 0);
         if (ok) {
@@ -222,7 +238,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
       // P.V(j) needs P(j) written (which implies P.V(j-1) completed) and V(j) staged.
       if (lane == 0) {
-        ok = wait_bar(bar_pready, j & 1) && wait_bar(bar_at(3 + j % 3), (j / 3) & 1);
+        ok = wait_bar(bar_pready, j & 1) && wait_bar(bar_at(3 + (j & 1)), (j >> 1) & 1);
         if (ok) {
           tc::fence_after_sync();
           issue_pv(j);
@@ -230,22 +246,28 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
-      if (j >= 1 && j + 2 < nblocks) stage(j + 2, true);  // P.V(j-1) done: V slot (j-1)%3 is free
+      // P(j) ready implies P.V(j-1) completed: V slot (j+1)&1 is free for block j+1.
+      if (j >= 1 && j + 1 < nblocks) stage(j + 1, true);
     }
     if (!ok && lane == 0) fail_flag = 1;
   } else {
     // =========================== softmax warps ===========================
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int row = (warp & 3) * 32 + lane;  // query row = TMEM lane
+    const int hf = warp >> 2;                // which half of the columns
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    auto sync_softmax = [] { asm volatile("bar.sync 1, 256;" ::: "memory"); };
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblocks && ok; ++j) {
+    // Every softmax thread runs the same number of iterations (named barrier
+    // below); failures are published in fail_flag and read after the barrier.
+    for (int j = 0; j < nblocks; ++j) {
       ok = wait_bar(bar_s, j & 1);
       tc::fence_after_sync();
-      float s[128];
+      float s[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v[32];
-        tc::ld32(tS + lane_base + c * 32, v);
+        tc::ld32(tS + lane_base + hf * 64 + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
       }
@@ -256,24 +278,34 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       ok = __all_sync(0xffffffffu, ok);
       int phys_unused;
       const uint32_t mask = page_bits(j, phys_unused);
-      const int tok0 = (p_lo + j * C::PPB) * BS;
-      const bool edge = mask != ((1u << C::PPB) - 1u) || tok0 < ws || tok0 + 128 > ctx;
+      const int tok0 = (p_lo + j * C::PPB) * BS + hf * 64;
+      const uint32_t hmask = (mask >> (hf * 64 / BS)) & ((1u << (64 / BS)) - 1u);
+      const bool edge = hmask != ((1u << (64 / BS)) - 1u) || tok0 < ws || tok0 + 64 > ctx;
       float mx = -INFINITY;
       if (edge) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 64; ++i) {
           const int t = tok0 + i;
-          const bool valid = ((mask >> (i / BS)) & 1u) && t >= ws && t < ctx;
+          const bool valid = ((hmask >> (i / BS)) & 1u) && t >= ws && t < ctx;
           s[i] = valid ? s[i] * p.qscale : -INFINITY;
           mx = fmaxf(mx, s[i]);
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 64; ++i) {
           s[i] *= p.qscale;
           mx = fmaxf(mx, s[i]);
         }
       }
+      // Row max over both halves (the two threads of a row reach the same decision).
+      red_max[j & 1][hf][row] = mx;
+      if (!ok) fail_flag = 1;
+      sync_softmax();
+      if (fail_flag) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(red_max[j & 1][0][row], red_max[j & 1][1][row]);
       const float m_new = fmaxf(m_run, mx);
       float m_use = m_run, alpha = 1.f;
       bool rescale = false;
@@ -286,39 +318,39 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
       const float msub = (m_use == -INFINITY) ? 0.f : m_use;  // all-masked rows: every p = ex2(-inf) = 0
       float psum = 0.f;
-      uint32_t ph[64];
+      uint32_t ph[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = tc::ex2(s[2 * i] - msub);
         const float p1 = tc::ex2(s[2 * i + 1] - msub);
         psum += p0 + p1;
         const __half2 hv = __floats2half2_rn(p0, p1);
         ph[i] = *reinterpret_cast<const uint32_t*>(&hv);
       }
-      l_run = l_run * alpha + psum;
+      l_run = l_run * alpha + psum;  // partial row sum of this half
       m_run = m_use;
       // P.V(j-1) must be done before P and the O rows are touched.
-      if (j > 0) ok = ok && wait_bar(bar_o, (j - 1) & 1);
-      ok = __all_sync(0xffffffffu, ok);
+      if (j > 0 && !wait_bar(bar_o, (j - 1) & 1)) fail_flag = 1;  // seen at the next barrier
       tc::fence_after_sync();
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           float v[32];
-          tc::ld32(tO + lane_base + c * 32, v);
+          const uint32_t col = tO + lane_base + hf * (D / 2) + c * 32;
+          tc::ld32(col, v);
           tc::wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tc::st32(tO + lane_base + c * 32, v);
+          tc::st32(col, v);
         }
         tc::wait_st();
       }
-      // P row -> smem, K-major with 128-byte swizzle (two 64-token halves).
+      // This half's 64 P values -> smem half hf, K-major with 128-byte swizzle.
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        const int half = c16 / 8, chunk = c16 % 8;
-        uint8_t* dst = base + C::P_OFF + half * kTileBytes + tid * 128 + ((chunk ^ (tid & 7)) * 16);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(ph[4 * c16], ph[4 * c16 + 1], ph[4 * c16 + 2], ph[4 * c16 + 3]);
+      for (int chunk = 0; chunk < 8; ++chunk) {
+        uint8_t* dst = base + C::P_OFF + hf * kTileBytes + row * 128 + ((chunk ^ (row & 7)) * 16);
+        *reinterpret_cast<uint4*>(dst) =
+            make_uint4(ph[4 * chunk], ph[4 * chunk + 1], ph[4 * chunk + 2], ph[4 * chunk + 3]);
       }
       fence_proxy_async_smem();
       tc::fence_before_sync();
@@ -326,17 +358,21 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       if (lane == 0) mbar_arrive(bar_pready);
     }
     // ---- epilogue ------------------------------------------------------------
-    const int qi = qt * 128 + tid;
-    __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D;
+    red_sum[hf][row] = l_run;
+    sync_softmax();
+    ok = ok && !fail_flag;
+    const float l_tot = red_sum[0][row] + red_sum[1][row];
+    const int qi = qt * 128 + row;
+    __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D + hf * (D / 2);
     if (nblocks > 0 && ok) ok = wait_bar(bar_o, (nblocks - 1) & 1);
     ok = __all_sync(0xffffffffu, ok);
     tc::fence_after_sync();
     if (nblocks > 0 && ok) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
         float v[32];
-        tc::ld32(tO + lane_base + c * 32, v);
+        tc::ld32(tO + lane_base + hf * (D / 2) + c * 32, v);
         tc::wait_ld();
         if (qi < p.QL) {
 #pragma unroll
@@ -352,7 +388,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
     } else if (qi < p.QL) {
       // No visible token (or a failed wait): zero row, as attention.cu:334 does for l == 0.
-      for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
     }
     if (!ok && lane == 0) fail_flag = 1;
   }
