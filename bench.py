@@ -309,6 +309,7 @@ def run_ours(args) -> None:
     if not args.no_int4:
         extra = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)
         extra.update(prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
+        extra.update(evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
 
     # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
     cpu = None
@@ -425,6 +426,8 @@ def run_only(args) -> None:
         ms = time_loop(torch, lambda: _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, CTX, CTX, wsp, wsb, sp),
                        args.steps, args.warmup, lambda: None, stream)
         res = {"kernel": "paged_decode f16 cfg2", "ms": ms, "GB/s": step_bytes(B, CTX) / ms / 1e6}
+    elif args.only == "evict":
+        res = evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "prefill":
         res = prefill_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     else:
@@ -468,6 +471,58 @@ def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, 
                         "kernel": "prefill_kernel<128,16> (tcgen05)"}}
 
 
+def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """Ada-KV eviction (8 sequences x 32 heads x 32768
+    tokens, lognormal(0,1) scores, 4 sinks, retain 0.75, with compaction of
+    the kept indices) followed by block-skipping decode with window 4096."""
+    eb, ectx, win = 8, 32768, 4096
+    mb = ectx // BS
+    nb = eb * mb
+    memopt_C.init_pool(nb, BS, H, D)
+    kp, vp = memopt_C.get_pool_tensors()
+    g = torch.Generator(device=dev).manual_seed(21 + rank)
+    kp.normal_(generator=g)
+    vp.normal_(generator=g)
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(3 + rank))[: eb * mb].reshape(eb, mb)
+    bt = bt.to(torch.int32).to(dev)
+    scores = torch.empty(eb, H, ectx, device=dev).log_normal_(0.0, 1.0, generator=g)
+    ibf = torch.zeros(nb, dtype=torch.int32, device=dev)
+
+    idx_buf = torch.empty(eb, H, ectx, dtype=torch.int32, device=dev)
+    cnt_buf = torch.empty(eb, H, dtype=torch.int32, device=dev)
+
+    def evict():  # the kernel through the C-ABI, outputs preallocated
+        _capi.evict_tokens(scores, bt, ibf, kp, vp, 0.75, 4, idx_buf, cnt_buf, sp)
+
+    ev_steps = max(3, min(args.steps, 50))
+    ms_ev = max_over_ranks(time_loop(torch, evict, ev_steps, args.warmup, barrier, stream))
+    idx, cnt = memopt_C.evict_tokens(scores, bt, ibf, 0.75, 4, return_retained=True)
+    kept = float(cnt.float().mean().item()) / ectx
+    ev_bytes = 2 * eb * H * ectx * 4  # scores read + kept-index list written (no row is evicted with sinks)
+    q = torch.randn(eb, 1, H, D, dtype=torch.float16, device=dev, generator=g)
+    ctx = torch.full((eb,), ectx, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    wsb = _capi.workspace_size(eb, 1, H, D, mb, BS, ectx, win)
+    wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+    def step():
+        _capi.paged_attention_f16(q, kp, vp, bt, ctx, out, ectx, win, wsp, wsb, sp)
+
+    ms = max_over_ranks(time_loop(torch, step, max(args.steps, 20), args.warmup, barrier, stream))
+    dbytes = 2 * eb * win * H * D * 2 + 2 * eb * H * D * 2 + eb * (win // BS + 1) * 4
+    peak, _ = peaks()
+    return {"evict_tokens": {"workload": "BASELINE configs[3]: 8 x 32 heads x 32768 tokens, lognormal(0,1), "
+                                         "4 sinks, retain 0.75, kept indices compacted",
+                             "value": round(ev_bytes * ws_n / (ms_ev * 1e-3) / 1e9, 2), "unit": "GB/s",
+                             "ms_per_call": round(ms_ev, 5), "kept_fraction": round(kept, 4),
+                             "note": "reference semantics: with sinks the 32-step bisection keeps every token"},
+            "window_decode": {"workload": "BASELINE configs[3]: decode batch 8, ctx 32768, window 4096",
+                              "value": round(dbytes * ws_n / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                              "ms_per_step": round(ms, 5),
+                              "frac_of_hbm_peak": round(dbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                              "decode_tokens_per_s": round(eb * ws_n / (ms * 1e-3), 1)}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -476,7 +531,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
-    ap.add_argument("--only", choices=["fp16", "int4", "prefill"], help="time one kernel family alone (profiling)")
+    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

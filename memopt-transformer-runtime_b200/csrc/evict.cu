@@ -27,9 +27,9 @@
 namespace memopt {
 namespace {
 
-constexpr int kEvictThreads = 1024;
-constexpr int kEvictWarps = kEvictThreads / 32;
-constexpr int kMaxEvictLen = kEvictThreads * 32;
+// Up to 16 scores per thread the CTA has 1024 threads; longer rows use 512
+// threads holding up to 64 scores each (register budget 128 per thread).
+constexpr int kMaxEvictLen = 32768;
 
 __device__ __forceinline__ int warp_sum_i(int v) {
 #pragma unroll
@@ -37,7 +37,7 @@ __device__ __forceinline__ int warp_sum_i(int v) {
   return v;
 }
 
-template <int VPT>
+template <int VPT, int kEvictThreads>
 __global__ void __launch_bounds__(kEvictThreads, 1)
 evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_heads, int seq_len,
                     int32_t* __restrict__ block_tables, int max_blocks_per_seq,
@@ -51,6 +51,7 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int L = seq_len;
+  constexpr int kEvictWarps = kEvictThreads / 32;
 
   __shared__ float red_f[2][kEvictWarps];
   __shared__ int red_i[2][kEvictWarps];
@@ -60,14 +61,24 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   const float* src = scores + (static_cast<int64_t>(seq) * num_heads + head) * L;
   float v[VPT];
   const int t0 = tid * VPT;
+  const bool vec = (VPT % 4 == 0) && (L % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  if (vec) {
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int t = t0 + i;
-    float s = 0.f;
-    if (t < L) s = __ldg(src + t);
-    if (t < num_sinks) s = 1e38f;
-    v[i] = s;
+    for (int k = 0; k < VPT / 4; ++k) {
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0 + 4 * k < L) f = __ldg(reinterpret_cast<const float4*>(src + t0) + k);
+      v[4 * k] = f.x;
+      v[4 * k + 1] = f.y;
+      v[4 * k + 2] = f.z;
+      v[4 * k + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) v[i] = (t0 + i < L) ? __ldg(src + t0 + i) : 0.f;
   }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+    if (t0 + i < num_sinks) v[i] = 1e38f;
 
   // ---- min / max ---------------------------------------------------------
   float lmin = 1e38f, lmax = -1e38f;
@@ -103,12 +114,30 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     thr = gmin - 1.0f;
   } else {
     float lo = gmin, hi = gmax;
+    // This thread's own range: a midpoint above it counts 0, at or below its
+    // minimum counts every valid element, without a scan (exact either way).
+    int nvalid = 0;
+    float tmin = INFINITY, tmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      if (t0 + i < L) {
+        ++nvalid;
+        tmin = fminf(tmin, v[i]);
+        tmax = fmaxf(tmax, v[i]);
+      }
+    }
 #pragma unroll 1
     for (int it = 0; it < 32; ++it) {
       const float mid = __fmaf_rn(hi - lo, 0.5f, lo);
       int c = 0;
+      if (nvalid == 0 || mid > tmax) {
+        c = 0;
+      } else if (mid <= tmin) {
+        c = nvalid;
+      } else {
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) c += (t0 + i < L && v[i] >= mid) ? 1 : 0;
+        for (int i = 0; i < VPT; ++i) c += (t0 + i < L && v[i] >= mid) ? 1 : 0;
+      }
       c = warp_sum_i(c);
       const int buf = it & 1;
       if (lane == 0) red_i[buf][warp] = c;
@@ -183,10 +212,19 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     const int64_t pair = static_cast<int64_t>(seq) * num_heads + head;
     if (retained_idx != nullptr) {
       int32_t* dst = retained_idx + pair * L;
+      const int nval = max(0, min(VPT, L - t0));
+      const bool aligned = ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) && (out % 4 == 0);
+      if (VPT % 4 == 0 && kept == nval && nval == VPT && aligned) {
+        // Every token of this thread is kept: its indices are one contiguous run.
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const int t = t0 + i;
-        if (t < L && !(v[i] < thr)) dst[out++] = t;
+        for (int k = 0; k < VPT / 4; ++k)
+          reinterpret_cast<int4*>(dst + out)[k] = make_int4(t0 + 4 * k, t0 + 4 * k + 1, t0 + 4 * k + 2, t0 + 4 * k + 3);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+          const int t = t0 + i;
+          if (t < L && !(v[i] < thr)) dst[out++] = t;
+        }
       }
       for (int t = total + tid; t < L; t += kEvictThreads) dst[t] = -1;
     }
@@ -318,18 +356,18 @@ extern "C" int memopt_evict_tokens(const float* scores, int num_seqs, int num_he
   const int sinks = num_sink_tokens < 0 ? 0 : (num_sink_tokens > seq_len ? seq_len : num_sink_tokens);
   const dim3 grid(num_seqs, num_heads);
   cudaStream_t s = as_stream(stream);
-  const int vpt = (seq_len + kEvictThreads - 1) / kEvictThreads;
-#define MEMOPT_EVICT_LAUNCH(V)                                                                    \
-  evict_tokens_kernel<V><<<grid, kEvictThreads, 0, s>>>(                                        \
+  const int vpt1024 = (seq_len + 1023) / 1024;
+#define MEMOPT_EVICT_LAUNCH(V, NT)                                                                \
+  evict_tokens_kernel<V, NT><<<grid, NT, 0, s>>>(                                               \
       scores, num_seqs, num_heads, seq_len, block_tables, max_blocks_per_seq, is_block_free,     \
       total_pool_blocks, reinterpret_cast<__half*>(key_pool), reinterpret_cast<__half*>(value_pool), \
       block_size, head_dim, retain_ratio, sinks, retained_idx, retained_count)
-  if (vpt <= 1) MEMOPT_EVICT_LAUNCH(1);
-  else if (vpt <= 2) MEMOPT_EVICT_LAUNCH(2);
-  else if (vpt <= 4) MEMOPT_EVICT_LAUNCH(4);
-  else if (vpt <= 8) MEMOPT_EVICT_LAUNCH(8);
-  else if (vpt <= 16) MEMOPT_EVICT_LAUNCH(16);
-  else MEMOPT_EVICT_LAUNCH(32);
+  if (vpt1024 <= 1) MEMOPT_EVICT_LAUNCH(1, 1024);
+  else if (vpt1024 <= 2) MEMOPT_EVICT_LAUNCH(2, 1024);
+  else if (vpt1024 <= 4) MEMOPT_EVICT_LAUNCH(4, 1024);
+  else if (vpt1024 <= 8) MEMOPT_EVICT_LAUNCH(8, 1024);
+  else if (vpt1024 <= 16) MEMOPT_EVICT_LAUNCH(16, 1024);
+  else MEMOPT_EVICT_LAUNCH(64, 512);
 #undef MEMOPT_EVICT_LAUNCH
   MEMOPT_LAUNCH_CHECK("evict_tokens launch");
   return MEMOPT_OK;

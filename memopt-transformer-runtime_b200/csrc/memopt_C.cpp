@@ -259,8 +259,9 @@ pybind11::object evict_tokens(torch::Tensor attention_scores, torch::Tensor bloc
   torch::Tensor idx, cnt;
   if (return_retained) {
     auto o = torch::TensorOptions().dtype(torch::kInt32).device(attention_scores.device());
-    idx = torch::full({S, H, L}, -1, o);
-    cnt = torch::zeros({S, H}, o);
+    // The kernel writes every element (kept indices, then -1 padding).
+    idx = (S == 0 || L == 0) ? torch::full({S, H, L}, -1, o) : torch::empty({S, H, L}, o);
+    cnt = (S == 0 || L == 0) ? torch::zeros({S, H}, o) : torch::empty({S, H}, o);
   }
   if (S == 0 || L == 0) {
     if (return_retained) return pybind11::make_tuple(idx, cnt);

@@ -53,3 +53,12 @@ def paged_attention_int4(q, pages, block_size, bt, ctx, out, msl, win, ws, ws_by
 
 def workspace_size(B, QL, H, D, MB, BS, msl, win) -> int:
     return int(lib().memopt_paged_attention_workspace_size(B, QL, H, D, MB, BS, msl, win))
+
+
+def evict_tokens(scores, bt, ibf, kpool, vpool, retain_ratio, num_sinks, idx, cnt, stream):
+    S, Hh, L = scores.shape
+    check(lib().memopt_evict_tokens(
+        P(scores.data_ptr()), I(S), I(Hh), I(L), P(bt.data_ptr()), I(bt.shape[1]), P(ibf.data_ptr()),
+        I(ibf.shape[0]), P(kpool.data_ptr()), P(vpool.data_ptr()), I(kpool.shape[0]), I(kpool.shape[1]),
+        I(kpool.shape[3]), F(retain_ratio), I(num_sinks), P(idx.data_ptr() if idx is not None else 0),
+        P(cnt.data_ptr() if cnt is not None else 0), P(stream)), "memopt_evict_tokens")
