@@ -66,7 +66,7 @@ def build_lib(verbose: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         list(ex.map(lambda so: _compile_one(so[0], so[1], verbose), zip(srcs, objs)))
     tmp = LIB + ".tmp"
-    cmd = [_nvcc(), "-shared", "-cudart", "static", *objs, "-o", tmp,
+    cmd = [_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static", *objs, "-o", tmp,
            "-Xlinker", "-soname=libmemopt_b200.so"]
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB)

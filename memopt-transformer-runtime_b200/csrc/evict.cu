@@ -13,8 +13,8 @@
 //   * the per-block vote counts only evicted tokens with t % 32 == 0 (:978),
 //     so it can reach block_size only when block_size == 1 (:993-1014).
 // The reference runs one 128-thread CTA per (seq, head) with the scores in
-// shared memory and three barriers per bisection step; here a 1024-thread
-// CTA keeps the scores in registers (<= 32 per thread), each step costs one
+// shared memory and three barriers per bisection step; here one CTA keeps the
+// scores in registers (<= 64 per thread), each step costs one
 // barrier (double-buffered warp partials), and the kept tokens are also
 // stream-compacted into an ascending index list.
 //
@@ -27,8 +27,9 @@
 namespace memopt {
 namespace {
 
-// Up to 16 scores per thread the CTA has 1024 threads; longer rows use 512
-// threads holding up to 64 scores each (register budget 128 per thread).
+// Scores per thread (VPT) are a multiple of 4: rows up to 1024 tokens use 256
+// threads, up to 16384 tokens 1024 threads with 4..16 scores each, longer
+// rows 512 threads holding 64 scores each (register budget 128 per thread).
 constexpr int kMaxEvictLen = 32768;
 
 __device__ __forceinline__ int warp_sum_i(int v) {
@@ -45,6 +46,7 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
                     __half* __restrict__ kpool, __half* __restrict__ vpool, int block_size,
                     int head_dim, float retain_ratio, int num_sinks,
                     int32_t* __restrict__ retained_idx, int32_t* __restrict__ retained_count) {
+  static_assert(VPT % 4 == 0 && VPT <= 64, "VPT: multiple of 4, at most 64 (one 64-bit mask)");
   const int seq = blockIdx.x;
   const int head = blockIdx.y;
   const int tid = threadIdx.x;
@@ -57,16 +59,29 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   __shared__ int red_i[2][kEvictWarps];
   __shared__ int warp_tot[kEvictWarps];
 
-  // ---- load (thread owns tokens [tid*VPT, tid*VPT+VPT)) -------------------
+  // ---- load: warp w owns tokens [w*32*VPT, (w+1)*32*VPT); in round k lane
+  // holds the 4 tokens chunk + 128 k + 4 lane .. +3, so every warp load and
+  // every index store covers 512 contiguous bytes.  A lane's tokens ascend
+  // with i, so its valid ones are the first nv.
   const float* src = scores + (static_cast<int64_t>(seq) * num_heads + head) * L;
+  const int wbase = warp * (32 * VPT);
+  auto tok = [&](int i) { return wbase + (i >> 2) * 128 + lane * 4 + (i & 3); };
+  int nv = 0;
+#pragma unroll
+  for (int k = 0; k < VPT / 4; ++k) nv += min(4, max(0, L - tok(4 * k)));
+
+  // Tokens past L hold NaN: fminf/fmaxf skip it and `s >= mid` / `s < thr`
+  // are false for it, exactly how the reference treats a NaN score, so the
+  // scans below need no bounds test (a real NaN score is never counted and
+  // never evicted either).
   float v[VPT];
-  const int t0 = tid * VPT;
-  const bool vec = (VPT % 4 == 0) && (L % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  const bool vec = (L % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
   if (vec) {
 #pragma unroll
     for (int k = 0; k < VPT / 4; ++k) {
-      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t0 + 4 * k < L) f = __ldg(reinterpret_cast<const float4*>(src + t0) + k);
+      float4 f = make_float4(NAN, NAN, NAN, NAN);
+      const int t = tok(4 * k);
+      if (t < L) f = __ldg(reinterpret_cast<const float4*>(src + t));
       v[4 * k] = f.x;
       v[4 * k + 1] = f.y;
       v[4 * k + 2] = f.z;
@@ -74,33 +89,36 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) v[i] = (t0 + i < L) ? __ldg(src + t0 + i) : 0.f;
+    for (int i = 0; i < VPT; ++i) v[i] = i < nv ? __ldg(src + tok(i)) : NAN;
   }
+  if (wbase < num_sinks) {
 #pragma unroll
-  for (int i = 0; i < VPT; ++i)
-    if (t0 + i < num_sinks) v[i] = 1e38f;
+    for (int i = 0; i < VPT; ++i)
+      if (tok(i) < num_sinks) v[i] = 1e38f;
+  }
 
-  // ---- min / max ---------------------------------------------------------
-  float lmin = 1e38f, lmax = -1e38f;
+  // ---- min / max and this thread's count of comparable scores -----------
+  float tmin = 1e38f, tmax = -1e38f;
+  int ncmp = 0;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    if (t0 + i < L) {
-      lmin = fminf(lmin, v[i]);
-      lmax = fmaxf(lmax, v[i]);
-    }
+    tmin = fminf(tmin, v[i]);
+    tmax = fmaxf(tmax, v[i]);
+    ncmp += (v[i] == v[i]) ? 1 : 0;
   }
+  float gmin = tmin, gmax = tmax;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
-    lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    gmin = fminf(gmin, __shfl_xor_sync(0xffffffffu, gmin, o));
+    gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
   }
   if (lane == 0) {
-    red_f[0][warp] = lmin;
-    red_f[1][warp] = lmax;
+    red_f[0][warp] = gmin;
+    red_f[1][warp] = gmax;
   }
   __syncthreads();
-  float gmin = lane < kEvictWarps ? red_f[0][lane] : 1e38f;
-  float gmax = lane < kEvictWarps ? red_f[1][lane] : -1e38f;
+  gmin = lane < kEvictWarps ? red_f[0][lane] : 1e38f;
+  gmax = lane < kEvictWarps ? red_f[1][lane] : -1e38f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     gmin = fminf(gmin, __shfl_xor_sync(0xffffffffu, gmin, o));
@@ -114,29 +132,16 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     thr = gmin - 1.0f;
   } else {
     float lo = gmin, hi = gmax;
-    // This thread's own range: a midpoint above it counts 0, at or below its
-    // minimum counts every valid element, without a scan (exact either way).
-    int nvalid = 0;
-    float tmin = INFINITY, tmax = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      if (t0 + i < L) {
-        ++nvalid;
-        tmin = fminf(tmin, v[i]);
-        tmax = fmaxf(tmax, v[i]);
-      }
-    }
 #pragma unroll 1
     for (int it = 0; it < 32; ++it) {
       const float mid = __fmaf_rn(hi - lo, 0.5f, lo);
-      int c = 0;
-      if (nvalid == 0 || mid > tmax) {
+      // A midpoint above this thread's largest score counts nothing, one at
+      // or below its smallest counts every comparable score: no scan needed.
+      int c = mid > tmax ? 0 : ncmp;
+      if (mid > tmin && mid <= tmax) {
         c = 0;
-      } else if (mid <= tmin) {
-        c = nvalid;
-      } else {
 #pragma unroll
-        for (int i = 0; i < VPT; ++i) c += (t0 + i < L && v[i] >= mid) ? 1 : 0;
+        for (int i = 0; i < VPT; ++i) c += (v[i] >= mid) ? 1 : 0;
       }
       c = warp_sum_i(c);
       const int buf = it & 1;
@@ -149,17 +154,18 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     thr = lo;
   }
 
+  // ---- evicted tokens as a bit mask (bit i <-> v[i]) -----------------------
+  uint64_t ev = 0;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) ev |= static_cast<uint64_t>(v[i] < thr ? 1 : 0) << i;
+  const int kept = nv - __popcll(ev);
+
   // ---- zero evicted rows (partial pattern) ---------------------------------
   const int64_t hd = static_cast<int64_t>(head_dim);
   const int64_t table_size = static_cast<int64_t>(num_seqs) * max_blocks_per_seq;
-  int kept = 0;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int t = t0 + i;
-    if (t >= L) continue;
-    const bool evicted = v[i] < thr;
-    kept += evicted ? 0 : 1;
-    if (!evicted) continue;
+  for (uint64_t m = ev; m != 0; m &= m - 1) {
+    const int i = __ffsll(static_cast<long long>(m)) - 1;
+    const int t = tok(i);
     const int lb = t / block_size;
     const int pos = t - lb * block_size;
     const int64_t flat = static_cast<int64_t>(seq) * max_blocks_per_seq + lb;
@@ -176,10 +182,9 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     // Only here can a block's vote reach block_size: token t == lb, counted
     // when t % 32 == 0.  Votes follow every zeroing of this CTA.
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int t = t0 + i;
-      if (t >= L || (t & 31) != 0 || !(v[i] < thr)) continue;
+    for (uint64_t m = ev; m != 0; m &= m - 1) {
+      const int t = tok(__ffsll(static_cast<long long>(m)) - 1);
+      if ((t & 31) != 0) continue;
       const int64_t flat = static_cast<int64_t>(seq) * max_blocks_per_seq + t;
       if (flat >= table_size) continue;
       const int phys = block_tables[flat];
@@ -190,14 +195,11 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   }
 
   // ---- stream compaction of kept token indices ---------------------------
+  // Warp offsets come from a block scan of per-warp kept counts; inside a
+  // warp the 128-token rounds are emitted in order with a lane scan each.
   if (retained_idx != nullptr || retained_count != nullptr) {
-    int incl = kept;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
+    const int wkept = warp_sum_i(kept);
+    if (lane == 0) warp_tot[warp] = wkept;
     __syncthreads();
     const int wt = lane < kEvictWarps ? warp_tot[lane] : 0;
     int wincl = wt;
@@ -206,24 +208,33 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
       const int n = __shfl_up_sync(0xffffffffu, wincl, o);
       if (lane >= o) wincl += n;
     }
-    const int warp_off = __shfl_sync(0xffffffffu, wincl - wt, warp);
+    int out = __shfl_sync(0xffffffffu, wincl - wt, warp);
     const int total = __shfl_sync(0xffffffffu, wincl, 31);
-    int out = warp_off + incl - kept;
     const int64_t pair = static_cast<int64_t>(seq) * num_heads + head;
     if (retained_idx != nullptr) {
       int32_t* dst = retained_idx + pair * L;
-      const int nval = max(0, min(VPT, L - t0));
-      const bool aligned = ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) && (out % 4 == 0);
-      if (VPT % 4 == 0 && kept == nval && nval == VPT && aligned) {
-        // Every token of this thread is kept: its indices are one contiguous run.
+      const bool dst16 = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+      const uint64_t keepm = ~ev & (nv >= 64 ? ~0ull : ((1ull << nv) - 1ull));
+#pragma unroll 1
+      for (int k = 0; k < VPT / 4; ++k) {
+        const uint32_t b = static_cast<uint32_t>(keepm >> (4 * k)) & 0xFu;
+        const int n4 = __popc(b);
+        const int t = tok(4 * k);
+        if (__all_sync(0xffffffffu, b == 0xFu) && dst16 && (out & 3) == 0) {
+          reinterpret_cast<int4*>(dst + out)[lane] = make_int4(t, t + 1, t + 2, t + 3);
+          out += 128;
+        } else {
+          int incl = n4;
 #pragma unroll
-        for (int k = 0; k < VPT / 4; ++k)
-          reinterpret_cast<int4*>(dst + out)[k] = make_int4(t0 + 4 * k, t0 + 4 * k + 1, t0 + 4 * k + 2, t0 + 4 * k + 3);
-      } else {
+          for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+          }
+          int pos = out + incl - n4;
 #pragma unroll
-        for (int i = 0; i < VPT; ++i) {
-          const int t = t0 + i;
-          if (t < L && !(v[i] < thr)) dst[out++] = t;
+          for (int j = 0; j < 4; ++j)
+            if (b & (1u << j)) dst[pos++] = t + j;
+          out += __shfl_sync(0xffffffffu, incl, 31);
         }
       }
       for (int t = total + tid; t < L; t += kEvictThreads) dst[t] = -1;
@@ -362,8 +373,7 @@ extern "C" int memopt_evict_tokens(const float* scores, int num_seqs, int num_he
       scores, num_seqs, num_heads, seq_len, block_tables, max_blocks_per_seq, is_block_free,     \
       total_pool_blocks, reinterpret_cast<__half*>(key_pool), reinterpret_cast<__half*>(value_pool), \
       block_size, head_dim, retain_ratio, sinks, retained_idx, retained_count)
-  if (vpt1024 <= 1) MEMOPT_EVICT_LAUNCH(1, 1024);
-  else if (vpt1024 <= 2) MEMOPT_EVICT_LAUNCH(2, 1024);
+  if (seq_len <= 1024) MEMOPT_EVICT_LAUNCH(4, 256);
   else if (vpt1024 <= 4) MEMOPT_EVICT_LAUNCH(4, 1024);
   else if (vpt1024 <= 8) MEMOPT_EVICT_LAUNCH(8, 1024);
   else if (vpt1024 <= 16) MEMOPT_EVICT_LAUNCH(16, 1024);

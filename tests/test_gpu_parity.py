@@ -130,6 +130,14 @@ def _evict_case(S, H, L, BS, D, r, sinks, seed, dist="lognormal", extra_pages=3,
         sc = rng.integers(0, 4, (S, H, L)).astype(np.float32)
     elif dist == "const":
         sc = np.full((S, H, L), 2.0, np.float32)
+    elif dist == "specials":  # NaN, +-inf and huge scores scattered through lognormal rows
+        sc = rng.lognormal(0, 1, (S, H, L)).astype(np.float32)
+        m = rng.random((S, H, L))
+        sc[m < 0.02] = np.nan
+        sc[(m >= 0.02) & (m < 0.025)] = np.inf
+        sc[(m >= 0.025) & (m < 0.03)] = -np.inf
+        sc[(m >= 0.03) & (m < 0.032)] = 3e38
+        sc[0, 0, : min(L, 70)] = np.nan  # a whole thread's worth of NaN
     else:
         sc = rng.standard_normal((S, H, L)).astype(np.float32)
     MB = (L + BS - 1) // BS
@@ -155,6 +163,12 @@ def _evict_case(S, H, L, BS, D, r, sinks, seed, dist="lognormal", extra_pages=3,
     (2, 2, 32768, 16, 64, 0.75, 0, "lognormal", False),
     (2, 2, 32768, 16, 64, 0.75, 4, "lognormal", False),
     (1, 2, 300, 1, 32, 0.5, 0, "normal", False),
+    (2, 3, 1023, 16, 64, 0.6, 0, "specials", False),
+    (2, 3, 4097, 16, 64, 0.75, 3, "specials", True),
+    (1, 2, 9001, 16, 64, 0.4, 0, "specials", False),
+    (1, 2, 20001, 16, 64, 0.75, 0, "specials", False),
+    (1, 2, 32767, 16, 64, 0.75, 5, "specials", False),
+    (1, 2, 16384, 16, 64, 0.9, 0, "ties", False),
 ])
 def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + S, dist, holes=holes)
