@@ -185,8 +185,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   const int mg = lane >> 2;      // int4 (mma fragments): group id
   const int mt4 = lane & 3;      // int4 (mma fragments): thread in group
   constexpr int G = D / 64;      // int4 scale groups per row
-  constexpr int NKM = D / 16;    // int4: k-steps of the score mma
-  constexpr int NT = D / 8;      // int4: n-tiles of the P.V mma
+  constexpr int NKB = D / 32;    // int4: k-blocks of the score mma (= P.V dim-block pairs)
   uint32_t c_seq = 0;
   bool failed = false;
 
@@ -199,7 +198,14 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     const int64_t pair = item / p.n_chunks;
 
     float q[8];
-    uint32_t qb[INT4 ? NKM : 1][2];
+    // INT4: B operand of the score mma (m16n8k32, s8).  q is rounded to 16-bit
+    // integers q_int = rint(q / qsc) (|q_int| <= 32639) and split exactly as
+    // q_int = 256 hi + lo with hi, lo in [-128, 127]; column n < 2G of B holds
+    // part (n & 1 ? lo : hi) of the dims of scale group n >> 1.  Lane (mg, mt4)
+    // of k-block kb covers word wi = NKB*mt4 + kb of a K row: its even
+    // dims in b0, its odd dims in b1 (the A side splits the word the same way).
+    uint32_t qb[INT4 ? NKB : 1][2];
+    float sfac = 0.f;
     if constexpr (!INT4) {
       const uint4 qv = *reinterpret_cast<const uint4*>(p.q + pair * D + cl * 8);
       const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
@@ -210,27 +216,43 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         q[2 * i + 1] = f.y * p.qscale;
       }
     } else {
-      // B operand of the score mma: column g holds the q dims of group g.
       const __half* qrow = p.q + pair * D;
+      float am = 0.f;
 #pragma unroll
-      for (int m = 0; m < NKM; ++m) {
-        const int word = (D / 32) * mt4 + m / 2;
-        const int d0 = 8 * word + 2 * (m % 2);
-        const bool use = mg == word / 8;
-        const __half z = __ushort_as_half(0);
-        const __half2 lo = use ? __halves2half2(qrow[d0], qrow[d0 + 4]) : __halves2half2(z, z);
-        const __half2 hi = use ? __halves2half2(qrow[d0 + 1], qrow[d0 + 5]) : __halves2half2(z, z);
-        qb[m][0] = *reinterpret_cast<const uint32_t*>(&lo);
-        qb[m][1] = *reinterpret_cast<const uint32_t*>(&hi);
+      for (int e = lane; e < D; e += 32) am = fmaxf(am, fabsf(__half2float(qrow[e])));
+#pragma unroll
+      for (int mk = 16; mk >= 1; mk >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, mk));
+      const float qsc = am > 0.f ? am / 32639.f : 1.f;
+      const float qinv = am > 0.f ? 32639.f / am : 1.f;
+      // score = sum_g ks_g * sum_d 16 (c - 8) q_int * qsc / 16, then * qscale
+      sfac = qsc * 0.0625f * p.qscale;
+      const bool part_lo = (mg & 1) != 0;
+#pragma unroll
+      for (int kb = 0; kb < NKB; ++kb) {
+        const int wi = NKB * mt4 + kb;  // word of the K row: dims 8 wi .. 8 wi + 7
+        const bool use = mg < 2 * G && (mg >> 1) == wi / 8;
+#pragma unroll
+        for (int odd = 0; odd < 2; ++odd) {
+          uint32_t r = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int qi = __float2int_rn(__half2float(qrow[8 * wi + 2 * e + odd]) * qinv);
+            const int lo = ((qi + 128) & 255) - 128;
+            const int hi = (qi - lo) >> 8;
+            r |= (static_cast<uint32_t>(part_lo ? lo : hi) & 0xFFu) << (8 * e);
+          }
+          qb[kb][odd] = use ? r : 0u;
+        }
       }
     }
     float m = -INFINITY, l = 0.f;
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = 0.f;
-    float acc[INT4 ? NT : 1][2];
+    // INT4 P.V accumulators: (D/32) dim blocks x (low, high nibble) fragments.
+    float acc[INT4 ? 2 * NKB : 1][4];
 #pragma unroll
-    for (int j = 0; j < (INT4 ? NT : 1); ++j) acc[j][0] = acc[j][1] = 0.f;
+    for (int j = 0; j < (INT4 ? 2 * NKB : 1); ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
     // Warp-uniform bounded wait for stage `seq` (a completed phase stays observable).
     auto wait_stage = [&](uint32_t seq) -> bool {
@@ -351,15 +373,16 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         const int trow[2] = {0, (BS == 32) ? 16 : 0};
         const int ttok[2] = {(c_lo + ja) * BS, (BS == 32) ? (c_lo + ja) * BS + 16 : (c_lo + jb) * BS};
         float slo[2], shi[2];
-        // ---- scores on the tensor pipe ----
+        // ---- scores: exact integer products on the tensor pipe ----
+        // A = K codes as signed bytes 16 (c - 8) (rows: tokens mg, mg + 8),
+        // B = q_int halves (qb); lane mt4 < G gets the group-mt4 sums.
 #pragma unroll
         for (int ti = 0; ti < 2; ++ti) {
           slo[ti] = -INFINITY;
           shi[ti] = -INFINITY;
           if (ti == 1 && !has2) break;
           const uint8_t* kr = tstg[ti] + trow[ti] * (D / 2);
-          const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
-          uint32_t w0[D / 32], w1[D / 32];
+          uint32_t w0[NKB], w1[NKB];
           if constexpr (D == 128) {
             const uint4 x0 = *reinterpret_cast<const uint4*>(kr + mg * (D / 2) + mt4 * 16);
             const uint4 x1 = *reinterpret_cast<const uint4*>(kr + (mg + 8) * (D / 2) + mt4 * 16);
@@ -371,31 +394,29 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             w0[0] = x0.x; w0[1] = x0.y;
             w1[0] = x1.x; w1[1] = x1.y;
           }
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-          float c2[4] = {0.f, 0.f, 0.f, 0.f};  // second chain: halves the mma dependency depth
+          int c[4] = {0, 0, 0, 0};
 #pragma unroll
-          for (int i = 0; i < D / 32; ++i) {
-            // Pair k of a word is (elem k, elem k+4); pairs 2,3 come from w >> 8.
+          for (int kb = 0; kb < NKB; ++kb) {
             uint32_t a[4];
-            a[0] = lo_pair(w0[i]); a[1] = lo_pair(w1[i]);
-            a[2] = hi_pair(w0[i]); a[3] = hi_pair(w1[i]);
-            mma16816(c, a, qb[2 * i][0], qb[2 * i][1]);
-            const uint32_t u0 = w0[i] >> 8, u1 = w1[i] >> 8;
-            a[0] = lo_pair(u0); a[1] = lo_pair(u1);
-            a[2] = hi_pair(u0); a[3] = hi_pair(u1);
-            mma16816(c2, a, qb[2 * i + 1][0], qb[2 * i + 1][1]);
+            a[0] = s8x16_even(w0[kb]);
+            a[1] = s8x16_even(w1[kb]);
+            a[2] = s8x16_odd(w0[kb]);
+            a[3] = s8x16_odd(w1[kb]);
+            mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) c[e] += c2[e];
-          // Lanes with mt4 == 0 hold (group0, group1) partials of tokens mg, mg+8.
-          float a_lo = __half2float(ksc[mg * G]) * c[0];
-          float a_hi = __half2float(ksc[(mg + 8) * G]) * c[2];
+          // Lane mt4 < G: (hi, lo) sums of group mt4 for tokens mg, mg + 8.
+          float a_lo = 0.f, a_hi = 0.f;
+          if (mt4 < G) {
+            const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
+            a_lo = __half2float(ksc[mg * G + mt4]) * static_cast<float>(c[0] * 256 + c[1]);
+            a_hi = __half2float(ksc[(mg + 8) * G + mt4]) * static_cast<float>(c[2] * 256 + c[3]);
+          }
           if constexpr (G > 1) {
-            a_lo = fmaf(__half2float(ksc[mg * G + 1]), c[1], a_lo);
-            a_hi = fmaf(__half2float(ksc[(mg + 8) * G + 1]), c[3], a_hi);
+            a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
+            a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
           }
-          a_lo = __shfl_sync(0xffffffffu, a_lo * p.qscale, lane & ~3);
-          a_hi = __shfl_sync(0xffffffffu, a_hi * p.qscale, lane & ~3);
+          a_lo = __shfl_sync(0xffffffffu, a_lo * sfac, lane & ~3);
+          a_hi = __shfl_sync(0xffffffffu, a_hi * sfac, lane & ~3);
           const int tl = ttok[ti] + mg;
           const bool interior = ttok[ti] >= win_start && ttok[ti] + 16 <= ctx;
           slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
@@ -417,56 +438,65 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
           if (alpha != 1.f) {  // warp-uniform; skipped once the running max settles
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-              acc[j][0] *= alpha;
-              acc[j][1] *= alpha;
+            for (int j = 0; j < 2 * NKB; ++j) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[j][e] *= alpha;
             }
           }
-          // ---- P.V on the tensor pipe ----
+          // ---- P.V on the tensor pipe, dims as rows ----
+          // A = V codes (c - 8) in fp16: rows = 16 dims of a block, k = the
+          // tile's tokens with k (2t, 2t+1, 8+2t, 9+2t) <-> tokens (t, t+4,
+          // t+8, t+12); B = p * scale with column g = scale group g.
+          // Lane (mg, mt4) reads dims [D/8 * mg, D/8 * (mg + 1)) of those four
+          // token rows; block j pairs bytes 2j, 2j+1 of that run: low nibbles
+          // -> fragment (j, low) = dims D/8 mg + 4j + {0, 2}, high nibbles ->
+          // (j, high) = dims D/8 mg + 4j + {1, 3}.
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
             if (ti == 1 && !has2) break;
             const uint8_t* vr = tstg[ti] + C::K_BYTES + trow[ti] * (D / 2);
-            const __half* vsc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES + C::S_BYTES) + trow[ti] * G;
-            uint32_t wa[4], wb[4];
-            const int gs = mg < G ? mg : G - 1;  // scale group of A row mg (rows >= G unused)
-            // p of tokens 0..7 travel in the low half, 8..15 in the high half.
-            const uint32_t pk = pack_half2(slo[ti], shi[ti]);
-            const uint32_t psel = (mt4 & 1) ? 0x7632u : 0x5410u;
-            uint32_t a[4];
-#pragma unroll
-            for (int sp = 0; sp < 2; ++sp) {
-              // Token slots 2sp, 2sp+1 of this lane (conflict-free token order).
-              const int r0 = (mt4 >> 1) + 2 * (4 * (mt4 & 1) + 2 * sp);
-              const int r1 = r0 + 2;
-              wa[2 * sp] = *reinterpret_cast<const uint32_t*>(vr + r0 * (D / 2) + 4 * mg);
-              wa[2 * sp + 1] = *reinterpret_cast<const uint32_t*>(vr + r1 * (D / 2) + 4 * mg);
-              if constexpr (D == 128) {
-                wb[2 * sp] = *reinterpret_cast<const uint32_t*>(vr + r0 * (D / 2) + 4 * (mg + 8));
-                wb[2 * sp + 1] = *reinterpret_cast<const uint32_t*>(vr + r1 * (D / 2) + 4 * (mg + 8));
-              }
-              const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * (r0 & 7));
-              const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * (r1 & 7));
-              const uint32_t p01 = __byte_perm(u0, u1, psel);
-              const uint32_t s0 = __half_as_ushort(vsc[r0 * G + gs]);
-              const uint32_t s1 = __half_as_ushort(vsc[r1 * G + gs]);
-              const uint32_t v01 = s0 | (s1 << 16);
-              const __half2 pv = __hmul2(*reinterpret_cast<const __half2*>(&p01),
-                                         *reinterpret_cast<const __half2*>(&v01));
-              a[2 * sp] = *reinterpret_cast<const uint32_t*>(&pv);
+            const int tile = trow[ti] / 16;
+            const int grp = G > 1 ? (mg & 1) : 0;  // column mg of B (columns >= G unused)
+            const uint8_t* vsb = tstg[ti] + 2 * C::K_BYTES + C::S_BYTES + (tile * G + grp) * 32;
+            const uint32_t pk = pack_half2(slo[ti], shi[ti]);   // (p_mg, p_mg+8)
+            const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * mt4);        // (p_t, p_t+8)
+            const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * mt4 + 16);   // (p_t+4, p_t+12)
+            const uint32_t p04 = __byte_perm(u0, u1, 0x5410);
+            const uint32_t p8c = __byte_perm(u0, u1, 0x7632);
+            const uint32_t vs04 = *reinterpret_cast<const uint32_t*>(vsb + 4 * mt4);
+            const uint32_t vs8c = *reinterpret_cast<const uint32_t*>(vsb + 16 + 4 * mt4);
+            const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
+            const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
+            uint32_t T0[2], T4[2], Y0[2], Y4[2];
+            if constexpr (D == 128) {
+              // rows t, t+4, t+8, t+12 share bit 1 with t: 32-byte halves exchanged when set
+              const int off = 8 * (mg ^ ((mt4 & 2) ? 4 : 0));
+              const uint2 r0 = *reinterpret_cast<const uint2*>(vr + mt4 * 64 + off);
+              const uint2 r4 = *reinterpret_cast<const uint2*>(vr + (mt4 + 4) * 64 + off);
+              const uint2 r8 = *reinterpret_cast<const uint2*>(vr + (mt4 + 8) * 64 + off);
+              const uint2 rc = *reinterpret_cast<const uint2*>(vr + (mt4 + 12) * 64 + off);
+              T0[0] = r0.x; T0[1] = r0.y; T4[0] = r4.x; T4[1] = r4.y;
+              Y0[0] = r8.x; Y0[1] = r8.y; Y4[0] = rc.x; Y4[1] = rc.y;
+            } else {
+              T0[0] = *reinterpret_cast<const uint32_t*>(vr + mt4 * 32 + 4 * mg);
+              T4[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 4) * 32 + 4 * mg);
+              Y0[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 8) * 32 + 4 * mg);
+              Y4[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 12) * 32 + 4 * mg);
+              T0[1] = T4[1] = Y0[1] = Y4[1] = 0u;
             }
-            a[1] = 0u;
-            a[3] = 0u;
-            // n-tiles 2jb and 2jb+1 read the low and high nibble of byte jb%4
-            // of word (mg + 8 * (jb / 4)) from the four token rows.
 #pragma unroll
-            for (int jq = 0; jq < NT / 2; ++jq) {
-              const uint32_t* w = (jq < 4) ? wa : wb;
-              const uint32_t sel = static_cast<uint32_t>(jq % 4) | (static_cast<uint32_t>(4 + jq % 4) << 8);
-              const uint32_t x01 = __byte_perm(w[0], w[1], sel);
-              const uint32_t x23 = __byte_perm(w[2], w[3], sel);
-              mma16816_top(acc[2 * jq][0], acc[2 * jq][1], a, lo_pair(x01), lo_pair(x23));
-              mma16816_top(acc[2 * jq + 1][0], acc[2 * jq + 1][1], a, hi_pair(x01), hi_pair(x23));
+            for (int j = 0; j < NKB; ++j) {
+              const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
+              const uint32_t x = __byte_perm(T0[j >> 1], T4[j >> 1], sel);  // tokens t | t+4
+              const uint32_t y = __byte_perm(Y0[j >> 1], Y4[j >> 1], sel);  // tokens t+8 | t+12
+              const uint32_t x8 = x >> 8, y8 = y >> 8;
+              uint32_t a[4];
+              a[0] = lo_pair(x); a[1] = lo_pair(x8); a[2] = lo_pair(y); a[3] = lo_pair(y8);
+              mma16816(acc[2 * j], a, b0, b1);
+              a[0] = hi_pair(x); a[1] = hi_pair(x8); a[2] = hi_pair(y); a[3] = hi_pair(y8);
+              mma16816(acc[2 * j + 1], a, b0, b1);
             }
           }
         }
@@ -489,7 +519,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
     for (int mk = 16; mk >= 1; mk >>= 1) l += __shfl_xor_sync(0xffffffffu, l, mk);
     // Each writing lane owns DPW contiguous output dims starting at dbase.
-    constexpr int DPW = INT4 ? 16 : 8;
+    constexpr int DPW = INT4 ? D / 8 : 8;
     float ov[DPW];
     int dbase = 0;
     bool writer = false;
@@ -504,19 +534,19 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       dbase = cl * 8;
       writer = r == 0;
     } else {
-      // Lane (g < G, t) holds dims 64g + 16t + [0, 16): acc[8g + jj][c] is
-      // dim 64g + 8(2t + c) + jj.
+      // Lane (mg, 0) holds dims D/8 mg + [0, D/8): fragment (j, hl) row mg
+      // is dim D/8 mg + 4j + hl, row mg + 8 is + 2; column = scale group.
+      const int grp = (D / 8) * mg / 64;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int j = 0; j < NKB; ++j) {
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          float v = acc[jj][c];
-          if constexpr (G > 1) v = (mg == 1) ? acc[8 + jj][c] : v;
-          ov[c * 8 + jj] = v;
+        for (int hl = 0; hl < 2; ++hl) {
+          ov[4 * j + hl] = grp ? acc[2 * j + hl][1] : acc[2 * j + hl][0];
+          ov[4 * j + 2 + hl] = grp ? acc[2 * j + hl][3] : acc[2 * j + hl][2];
         }
       }
-      dbase = 64 * mg + 16 * mt4;
-      writer = mg < G;
+      dbase = (D / 8) * mg;
+      writer = mt4 == 0;
     }
 
     if (p.n_chunks == 1) {

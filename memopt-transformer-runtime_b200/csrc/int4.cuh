@@ -54,4 +54,21 @@ __device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
   return w;
 }
 
+// INT4 page layout helpers (one page per (block, head)):
+//   [K codes BS*D/2 | V codes BS*D/2 | K scales BS*(D/64) fp16 | V scales]
+// K row pos holds byte i = q[2i] | q[2i+1] << 4 at byte i.  The V row holds
+// the same bytes, but for D == 128 byte i sits at i ^ 32 when bit 1 of pos is
+// set (the decode reads rows t and t+2 of a tile in one shared-memory
+// instruction; the exchange puts them in different banks).  K scales are
+// [BS][D/64]; V scales, per 16-token tile, [D/64][16] with token r of the
+// tile at slot 2(r & 3) + ((r >> 2) & 1) + 8(r >> 3), which puts the tokens
+// (t, t+4) and (t+8, t+12) that one decode lane pairs next to each other.
+__host__ __device__ __forceinline__ int int4_vrow_swizzle(int pos, int byte, int head_dim) {
+  return (head_dim == 128 && (pos & 2)) ? (byte ^ 32) : byte;
+}
+__host__ __device__ __forceinline__ int int4_vscale_index(int pos, int group, int groups) {
+  const int r = pos & 15;
+  return ((pos >> 4) * groups + group) * 16 + 2 * (r & 3) + ((r >> 2) & 1) + 8 * (r >> 3);
+}
+
 }  // namespace memopt

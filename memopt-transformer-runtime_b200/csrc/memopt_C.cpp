@@ -74,9 +74,9 @@ void init_pool(int num_blocks, int block_size, int num_heads, int head_dim, cons
   p.k = p.v = p.kvp = torch::Tensor();
   memopt_pool_reset();
   check(memopt_pool_init(num_blocks, block_size, num_heads, head_dim), "init_pool");
-  if (int4 && head_dim % 64 != 0) {
+  if (int4 && (head_dim % 64 != 0 || block_size % 16 != 0)) {
     memopt_pool_reset();
-    TORCH_CHECK(false, "init_pool: kv_format='int4' needs head_dim % 64 == 0");
+    TORCH_CHECK(false, "init_pool: kv_format='int4' needs head_dim % 64 == 0 and block_size % 16 == 0");
   }
   auto dev = torch::Device(torch::kCUDA, c10::cuda::current_device());
   if (!int4) {
@@ -107,7 +107,8 @@ void free_block(int block_idx) { check(memopt_pool_free_block(block_idx), "free_
 int free_blocks_count() { return memopt_pool_free_blocks_count(); }
 
 namespace {
-// Strided views of the four regions of every INT4 page (see memopt_b200.h).
+// Strided views of the four regions of every INT4 page in stored order (the
+// layout is documented at memopt_write_cache_int4 in memopt_b200.h).
 std::vector<torch::Tensor> int4_views(const torch::Tensor& kvp, int bs, int d) {
   const int64_t nb = kvp.size(0), h = kvp.size(1), pb = kvp.size(2), g = d / 64;
   const int64_t codes = static_cast<int64_t>(bs) * (d / 2);
@@ -115,7 +116,9 @@ std::vector<torch::Tensor> int4_views(const torch::Tensor& kvp, int bs, int d) {
   auto vc = kvp.as_strided({nb, h, bs, d / 2}, {h * pb, pb, d / 2, 1}, kvp.storage_offset() + codes);
   auto k16 = kvp.view(torch::kFloat16);  // [nb, h, pb / 2]
   auto ks = k16.as_strided({nb, h, bs, g}, {h * pb / 2, pb / 2, g, 1}, k16.storage_offset() + codes);
-  auto vs = k16.as_strided({nb, h, bs, g}, {h * pb / 2, pb / 2, g, 1}, k16.storage_offset() + codes + bs * g);
+  // V scales are stored per 16-token tile as [G][16] in a permuted token order.
+  auto vs = k16.as_strided({nb, h, bs / 16, g, 16}, {h * pb / 2, pb / 2, g * 16, 16, 1},
+                           k16.storage_offset() + codes + bs * g);
   return {kc, ks, vc, vs};
 }
 }  // namespace

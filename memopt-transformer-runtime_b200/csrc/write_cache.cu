@@ -137,14 +137,16 @@ write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict_
           const int h = g / gpr;
           const int gi = g - h * gpr;
           uint8_t* page = pages + (blk * num_heads + h) * page_bytes;
-          const int64_t code_off = static_cast<int64_t>(pos) * (head_dim / 2) + gi * 32 + (c & 7) * 4;
-          *reinterpret_cast<uint32_t*>(page + code_off) = int4_pack8(fk, sk);
-          *reinterpret_cast<uint32_t*>(page + codes_bytes + code_off) = int4_pack8(fv, sv);
+          const int byte = gi * 32 + (c & 7) * 4;  // logical byte of the row
+          const int64_t row = static_cast<int64_t>(pos) * (head_dim / 2);
+          *reinterpret_cast<uint32_t*>(page + row + byte) = int4_pack8(fk, sk);
+          *reinterpret_cast<uint32_t*>(page + codes_bytes + row + int4_vrow_swizzle(pos, byte, head_dim)) =
+              int4_pack8(fv, sv);
           if ((c & 7) == 0) {
             __half* ks = reinterpret_cast<__half*>(page + 2 * codes_bytes);
             __half* vs = reinterpret_cast<__half*>(page + 2 * codes_bytes + scale_bytes);
             ks[pos * gpr + gi] = __float2half_rn(sk);
-            vs[pos * gpr + gi] = __float2half_rn(sv);
+            vs[int4_vscale_index(pos, gi, gpr)] = __float2half_rn(sv);
           }
         }
       }
@@ -172,6 +174,8 @@ extern "C" int memopt_write_cache_f16(const void* keys, const void* values,
                                       int32_t* bad_slot_count, void* stream) {
   if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0 || num_blocks < 0 || block_size <= 0)
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache: invalid geometry");
+  if (block_size % 16 != 0)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "write_cache_int4: block_size must be a multiple of 16");
   if (num_tokens == 0) return MEMOPT_OK;
   if (!keys || !values || !slot_mapping || !key_pool || !value_pool)
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache: null pointer");

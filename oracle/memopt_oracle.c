@@ -141,8 +141,20 @@ void oracle_write_cache_f16(const uint16_t* keys, const uint16_t* values, const 
 }
 
 /* INT4 pages: one page per (block, head) of
- * [K codes BS*D/2 | V codes BS*D/2 | K scales BS*(D/64) fp16 | V scales]. */
+ * [K codes BS*D/2 | V codes BS*D/2 | K scales BS*(D/64) fp16 | V scales].
+ * K row pos: byte i = code(2i) | code(2i+1) << 4 (the reference packing).
+ * V row pos: the same bytes, except that for D == 128 byte i is stored at
+ * i ^ 32 when bit 1 of pos is set.  K scales [BS][D/64].  V scales, per
+ * 16-token tile: [D/64][16] with token r of the tile at slot
+ * 2(r & 3) + ((r >> 2) & 1) + 8(r >> 3).  BS is a multiple of 16. */
 static int64_t int4_page_bytes(int BS, int D) { return (int64_t)BS * D + (int64_t)BS * (D / 64) * 4; }
+static int64_t int4_vrow_byte(int pos, int i, int D) {
+  return (int64_t)pos * (D / 2) + ((D == 128 && (pos & 2)) ? (i ^ 32) : i);
+}
+static int64_t int4_vscale_index(int pos, int g, int G) {
+  const int r = pos & 15;
+  return ((int64_t)(pos >> 4) * G + g) * 16 + 2 * (r & 3) + ((r >> 2) & 1) + 8 * (r >> 3);
+}
 
 void oracle_write_cache_int4(const uint16_t* keys, const uint16_t* values, const int32_t* slots,
                              int64_t T, int H, int D, uint8_t* pages, int64_t NB, int BS) {
@@ -161,11 +173,15 @@ void oracle_write_cache_int4(const uint16_t* keys, const uint16_t* values, const
           float v[64];
           for (int i = 0; i < 64; ++i) v[i] = oracle_f16_to_f32(src[i]);
           const float sc = int4_scale(v, 64);
-          uint8_t* c = page + kv * codes + (int64_t)pos * (D / 2) + g * 32;
-          for (int i = 0; i < 32; ++i)
-            c[i] = (uint8_t)(int4_code(v[2 * i], sc) | (int4_code(v[2 * i + 1], sc) << 4));
+          for (int i = 0; i < 32; ++i) {
+            const uint8_t b = (uint8_t)(int4_code(v[2 * i], sc) | (int4_code(v[2 * i + 1], sc) << 4));
+            const int bi = g * 32 + i;
+            if (kv) page[codes + int4_vrow_byte(pos, bi, D)] = b;
+            else page[(int64_t)pos * (D / 2) + bi] = b;
+          }
           const uint16_t hs = oracle_f32_to_f16(sc);
-          memcpy(page + 2 * codes + (int64_t)kv * BS * gpr * 2 + ((int64_t)pos * gpr + g) * 2, &hs, 2);
+          const int64_t si = kv ? int4_vscale_index(pos, g, gpr) : (int64_t)pos * gpr + g;
+          memcpy(page + 2 * codes + (int64_t)kv * BS * gpr * 2 + si * 2, &hs, 2);
         }
       }
     }
@@ -299,12 +315,14 @@ static void fetch_row(const kv_src* s, int kv, int64_t phys, int pos, int h, dou
     const int64_t pb = int4_page_bytes(s->BS, s->D), codes = (int64_t)s->BS * (s->D / 2);
     const int G = s->D / 64;
     const uint8_t* page = s->pages + (phys * s->H + h) * pb;
-    const uint8_t* c = page + kv * codes + (int64_t)pos * (s->D / 2);
-    const uint8_t* sc = page + 2 * codes + (int64_t)kv * s->BS * G * 2 + (int64_t)pos * G * 2;
+    const uint8_t* sc = page + 2 * codes + (int64_t)kv * s->BS * G * 2;
     for (int d = 0; d < s->D; ++d) {
-      const int code = (d & 1) ? (c[d / 2] >> 4) : (c[d / 2] & 0xF);
+      const uint8_t byte = kv ? page[codes + int4_vrow_byte(pos, d / 2, s->D)]
+                              : page[(int64_t)pos * (s->D / 2) + d / 2];
+      const int code = (d & 1) ? (byte >> 4) : (byte & 0xF);
+      const int64_t si = kv ? int4_vscale_index(pos, d / 64, G) : (int64_t)pos * G + d / 64;
       uint16_t hs;
-      memcpy(&hs, sc + (d / 64) * 2, 2);
+      memcpy(&hs, sc + si * 2, 2);
       out[d] = (double)(code - 8) * (double)oracle_f16_to_f32(hs);
     }
   }

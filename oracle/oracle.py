@@ -99,14 +99,24 @@ def write_cache_int4(keys, values, slots, pages, block_size) -> None:
 
 
 def int4_views(pages, block_size, head_dim):
-    """(k_codes, k_scales, v_codes, v_scales) numpy views of the INT4 pages."""
+    """(k_codes, k_scales, v_codes, v_scales) of the INT4 pages in logical order:
+    codes [NB, H, BS, D/2] (byte i = code(2i) | code(2i+1) << 4), fp16 scales
+    [NB, H, BS, D/64].  The V rows and V scales are un-permuted from the stored
+    order (for D == 128 the 32-byte halves of V rows whose index has bit 1 set
+    are exchanged; V scales are [BS/16][D/64][16] in a per-tile token order)."""
     NB, H, PB = pages.shape
     BS, D, G = block_size, head_dim, head_dim // 64
     cb = BS * D // 2
     kc = pages[:, :, :cb].reshape(NB, H, BS, D // 2)
-    vc = pages[:, :, cb:2 * cb].reshape(NB, H, BS, D // 2)
+    vc = pages[:, :, cb:2 * cb].reshape(NB, H, BS, D // 2).copy()
+    if D == 128:
+        swap = (np.arange(BS) & 2) != 0
+        vc[:, :, swap] = np.concatenate([vc[:, :, swap, 32:], vc[:, :, swap, :32]], axis=-1)
     ks = np.ascontiguousarray(pages[:, :, 2 * cb:2 * cb + BS * G * 2]).view(np.float16).reshape(NB, H, BS, G)
-    vs = np.ascontiguousarray(pages[:, :, 2 * cb + BS * G * 2:]).view(np.float16).reshape(NB, H, BS, G)
+    vraw = np.ascontiguousarray(pages[:, :, 2 * cb + BS * G * 2:]).view(np.float16).reshape(NB, H, BS // 16, G, 16)
+    r = np.arange(16)
+    slot = 2 * (r & 3) + ((r >> 2) & 1) + 8 * (r >> 3)
+    vs = vraw[..., slot].transpose(0, 1, 2, 4, 3).reshape(NB, H, BS, G)
     return kc, ks, vc, vs
 
 
