@@ -174,6 +174,8 @@ int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t*
   p.NB = NB;
   p.window = clamp_window(window, max_seq_len);
   p.qscale = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  p.magic_f16 = 0x64006400u;
+  p.magic_s8 = 0x80808080u;
   const int64_t pairs = static_cast<int64_t>(batch) * q_len * H;
   const Split sp = choose_split(pairs, MB, BS, p.window);
   p.chunk_pages = sp.chunk_pages;

@@ -43,6 +43,11 @@ struct Params {
   int64_t NB;
   int window;    // already clamped as in attention.cu:453-455
   float qscale;  // log2(e) / sqrt(D)
+  // INT4 code conversion constants, passed at run time so that they stay in
+  // registers and every (x & mask) | const or (x & mask) ^ const is a single
+  // three-input logic op: 0x64006400 (fp16 1024 in both halves), 0x80808080.
+  uint32_t magic_f16;
+  uint32_t magic_s8;
   int chunk_pages;  // pages per item (walked in 32-page sub-windows)
   int n_chunks;
   int64_t total_items;
@@ -186,6 +191,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   const int mt4 = lane & 3;      // int4 (mma fragments): thread in group
   constexpr int G = D / 64;      // int4 scale groups per row
   constexpr int NKB = D / 32;    // int4: k-blocks of the score mma (= P.V dim-block pairs)
+  const uint32_t kF16 = p.magic_f16;
+  const uint32_t kS8 = p.magic_s8;
   uint32_t c_seq = 0;
   bool failed = false;
 
@@ -398,19 +405,19 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
           for (int kb = 0; kb < NKB; ++kb) {
             uint32_t a[4];
-            a[0] = s8x16_even(w0[kb]);
-            a[1] = s8x16_even(w1[kb]);
-            a[2] = s8x16_odd(w0[kb]);
-            a[3] = s8x16_odd(w1[kb]);
+            a[0] = s8x16_even(w0[kb], kS8);
+            a[1] = s8x16_even(w1[kb], kS8);
+            a[2] = s8x16_odd(w0[kb], kS8);
+            a[3] = s8x16_odd(w1[kb], kS8);
             mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
           // Lane mt4 < G: (hi, lo) sums of group mt4 for tokens mg, mg + 8.
-          float a_lo = 0.f, a_hi = 0.f;
-          if (mt4 < G) {
-            const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
-            a_lo = __half2float(ksc[mg * G + mt4]) * static_cast<float>(c[0] * 256 + c[1]);
-            a_hi = __half2float(ksc[(mg + 8) * G + mt4]) * static_cast<float>(c[2] * 256 + c[3]);
-          }
+          // Lanes mt4 >= G compute a value that is never used: the group sum
+          // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
+          const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
+          const int gsel = G > 1 ? (mt4 & 1) : 0;
+          float a_lo = __half2float(ksc[mg * G + gsel]) * static_cast<float>(c[0] * 256 + c[1]);
+          float a_hi = __half2float(ksc[(mg + 8) * G + gsel]) * static_cast<float>(c[2] * 256 + c[3]);
           if constexpr (G > 1) {
             a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
             a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
@@ -493,9 +500,9 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               const uint32_t y = __byte_perm(Y0[j >> 1], Y4[j >> 1], sel);  // tokens t+8 | t+12
               const uint32_t x8 = x >> 8, y8 = y >> 8;
               uint32_t a[4];
-              a[0] = lo_pair(x); a[1] = lo_pair(x8); a[2] = lo_pair(y); a[3] = lo_pair(y8);
+              a[0] = lo_pair(x, kF16); a[1] = lo_pair(x8, kF16); a[2] = lo_pair(y, kF16); a[3] = lo_pair(y8, kF16);
               mma16816(acc[2 * j], a, b0, b1);
-              a[0] = hi_pair(x); a[1] = hi_pair(x8); a[2] = hi_pair(y); a[3] = hi_pair(y8);
+              a[0] = hi_pair(x, kF16); a[1] = hi_pair(x8, kF16); a[2] = hi_pair(y, kF16); a[3] = hi_pair(y8, kF16);
               mma16816(acc[2 * j + 1], a, b0, b1);
             }
           }

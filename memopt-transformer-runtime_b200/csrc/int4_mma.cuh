@@ -34,9 +34,22 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Half2 (n_a - 8, n_b - 8) of the nibbles at bits [0,4) and [16,20) of x.
-__device__ __forceinline__ uint32_t lo_pair(uint32_t x) {
-  uint32_t h = (x & 0x000F000Fu) | 0x64006400u;  // 1024 + n, exactly
+// d = (a & b) | c and d = (a & b) ^ c as one three-input logic op.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t and_xor(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Half2 (n_a - 8, n_b - 8) of the nibbles at bits [0,4) and [16,20) of x
+// (k_f16 = 0x64006400): the half 0x6400 | n is 1024 + n exactly.
+__device__ __forceinline__ uint32_t lo_pair(uint32_t x, uint32_t k_f16) {
+  uint32_t h = and_or(x, 0x000F000Fu, k_f16);
   const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6408)));
   return *reinterpret_cast<const uint32_t*>(&r);
 }
@@ -44,8 +57,8 @@ __device__ __forceinline__ uint32_t lo_pair(uint32_t x) {
 // Half2 (n_a - 8, n_b - 8) of the nibbles at bits [4,8) and [20,24) of x:
 // the half 0x6400 | n << 4 is 1024 + 16 n, and (1024 + 16 n) / 16 - 72 = n - 8
 // with a single exact fma.
-__device__ __forceinline__ uint32_t hi_pair(uint32_t x) {
-  uint32_t h = (x & 0x00F000F0u) | 0x64006400u;
+__device__ __forceinline__ uint32_t hi_pair(uint32_t x, uint32_t k_f16) {
+  uint32_t h = and_or(x, 0x00F000F0u, k_f16);
   const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x2C00)),
                             __half2half2(__ushort_as_half(0xD480)));
   return *reinterpret_cast<const uint32_t*>(&r);
@@ -60,11 +73,12 @@ __device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], uint32_t b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Four codes of a word as signed bytes 16 (n - 8): placing the nibble in the
-// high half of a byte and flipping its top bit gives the two's complement of
-// 16 (n - 8) exactly.  Even elements (low nibbles) / odd elements (high).
-__device__ __forceinline__ uint32_t s8x16_even(uint32_t w) { return ((w << 4) & 0xF0F0F0F0u) ^ 0x80808080u; }
-__device__ __forceinline__ uint32_t s8x16_odd(uint32_t w) { return (w & 0xF0F0F0F0u) ^ 0x80808080u; }
+// Four codes of a word as signed bytes 16 (n - 8) (k_s8 = 0x80808080):
+// placing the nibble in the high half of a byte and flipping its top bit gives
+// the two's complement of 16 (n - 8) exactly.  Even elements (low nibbles) /
+// odd elements (high nibbles).
+__device__ __forceinline__ uint32_t s8x16_even(uint32_t w, uint32_t k_s8) { return and_xor(w << 4, 0xF0F0F0F0u, k_s8); }
+__device__ __forceinline__ uint32_t s8x16_odd(uint32_t w, uint32_t k_s8) { return and_xor(w, 0xF0F0F0F0u, k_s8); }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
