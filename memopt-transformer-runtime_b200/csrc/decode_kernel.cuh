@@ -193,6 +193,12 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
   constexpr int NKB = D / 32;    // int4: k-blocks of the score mma (= P.V dim-block pairs)
   const uint32_t kF16 = p.magic_f16;
   const uint32_t kS8 = p.magic_s8;
+  // INT4: this lane's byte offsets inside a page stage (tile 0).
+  const int i4_grp = G > 1 ? (mg & 1) : 0;  // B column mg of P.V -> scale group (columns >= G unused)
+  const uint32_t o_k = mg * (D / 2) + mt4 * (D / 8);                        // K row mg; row mg + 8 at + 8 D/2
+  const uint32_t o_ks = 2 * C::K_BYTES + (mg * G + (G > 1 ? (mt4 & 1) : 0)) * 2;  // row mg + 8 at + 16 G
+  const uint32_t o_v = C::K_BYTES + (D == 128 ? mt4 * 64 + 8 * (mg ^ ((mt4 & 2) ? 4 : 0)) : mt4 * 32 + 4 * mg);
+  const uint32_t o_vs = 2 * C::K_BYTES + C::S_BYTES + i4_grp * 32 + 4 * mt4;
   uint32_t c_seq = 0;
   bool failed = false;
 
@@ -372,12 +378,13 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           failed = true;
           break;
         }
-        const uint8_t* stg_a = stages + static_cast<int>(c_seq % NS) * C::STAGE;
-        const uint8_t* stg_b = two_pages ? stages + static_cast<int>((c_seq + 1) % NS) * C::STAGE : stg_a;
+        const uint32_t sa = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
+        const uint32_t sb = two_pages ? st0 + static_cast<uint32_t>((c_seq + 1) % NS) * C::STAGE : sa;
         const bool has2 = (BS == 32) || two_pages;
-        // tile -> (stage, first row in the stage, first token position)
-        const uint8_t* tstg[2] = {stg_a, (BS == 32) ? stg_a : stg_b};
-        const int trow[2] = {0, (BS == 32) ? 16 : 0};
+        // tile ti: stage base and the tile's index inside its page (BS == 32
+        // pages hold two 16-token tiles).
+        const uint32_t tb[2] = {sa, (BS == 32) ? sa : sb};
+        const int tt[2] = {0, (BS == 32) ? 1 : 0};
         const int ttok[2] = {(c_lo + ja) * BS, (BS == 32) ? (c_lo + ja) * BS + 16 : (c_lo + jb) * BS};
         float slo[2], shi[2];
         // ---- scores: exact integer products on the tensor pipe ----
@@ -388,19 +395,22 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           slo[ti] = -INFINITY;
           shi[ti] = -INFINITY;
           if (ti == 1 && !has2) break;
-          const uint8_t* kr = tstg[ti] + trow[ti] * (D / 2);
+          const uint32_t kr = tb[ti] + tt[ti] * 16 * (D / 2) + o_k;
           uint32_t w0[NKB], w1[NKB];
           if constexpr (D == 128) {
-            const uint4 x0 = *reinterpret_cast<const uint4*>(kr + mg * (D / 2) + mt4 * 16);
-            const uint4 x1 = *reinterpret_cast<const uint4*>(kr + (mg + 8) * (D / 2) + mt4 * 16);
+            const uint4 x0 = lds_v4(kr);
+            const uint4 x1 = lds_v4(kr + 8 * (D / 2));
             w0[0] = x0.x; w0[1] = x0.y; w0[2] = x0.z; w0[3] = x0.w;
             w1[0] = x1.x; w1[1] = x1.y; w1[2] = x1.z; w1[3] = x1.w;
           } else {
-            const uint2 x0 = *reinterpret_cast<const uint2*>(kr + mg * (D / 2) + mt4 * 8);
-            const uint2 x1 = *reinterpret_cast<const uint2*>(kr + (mg + 8) * (D / 2) + mt4 * 8);
+            const uint2 x0 = lds_v2(kr);
+            const uint2 x1 = lds_v2(kr + 8 * (D / 2));
             w0[0] = x0.x; w0[1] = x0.y;
             w1[0] = x1.x; w1[1] = x1.y;
           }
+          const uint32_t ksa = tb[ti] + tt[ti] * 16 * G * 2 + o_ks;
+          const float ks_lo = lds_f16_as_f32(ksa);
+          const float ks_hi = lds_f16_as_f32(ksa + 16 * G);
           int c[4] = {0, 0, 0, 0};
 #pragma unroll
           for (int kb = 0; kb < NKB; ++kb) {
@@ -411,13 +421,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a[3] = s8x16_odd(w1[kb], kS8);
             mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
-          // Lane mt4 < G: (hi, lo) sums of group mt4 for tokens mg, mg + 8.
           // Lanes mt4 >= G compute a value that is never used: the group sum
           // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
-          const __half* ksc = reinterpret_cast<const __half*>(tstg[ti] + 2 * C::K_BYTES) + trow[ti] * G;
-          const int gsel = G > 1 ? (mt4 & 1) : 0;
-          float a_lo = __half2float(ksc[mg * G + gsel]) * static_cast<float>(c[0] * 256 + c[1]);
-          float a_hi = __half2float(ksc[(mg + 8) * G + gsel]) * static_cast<float>(c[2] * 256 + c[3]);
+          float a_lo = ks_lo * static_cast<float>(c[0] * 256 + c[1]);
+          float a_hi = ks_hi * static_cast<float>(c[2] * 256 + c[3]);
           if constexpr (G > 1) {
             a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
             a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
@@ -461,36 +468,33 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
             if (ti == 1 && !has2) break;
-            const uint8_t* vr = tstg[ti] + C::K_BYTES + trow[ti] * (D / 2);
-            const int tile = trow[ti] / 16;
-            const int grp = G > 1 ? (mg & 1) : 0;  // column mg of B (columns >= G unused)
-            const uint8_t* vsb = tstg[ti] + 2 * C::K_BYTES + C::S_BYTES + (tile * G + grp) * 32;
             const uint32_t pk = pack_half2(slo[ti], shi[ti]);   // (p_mg, p_mg+8)
             const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * mt4);        // (p_t, p_t+8)
             const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * mt4 + 16);   // (p_t+4, p_t+12)
             const uint32_t p04 = __byte_perm(u0, u1, 0x5410);
             const uint32_t p8c = __byte_perm(u0, u1, 0x7632);
-            const uint32_t vs04 = *reinterpret_cast<const uint32_t*>(vsb + 4 * mt4);
-            const uint32_t vs8c = *reinterpret_cast<const uint32_t*>(vsb + 16 + 4 * mt4);
+            const uint32_t vsa = tb[ti] + tt[ti] * G * 32 + o_vs;
+            const uint32_t vs04 = lds_u32(vsa);
+            const uint32_t vs8c = lds_u32(vsa + 16);
             const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
             const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
             const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
             const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
+            const uint32_t vr = tb[ti] + tt[ti] * 16 * (D / 2) + o_v;
             uint32_t T0[2], T4[2], Y0[2], Y4[2];
             if constexpr (D == 128) {
-              // rows t, t+4, t+8, t+12 share bit 1 with t: 32-byte halves exchanged when set
-              const int off = 8 * (mg ^ ((mt4 & 2) ? 4 : 0));
-              const uint2 r0 = *reinterpret_cast<const uint2*>(vr + mt4 * 64 + off);
-              const uint2 r4 = *reinterpret_cast<const uint2*>(vr + (mt4 + 4) * 64 + off);
-              const uint2 r8 = *reinterpret_cast<const uint2*>(vr + (mt4 + 8) * 64 + off);
-              const uint2 rc = *reinterpret_cast<const uint2*>(vr + (mt4 + 12) * 64 + off);
+              // rows t, t+4, t+8, t+12 share bit 1 with t (folded into o_v)
+              const uint2 r0 = lds_v2(vr);
+              const uint2 r4 = lds_v2(vr + 4 * 64);
+              const uint2 r8 = lds_v2(vr + 8 * 64);
+              const uint2 rc = lds_v2(vr + 12 * 64);
               T0[0] = r0.x; T0[1] = r0.y; T4[0] = r4.x; T4[1] = r4.y;
               Y0[0] = r8.x; Y0[1] = r8.y; Y4[0] = rc.x; Y4[1] = rc.y;
             } else {
-              T0[0] = *reinterpret_cast<const uint32_t*>(vr + mt4 * 32 + 4 * mg);
-              T4[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 4) * 32 + 4 * mg);
-              Y0[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 8) * 32 + 4 * mg);
-              Y4[0] = *reinterpret_cast<const uint32_t*>(vr + (mt4 + 12) * 32 + 4 * mg);
+              T0[0] = lds_u32(vr);
+              T4[0] = lds_u32(vr + 4 * 32);
+              Y0[0] = lds_u32(vr + 8 * 32);
+              Y4[0] = lds_u32(vr + 12 * 32);
               T0[1] = T4[1] = Y0[1] = Y4[1] = 0u;
             }
 #pragma unroll
