@@ -33,7 +33,7 @@ struct Params {
   __half* out;       // [B, QL, H, D]
   const int32_t* bt;   // [B, MB]
   const int32_t* ctx;  // [B]
-  // INT4 pool: one page of STAGE_RAW bytes per (block, head)
+  // INT4 pool: one page of PAGE_RAW bytes per (block, head)
   const uint8_t* pages;
   // split-K workspace
   int32_t* tickets;  // [pairs]
@@ -61,19 +61,29 @@ struct Cfg {
   static constexpr int DUP = LPR / TPL; // lanes holding the same score
   static constexpr int K_BYTES = INT4 ? BS * D / 2 : BS * D * 2;
   static constexpr int S_BYTES = INT4 ? BS * (D / 64) * 2 : 0;
-  static constexpr int STAGE_RAW = 2 * K_BYTES + 2 * S_BYTES;
+  static constexpr int PAGE_RAW = 2 * K_BYTES + 2 * S_BYTES;  // one page (INT4: one (block, head) page)
+  // INT4 with 16-token pages: a stage holds two pages (the two tiles of one
+  // softmax step) behind one mbarrier, halving the per-page pipeline work.
+  static constexpr int PPS = (INT4 && BS == 16) ? 2 : 1;
+  static constexpr int STAGE_RAW = PPS * PAGE_RAW;
   static constexpr int STAGE = (STAGE_RAW + 127) / 128 * 128;
   // fp16 pages are large: 3 stages of 8 KB per warp, 2 CTAs (8 warps) per SM.
   // INT4 pages are small and their consumer is issue-latency bound: ~12 KB of
   // stages per warp and 4 CTAs (16 warps) per SM at <= 128 registers.
-  static constexpr int WARP_BUDGET = INT4 ? 12288 : 24576;
+#ifndef MEMOPT_XP_BUDGET
+#define MEMOPT_XP_BUDGET 12288
+#endif
+#ifndef MEMOPT_XP_MINB
+#define MEMOPT_XP_MINB 4
+#endif
+  static constexpr int WARP_BUDGET = INT4 ? MEMOPT_XP_BUDGET : 24576;
   static constexpr int NS_RAW = WARP_BUDGET / STAGE;
   // INT4: largest power of two that fits (the ring index is then a mask;
   // per-page integer overhead matters at 2 KB pages).  fp16: as many as fit.
   static constexpr int NS_P2 = NS_RAW >= 16 ? 16 : NS_RAW >= 8 ? 8 : NS_RAW >= 4 ? 4 : 2;
   static constexpr int NS = INT4 ? NS_P2 : (NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW));
   static constexpr int NW = 4;            // warps per CTA
-  static constexpr int MIN_BLOCKS = INT4 ? 4 : 2;
+  static constexpr int MIN_BLOCKS = INT4 ? MEMOPT_XP_MINB : 2;
   static constexpr int BAR_BYTES = 1024;  // mbarriers
   static constexpr int SMEM = BAR_BYTES + NW * NS * STAGE;
   static_assert(TPL >= 1 && DUP >= 1, "unsupported geometry");
@@ -133,18 +143,22 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     mask = __ballot_sync(0xffffffffu, ok);
   };
 
-  auto issue = [&](uint32_t seq, int phys, int h) {
+  // phys2 >= 0: a second page into the same stage (INT4, PPS == 2).
+  auto issue = [&](uint32_t seq, int phys, int phys2, int h) {
     const int s = static_cast<int>(seq % NS);
     const uint32_t bar = bar0 + 8 * s;
     const uint32_t dst = st0 + s * C::STAGE;
     fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar, C::STAGE_RAW);
     if (!INT4) {
+      mbar_arrive_expect_tx(bar, C::STAGE_RAW);
       tma_load_3d(dst, &kmap, 0, h, phys * BS, bar);
       tma_load_3d(dst + C::K_BYTES, &vmap, 0, h, phys * BS, bar);
     } else {
-      const int64_t row = static_cast<int64_t>(phys) * p.H + h;
-      bulk_g2s(dst, p.pages + row * C::STAGE_RAW, C::STAGE_RAW, bar);
+      mbar_arrive_expect_tx(bar, (C::PPS == 2 && phys2 >= 0) ? 2 * C::PAGE_RAW : C::PAGE_RAW);
+      bulk_g2s(dst, p.pages + (static_cast<int64_t>(phys) * p.H + h) * C::PAGE_RAW, C::PAGE_RAW, bar);
+      if (C::PPS == 2 && phys2 >= 0)
+        bulk_g2s(dst + C::PAGE_RAW, p.pages + (static_cast<int64_t>(phys2) * p.H + h) * C::PAGE_RAW, C::PAGE_RAW,
+                 bar);
     }
   };
 
@@ -178,7 +192,13 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     const int j = __ffs(p_mask) - 1;
     p_mask &= p_mask - 1;
     const int phys = __shfl_sync(0xffffffffu, p_phys, j);
-    if (lane == 0) issue(p_seq, phys, p_h);
+    int phys2 = -1;
+    if (C::PPS == 2 && p_mask != 0) {  // the consumer pairs pages the same way
+      const int j2 = __ffs(p_mask) - 1;
+      p_mask &= p_mask - 1;
+      phys2 = __shfl_sync(0xffffffffu, p_phys, j2);
+    }
+    if (lane == 0) issue(p_seq, phys, phys2, p_h);
     ++p_seq;
   };
 
@@ -266,6 +286,30 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     float acc[INT4 ? 2 * NKB : 1][4];
 #pragma unroll
     for (int j = 0; j < (INT4 ? 2 * NKB : 1); ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    // INT4: the V codes enter the P.V mma as 1024 + c (low nibbles) and
+    // 1024 + 16 c (high nibbles); wsum (same fragment layout) accumulates the
+    // B column sums, and every kFlushSteps steps (and at the end of the item)
+    // the offsets are removed: low -= 1032 wsum, high -= 1152 wsum (the high
+    // fragments carry 16x the value).  Bounding the span keeps the common
+    // offset in the fp32 accumulators small relative to the result.
+    float wsum[4] = {0.f, 0.f, 0.f, 0.f};
+    int since_flush = 0;
+    constexpr int kFlushSteps = 4;
+    auto flush_offsets = [&]() {
+      if constexpr (INT4) {
+#pragma unroll
+        for (int j = 0; j < NKB; ++j) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[2 * j][e] = fmaf(-1032.f, wsum[e], acc[2 * j][e]);
+            acc[2 * j + 1][e] = fmaf(-1152.f, wsum[e], acc[2 * j + 1][e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) wsum[e] = 0.f;
+        since_flush = 0;
+      }
+    };
 
     // Warp-uniform bounded wait for stage `seq` (a completed phase stays observable).
     auto wait_stage = [&](uint32_t seq) -> bool {
@@ -374,12 +418,18 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           jb = __ffs(mask) - 1;
           mask &= mask - 1;
         }
-        if (!wait_stage(c_seq) || (two_pages && !wait_stage(c_seq + 1))) {
+        if (!wait_stage(c_seq)) {
           failed = true;
           break;
         }
+#ifdef MEMOPT_XP_NOCOMPUTE
+        acc[0][0] += __uint_as_float(lds_u32(st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE + 4 * lane) & 0x3FFFFu);
+        if (false) {
+#else
+        {
+#endif
         const uint32_t sa = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
-        const uint32_t sb = two_pages ? st0 + static_cast<uint32_t>((c_seq + 1) % NS) * C::STAGE : sa;
+        const uint32_t sb = sa + C::PAGE_RAW;  // second page of the stage (BS == 16)
         const bool has2 = (BS == 32) || two_pages;
         // tile ti: stage base and the tile's index inside its page (BS == 32
         // pages hold two 16-token tiles).
@@ -412,6 +462,9 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           const float ks_lo = lds_f16_as_f32(ksa);
           const float ks_hi = lds_f16_as_f32(ksa + 16 * G);
           int c[4] = {0, 0, 0, 0};
+#ifdef MEMOPT_XP_NOSCORE
+          c[0] = w0[0] ^ w1[1]; c[1] = w0[1] ^ w1[2]; c[2] = w0[2] ^ w1[3]; c[3] = w0[3] ^ w1[0];
+#else
 #pragma unroll
           for (int kb = 0; kb < NKB; ++kb) {
             uint32_t a[4];
@@ -421,6 +474,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a[3] = s8x16_odd(w1[kb], kS8);
             mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
+#endif
           // Lanes mt4 >= G compute a value that is never used: the group sum
           // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
           float a_lo = ks_lo * static_cast<float>(c[0] * 256 + c[1]);
@@ -456,6 +510,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
 #pragma unroll
               for (int e = 0; e < 4; ++e) acc[j][e] *= alpha;
             }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) wsum[e] *= alpha;
           }
           // ---- P.V on the tensor pipe, dims as rows ----
           // A = V codes (c - 8) in fp16: rows = 16 dims of a block, k = the
@@ -497,6 +553,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               Y4[0] = lds_u32(vr + 12 * 32);
               T0[1] = T4[1] = Y0[1] = Y4[1] = 0u;
             }
+#ifdef MEMOPT_XP_NOPV
+            acc[0][0] += __uint_as_float((T0[0] ^ T4[1] ^ Y0[0] ^ Y4[1] ^ b0 ^ b1) & 0x3FFFFu);
+            if (false)
+#endif
 #pragma unroll
             for (int j = 0; j < NKB; ++j) {
               const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
@@ -504,20 +564,22 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               const uint32_t y = __byte_perm(Y0[j >> 1], Y4[j >> 1], sel);  // tokens t+8 | t+12
               const uint32_t x8 = x >> 8, y8 = y >> 8;
               uint32_t a[4];
-              a[0] = lo_pair(x, kF16); a[1] = lo_pair(x8, kF16); a[2] = lo_pair(y, kF16); a[3] = lo_pair(y8, kF16);
+              a[0] = lo_raw(x, kF16); a[1] = lo_raw(x8, kF16); a[2] = lo_raw(y, kF16); a[3] = lo_raw(y8, kF16);
               mma16816(acc[2 * j], a, b0, b1);
-              a[0] = hi_pair(x, kF16); a[1] = hi_pair(x8, kF16); a[2] = hi_pair(y, kF16); a[3] = hi_pair(y8, kF16);
+              a[0] = hi_raw(x, kF16); a[1] = hi_raw(x8, kF16); a[2] = hi_raw(y, kF16); a[3] = hi_raw(y8, kF16);
               mma16816(acc[2 * j + 1], a, b0, b1);
             }
+            {  // column sums of B: A = all ones
+              const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
+              mma16816(wsum, ones, b0, b1);
+            }
           }
+        }
+        if (++since_flush == kFlushSteps) flush_offsets();
         }
         __syncwarp();
         ++c_seq;
         produce();
-        if (two_pages) {
-          ++c_seq;
-          produce();
-        }
       }
     }
     if (failed || !more) break;
@@ -547,13 +609,15 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
     } else {
       // Lane (mg, 0) holds dims D/8 mg + [0, D/8): fragment (j, hl) row mg
       // is dim D/8 mg + 4j + hl, row mg + 8 is + 2; column = scale group.
+      flush_offsets();
       const int grp = (D / 8) * mg / 64;
 #pragma unroll
       for (int j = 0; j < NKB; ++j) {
 #pragma unroll
         for (int hl = 0; hl < 2; ++hl) {
-          ov[4 * j + hl] = grp ? acc[2 * j + hl][1] : acc[2 * j + hl][0];
-          ov[4 * j + 2 + hl] = grp ? acc[2 * j + hl][3] : acc[2 * j + hl][2];
+          const float f = hl ? 0.0625f : 1.f;  // high fragments hold 16x
+          ov[4 * j + hl] = f * (grp ? acc[2 * j + hl][1] : acc[2 * j + hl][0]);
+          ov[4 * j + 2 + hl] = f * (grp ? acc[2 * j + hl][3] : acc[2 * j + hl][2]);
         }
       }
       dbase = (D / 8) * mg;

@@ -80,6 +80,12 @@ __device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], uint32_t b
 __device__ __forceinline__ uint32_t s8x16_even(uint32_t w, uint32_t k_s8) { return and_xor(w << 4, 0xF0F0F0F0u, k_s8); }
 __device__ __forceinline__ uint32_t s8x16_odd(uint32_t w, uint32_t k_s8) { return and_xor(w, 0xF0F0F0F0u, k_s8); }
 
+// Half2 (1024 + n_a, 1024 + n_b) of the nibbles at bits [0,4) and [16,20),
+// and (1024 + 16 n_a, 1024 + 16 n_b) of those at [4,8) and [20,24): one logic
+// op each, the offsets are removed after the products.
+__device__ __forceinline__ uint32_t lo_raw(uint32_t x, uint32_t k_f16) { return and_or(x, 0x000F000Fu, k_f16); }
+__device__ __forceinline__ uint32_t hi_raw(uint32_t x, uint32_t k_f16) { return and_or(x, 0x00F000F0u, k_f16); }
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
