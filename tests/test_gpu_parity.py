@@ -261,6 +261,30 @@ def test_attention_int4_vs_oracle(case):
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("qmul,vmean,win", [(8.0, 0.0, 32768), (0.05, 0.0, 32768), (1.0, 2.5, 32768),
+                                             (4.0, -1.5, 5000)])
+def test_attention_int4_long_context_stress(qmul, vmean, win):
+    """Long rows with peaked / flat attention and V with a large common mean:
+    the INT4 P.V path folds a per-code offset out of its fp32 accumulators
+    every few steps, which these cases would expose."""
+    B, H, D, BS, L = 1, 2, 128, 16, 32768
+    MB = L // BS
+    rng = np.random.default_rng(int(qmul * 100 + vmean * 10))
+    NB = MB + 3
+    bt = rng.permutation(NB)[:MB].astype(np.int32).reshape(1, MB)
+    k = rng.standard_normal((NB * BS, H, D)).astype(np.float16)
+    v = (rng.standard_normal((NB * BS, H, D)) + vmean).astype(np.float16)
+    q = (rng.standard_normal((B, 1, H, D)) * qmul).astype(np.float16)
+    pages = torch.zeros(NB, H, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV),
+                          torch.from_numpy(np.arange(NB * BS, dtype=np.int32)).to(DEV), pages, BS)
+    cl = np.array([L], np.int32)
+    got = capi.attention_int4(torch.from_numpy(q).to(DEV), pages, BS, torch.from_numpy(bt).to(DEV),
+                              torch.from_numpy(cl).to(DEV), L, win)
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, L, win, BS)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
 def test_attention_deterministic_and_workspace_reuse():
     B, QL, H, D, BS, ctx, MB, msl, win, holes = ATTN_CASES[7]
     q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, 11, holes)
