@@ -69,21 +69,17 @@ struct Cfg {
   static constexpr int STAGE = (STAGE_RAW + 127) / 128 * 128;
   // fp16 pages are large: 3 stages of 8 KB per warp, 2 CTAs (8 warps) per SM.
   // INT4 pages are small and their consumer is issue-latency bound: ~12 KB of
-  // stages per warp and 4 CTAs (16 warps) per SM at <= 128 registers.
-#ifndef MEMOPT_XP_BUDGET
-#define MEMOPT_XP_BUDGET 12288
-#endif
-#ifndef MEMOPT_XP_MINB
-#define MEMOPT_XP_MINB 4
-#endif
-  static constexpr int WARP_BUDGET = INT4 ? MEMOPT_XP_BUDGET : 24576;
+  // stages per warp (two 2-page stages at 16-token pages) and 4 CTAs
+  // (16 warps) per SM at <= 128 registers; occupancy matters more here than
+  // ring depth (3 CTAs with four 2-page stages per warp measured slower).
+  static constexpr int WARP_BUDGET = INT4 ? 12288 : 24576;
   static constexpr int NS_RAW = WARP_BUDGET / STAGE;
   // INT4: largest power of two that fits (the ring index is then a mask;
   // per-page integer overhead matters at 2 KB pages).  fp16: as many as fit.
   static constexpr int NS_P2 = NS_RAW >= 16 ? 16 : NS_RAW >= 8 ? 8 : NS_RAW >= 4 ? 4 : 2;
   static constexpr int NS = INT4 ? NS_P2 : (NS_RAW < 2 ? 2 : (NS_RAW > 16 ? 16 : NS_RAW));
   static constexpr int NW = 4;            // warps per CTA
-  static constexpr int MIN_BLOCKS = INT4 ? MEMOPT_XP_MINB : 2;
+  static constexpr int MIN_BLOCKS = INT4 ? 4 : 2;
   static constexpr int BAR_BYTES = 1024;  // mbarriers
   static constexpr int SMEM = BAR_BYTES + NW * NS * STAGE;
   static_assert(TPL >= 1 && DUP >= 1, "unsupported geometry");
@@ -422,12 +418,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           failed = true;
           break;
         }
-#ifdef MEMOPT_XP_NOCOMPUTE
-        acc[0][0] += __uint_as_float(lds_u32(st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE + 4 * lane) & 0x3FFFFu);
-        if (false) {
-#else
         {
-#endif
         const uint32_t sa = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
         const uint32_t sb = sa + C::PAGE_RAW;  // second page of the stage (BS == 16)
         const bool has2 = (BS == 32) || two_pages;
@@ -462,9 +453,6 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           const float ks_lo = lds_f16_as_f32(ksa);
           const float ks_hi = lds_f16_as_f32(ksa + 16 * G);
           int c[4] = {0, 0, 0, 0};
-#ifdef MEMOPT_XP_NOSCORE
-          c[0] = w0[0] ^ w1[1]; c[1] = w0[1] ^ w1[2]; c[2] = w0[2] ^ w1[3]; c[3] = w0[3] ^ w1[0];
-#else
 #pragma unroll
           for (int kb = 0; kb < NKB; ++kb) {
             uint32_t a[4];
@@ -474,7 +462,6 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a[3] = s8x16_odd(w1[kb], kS8);
             mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
-#endif
           // Lanes mt4 >= G compute a value that is never used: the group sum
           // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
           float a_lo = ks_lo * static_cast<float>(c[0] * 256 + c[1]);
@@ -553,10 +540,6 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
               Y4[0] = lds_u32(vr + 12 * 32);
               T0[1] = T4[1] = Y0[1] = Y4[1] = 0u;
             }
-#ifdef MEMOPT_XP_NOPV
-            acc[0][0] += __uint_as_float((T0[0] ^ T4[1] ^ Y0[0] ^ Y4[1] ^ b0 ^ b1) & 0x3FFFFu);
-            if (false)
-#endif
 #pragma unroll
             for (int j = 0; j < NKB; ++j) {
               const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
