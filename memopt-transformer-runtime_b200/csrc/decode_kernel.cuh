@@ -470,8 +470,11 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
             a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
           }
-          a_lo = __shfl_sync(0xffffffffu, a_lo * sfac, lane & ~3);
-          a_hi = __shfl_sync(0xffffffffu, a_hi * sfac, lane & ~3);
+          // Only lanes mt4 == 0 hold the scores from here on: they are the
+          // only sources of the P.V operand and of l (other lanes' values are
+          // never read; the running max is taken from lane 0).
+          a_lo *= sfac;
+          a_hi *= sfac;
           const int tl = ttok[ti] + mg;
           const bool interior = ttok[ti] >= win_start && ttok[ti] + 16 <= ctx;
           slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
@@ -480,14 +483,15 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         float mp = fmaxf(fmaxf(slo[0], shi[0]), fmaxf(slo[1], shi[1]));
 #pragma unroll
         for (int mk = 16; mk >= 4; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
+        mp = __shfl_sync(0xffffffffu, mp, 0);
         const float m_new = fmaxf(m, mp);
         if (m_new != -INFINITY) {
-          const float alpha = exp2f(m - m_new);
+          const float alpha = ex2_approx(m - m_new);
           m = m_new;
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
-            slo[ti] = exp2f(slo[ti] - m_new);
-            shi[ti] = exp2f(shi[ti] - m_new);
+            slo[ti] = ex2_approx(slo[ti] - m_new);
+            shi[ti] = ex2_approx(shi[ti] - m_new);
           }
           const float psum = (slo[0] + shi[0]) + (slo[1] + shi[1]);
           l = l * alpha + (mt4 == 0 ? psum : 0.f);

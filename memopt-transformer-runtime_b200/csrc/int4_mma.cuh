@@ -86,6 +86,13 @@ __device__ __forceinline__ uint32_t s8x16_odd(uint32_t w, uint32_t k_s8) { retur
 __device__ __forceinline__ uint32_t lo_raw(uint32_t x, uint32_t k_f16) { return and_or(x, 0x000F000Fu, k_f16); }
 __device__ __forceinline__ uint32_t hi_raw(uint32_t x, uint32_t k_f16) { return and_or(x, 0x00F000F0u, k_f16); }
 
+// 2^x with the hardware approximation (relative error ~2^-22; -inf -> 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
