@@ -97,13 +97,19 @@ int memopt_write_cache_f16(const void* keys, const void* values,
  * kv_pages: uint8 [num_blocks, num_heads, page_bytes], one contiguous page per
  * (block, head) laid out as
  *   K codes  [block_size][head_dim/2]   (byte i of a row = q[2i] | q[2i+1] << 4)
- *   V codes  [block_size][head_dim/2]
+ *   V codes  [block_size][head_dim/2]   same bytes; for head_dim 128 byte i of
+ *                                        row pos is stored at i ^ 32 when bit 1
+ *                                        of pos is set
  *   K scales [block_size][head_dim/64]  fp16
- *   V scales [block_size][head_dim/64]  fp16
+ *   V scales [block_size/16][head_dim/64][16] fp16, token r of a 16-token tile
+ *                                        at slot 2(r&3) + ((r>>2)&1) + 8(r>>3)
  * page_bytes = memopt_int4_page_bytes(block_size, head_dim).  Groups are 64
  * consecutive head_dim elements of one (token, head); the code is computed
  * from the fp32 scale absmax/7 (1.0 for an all-zero group) and the stored
- * scale is that fp32 scale rounded to fp16.  head_dim % 64 == 0. */
+ * scale is that fp32 scale rounded to fp16.  head_dim % 64 == 0 and
+ * block_size % 16 == 0.  The V permutations serve the decode kernel's
+ * conflict-free shared-memory fragment loads; every token still owns whole
+ * 32-byte sectors of its K and V rows. */
 size_t memopt_int4_page_bytes(int block_size, int head_dim);
 int memopt_write_cache_int4(const void* keys, const void* values,
                             const int32_t* slot_mapping, int64_t num_tokens,
