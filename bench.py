@@ -221,27 +221,16 @@ def config_dict(n: int) -> dict:
 def run_ours(args) -> None:
     import torch
 
+    from memopt.sharding import RankGroup, dist_env, job_rate
+
     ws_n, rank, local = dist_env()
-    dist = None
-    if ws_n > 1:
-        import torch.distributed as dist  # noqa: F811
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
+    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    # One process, one GPU and one pool per rank; sequences are sharded (each
+    # rank runs the per-GPU workload on its own sequences: weak scaling).
+    group = RankGroup.init("nccl", dev)
+    barrier = group.barrier
+    max_over_ranks = group.max
 
     import memopt_C
     from memopt import _capi
@@ -261,8 +250,8 @@ def run_ours(args) -> None:
         ms = time_loop(torch, step, args.steps, args.warmup, barrier, stream)
     ms = max_over_ranks(ms)
     sbytes = step_bytes(B, CTX)
-    value = sbytes * ws_n / (ms * 1e-3) / 1e9
-    tokens = B * ws_n / (ms * 1e-3)
+    value = job_rate(sbytes, ms, ws_n) / 1e9
+    tokens = job_rate(B, ms, ws_n)
     peak, peak_kind = peaks()
     kernel_gbs = sbytes / (ms * 1e-3) / 1e9  # one kernel launch per step
 
@@ -302,7 +291,7 @@ def run_ours(args) -> None:
     ms_e2e = max_over_ranks(time_loop(torch, e2e_step, e2e_steps, args.warmup, barrier, stream))
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hslots, hbt, hctx))
     d2h = hout.numel() * hout.element_size()
-    e2e = sbytes * ws_n / (ms_e2e * 1e-3) / 1e9
+    e2e = job_rate(sbytes, ms_e2e, ws_n) / 1e9
 
     # ---- INT4 decode as a secondary line ---------------
     extra = {}
@@ -322,8 +311,7 @@ def run_ours(args) -> None:
                "decode_tokens_per_s": round(toks, 3)}
 
     if rank != 0:
-        if dist is not None:
-            dist.destroy_process_group()
+        group.destroy()
         return
     traffic = None
     tpath = os.path.join(REPO, "profiles", "traffic.json")
@@ -350,8 +338,7 @@ def run_ours(args) -> None:
         "extra": extra,
     }
     print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    group.destroy()
 
 
 def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
