@@ -369,7 +369,7 @@ def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_
         e1.record(stream)
         torch.cuda.synchronize()
         write_ms.append(e0.elapsed_time(e1))
-    wms = statistics.median(write_ms[1:] if len(write_ms) > 1 else write_ms)
+    wms = max_over_ranks(statistics.median(write_ms[1:] if len(write_ms) > 1 else write_ms))
     wbytes_chunk = 2 * chunk * H * D * 2 + 2 * chunk * H * (D // 2) + 2 * chunk * H * (D // 64) * 2 + chunk * 4
     q = torch.randn(b, 1, H, D, dtype=torch.float16, device=dev, generator=g)
     ctx = torch.full((b,), ctx_len, dtype=torch.int32, device=dev)
@@ -389,7 +389,7 @@ def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_
                             "frac_of_hbm_peak": round(sbytes / (ms * 1e-3) / 1e9 / peak, 4),
                             "decode_tokens_per_s": round(b * ws_n / (ms * 1e-3), 1),
                             "algorithmic_bytes_per_launch": sbytes},
-            "int4_write_cache": {"value": round(wbytes_chunk / (wms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "int4_write_cache": {"value": round(wbytes_chunk * ws_n / (wms * 1e-3) / 1e9, 2), "unit": "GB/s",
                                  "frac_of_hbm_peak": round(wbytes_chunk / (wms * 1e-3) / 1e9 / peak, 4),
                                  "tokens_per_launch": chunk, "ms_per_launch": round(wms, 5)}}
 
