@@ -34,6 +34,7 @@ B, H, D, BS, CTX = 32, 32, 128, 16, 4096
 MB = CTX // BS
 NB = B * MB  # 8192 pages
 INT4_B, INT4_CTX = 16, 16384
+LONG_B, LONG_CTX = 64, 131072  # BASELINE configs[4] decode (sharded over the ranks)
 METRIC = "paged decode attention HBM GB/s (% of peak) & decode tokens/s at 1/2/4/8 B200"
 
 
@@ -299,6 +300,7 @@ def run_ours(args) -> None:
         extra = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)
         extra.update(prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         extra.update(evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
+        extra.update(long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
 
     # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
     cpu = None
@@ -417,9 +419,62 @@ def run_only(args) -> None:
         res = evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "prefill":
         res = prefill_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
+    elif args.only == "long":
+        res = long_decode_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     else:
         res = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     print(json.dumps(res), flush=True)
+
+
+def long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """BASELINE configs[4] decode: 64 sequences x 131072 cached tokens in INT4
+    pages, the sequences sharded over the ranks (64 / N per GPU: strong
+    scaling for this line; 36.5 GB of pages on one GPU).  The pages hold
+    seeded random codes and fp16 scales in [0.05, 0.55) (the fused writer that
+    produces real pages is timed in the int4 line); decode reads every byte
+    of them either way."""
+    from memopt.sharding import shard_range
+
+    lo, hi = shard_range(LONG_B, ws_n, rank)
+    b = hi - lo
+    mb = LONG_CTX // BS
+    nb = b * mb
+    pbytes = BS * D + BS * (D // 64) * 4
+    g = torch.Generator(device=dev).manual_seed(31 + rank)
+    pages = torch.empty(nb, H, pbytes, dtype=torch.uint8, device=dev)
+    pages.random_(0, 256, generator=g)
+    sb = BS * (D // 64) * 2  # fp16 scale bytes per (page, head) for K, and again for V
+    step_pages = 65536
+    for p0 in range(0, nb, step_pages):
+        p1 = min(nb, p0 + step_pages)
+        sc = (torch.rand(p1 - p0, H, sb, device=dev, generator=g) * 0.5 + 0.05).half()
+        pages[p0:p1, :, BS * D:] = sc.view(torch.uint8).view(p1 - p0, H, 2 * sb)
+        del sc
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(41 + rank)).to(torch.int32).reshape(b, mb).to(dev)
+    q = torch.randn(b, 1, H, D, dtype=torch.float16, device=dev, generator=g)
+    ctx = torch.full((b,), LONG_CTX, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    wsb = _capi.workspace_size(b, 1, H, D, mb, BS, LONG_CTX, LONG_CTX)
+    wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+    def step():
+        _capi.paged_attention_int4(q, pages, BS, bt, ctx, out, LONG_CTX, LONG_CTX, wsp, wsb, sp)
+
+    steps = min(max(args.steps // 50, 10), 40)
+    ms = max_over_ranks(time_loop(torch, step, steps, min(args.warmup, 5), barrier, stream))
+    sbytes_rank = step_bytes(b, LONG_CTX, "int4")
+    total = step_bytes(LONG_B, LONG_CTX, "int4")
+    peak, _ = peaks()
+    del pages
+    torch.cuda.empty_cache()
+    return {"long_context_decode": {
+        "workload": f"BASELINE configs[4] decode: 64 x 131072 tokens INT4, {b} sequences on this GPU "
+                    f"(sequences sharded over {ws_n} GPU(s): strong scaling)",
+        "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "frac_of_hbm_peak_per_gpu": round(sbytes_rank / (ms * 1e-3) / 1e9 / peak, 4),
+        "decode_tokens_per_s": round(LONG_B / (ms * 1e-3), 1), "steps": steps,
+        "scaling": "strong", "bytes_per_step_whole_job": total,
+        "data": "seeded random INT4 codes and fp16 scales in [0.05, 0.55)"}}
 
 
 def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
@@ -519,7 +574,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
-    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict"], help="time one kernel family alone (profiling)")
+    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict", "long"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
