@@ -45,12 +45,38 @@ __device__ __forceinline__ uint32_t int4_code(float x, float scale) {
   return static_cast<uint32_t>(min(max(iq, 0), 15));
 }
 
+// The same code without an IEEE division per element.  With scale =
+// absmax / 7, |x / scale| is at most 7 plus rounding, and roundf(x / scale)
+// = sign(q) floor(|q| + 1/2) can differ from the value computed from
+// q' = x * rcp(scale) (a few ulp of 8 away, < 3e-6) only when |q'| + 1/2 is
+// within 1.6e-5 of an integer; those elements take the exact quotient.  The
+// result is bit-identical to int4_code, NaN and inf included (NaN -> 8; the
+// saturated conversion of an infinite quotient wraps and clamps to 0 in
+// both).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t int4_code_fast(float x, float scale, float rinv) {
+  const float q = x * rinv;
+  const float t = fabsf(q) + 0.5f;
+  float k = floorf(t);
+  const float fr = t - k;
+  // (also catches |q| + 1/2 rounding up to an integer, where floor would be off)
+  if (fr < 1.6e-5f || fr > 1.f - 1.6e-5f) k = fabsf(roundf(x / scale));
+  const int ik = static_cast<int>(k);
+  const int iq = (q < 0.f ? -ik : ik) + 8;
+  return static_cast<uint32_t>(min(max(iq, 0), 15));
+}
+
 // Eight consecutive codes packed into one little-endian word: nibble j holds
 // element j, so byte k = q[2k] | q[2k+1] << 4 as in the reference.
 __device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
+  const float rinv = rcp_approx(scale);
   uint32_t w = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
+  for (int j = 0; j < 8; ++j) w |= int4_code_fast(f[j], scale, rinv) << (4 * j);
   return w;
 }
 
