@@ -7,21 +7,25 @@
 // all rows of a sequence share one key set and the work is a dense
 // non-causal attention per (sequence, head).
 //
-// One CTA = (128-query tile, head, sequence), one warpgroup:
-//   * Q tile [128 x D] and, per step, a K/V block of 128 tokens (128/BS
-//     pages) are staged by TMA (3-D tensor maps over the query tensor and the
-//     fp16 pool, 128-byte swizzle, no multicast) into 1024-B aligned smem;
-//     K/V blocks are double-buffered;
-//   * thread 0 issues S = Q K^T (M=128, N=128, K=D) into TMEM columns
-//     [0,128), then O += P V (M=128, N=D, K=128 tokens; V is the MN-major
-//     operand) into TMEM columns [128, 128+D); completion is tracked with
-//     tcgen05.commit on mbarriers;
-//   * each thread owns one query row (TMEM lane): it loads its S row with
-//     tcgen05.ld, masks, runs the online softmax in the log2 domain, writes
-//     P (fp16) to smem in the swizzled K-major layout, and rescales its O row
-//     in TMEM only when its running max grows by more than 2^8 (stale maxima
-//     below that bound keep P <= 256, exact enough in fp16);
-//   * the epilogue divides O by the row sum and stores fp16 rows.
+// One CTA = (two 128-query tiles, head, sequence); keys are consumed in blocks
+// of 64 tokens (64/BS pages) shared by both tiles.
+//   * warp 8 stages Q once and K/V blocks by TMA (3-D tensor maps over the
+//     query tensor and the fp16 pool, 128-byte swizzle, no multicast) into
+//     rings of 3 K and 2 V stages, and its lane 0 issues the tcgen05.mma
+//     instructions: per tile, S(j) = Q K(j)^T (M=128, N=64, K=D) into one of
+//     two TMEM score buffers and O += P(j) V(j) (M=128, N=D, K=64; V is the
+//     MN-major operand) into the tile's O columns;
+//   * warps 0-3 (tile 0) and 4-7 (tile 1) run the softmax, one thread per
+//     query row (= TMEM lane): it loads its 64 scores with tcgen05.ld,
+//     releases the score buffer, runs the online softmax in the log2 domain,
+//     writes P (fp16) into one of the tile's two shared-memory P buffers
+//     (K-major, 128-byte swizzle) and rescales its O row in TMEM only when
+//     its running max grows by more than 2^8 (stale maxima below that bound
+//     keep P <= 256, exact enough in fp16).
+// With two score and two P buffers per tile, S(j+2) and P.V(j) run on the
+// tensor pipe while the softmax works on block j+1, and the two tiles'
+// softmax warps interleave on every SM sub-partition; no CTA-wide barrier is
+// taken per block.  The epilogue divides O by the row sum and stores fp16.
 // Pages that are skipped (entry < 0 or >= num_blocks) are zero-filled in smem
 // and masked; every mbarrier wait is bounded and reports through `err`.
 #include <cmath>
@@ -45,23 +49,35 @@ struct Params {
   float qscale;  // log2(e) / sqrt(D)
 };
 
-constexpr int kTileBytes = 128 * 128;  // 128 rows x 128 B (one 64-wide half)
-constexpr int kBtCache = 4096;         // block-table entries cached in smem per CTA
+constexpr int kBN = 64;                // key tokens per block
+constexpr int kTiles = 2;              // 128-row query tiles per CTA
+constexpr int kRows = 128 * kTiles;    // query rows per CTA
+constexpr int kBtCache = 1024;         // block-table entries cached in smem per CTA
+constexpr int kNSK = 3, kNSV = 2;      // K and V ring depths
+constexpr int kSoftmaxWarps = 4 * kTiles;
+constexpr int kMmaWarp = kSoftmaxWarps, kLoadWarp = kSoftmaxWarps + 1;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);  // + MMA warp + TMA load warp
 
 template <int D, int BS>
 struct Cfg {
   static constexpr int HALVES = D / 64;
-  static constexpr int PPB = 128 / BS;                 // pages per 128-token block
-  static constexpr int TILE = HALVES * kTileBytes;     // one 128-row tile (Q, K or V)
+  static constexpr int PPB = kBN / BS;                 // pages per block
+  static constexpr int Q_HALF = 128 * 128;             // 128 rows x 128 B
+  static constexpr int KV_HALF = kBN * 128;            // 64 rows x 128 B
+  static constexpr int Q_TILE = HALVES * Q_HALF;
+  static constexpr int KV_STAGE = HALVES * KV_HALF;
+  static constexpr int P_BUF = 128 * 128;              // 128 rows x 64 tokens fp16
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE;                   // K ring: 2 tiles
-  static constexpr int V_OFF = K_OFF + 2 * TILE;       // V ring: 2 tiles
-  static constexpr int P_OFF = V_OFF + 2 * TILE;       // P: 128 rows x 128 tokens fp16
-  static constexpr int BT_OFF = P_OFF + 2 * kTileBytes;  // block-table window (kBtCache entries)
-  static constexpr int SMEM = BT_OFF + 4 * 4096 + 1024;     // + alignment slack
+  static constexpr int K_OFF = Q_OFF + kTiles * Q_TILE;
+  static constexpr int V_OFF = K_OFF + kNSK * KV_STAGE;
+  static constexpr int P_OFF = V_OFF + kNSV * KV_STAGE;  // [tile][buffer]
+  static constexpr int BT_OFF = P_OFF + kTiles * 2 * P_BUF;
+  static constexpr int SMEM = BT_OFF + 4 * kBtCache + 1024;  // + alignment slack
   static constexpr uint32_t PAGE_TX = 1u * HALVES * BS * 128u;  // bytes of one page of K (or V)
-  static constexpr uint32_t IDESC_S = tc::idesc_f16(128, 128, false, false);
+  static constexpr uint32_t IDESC_S = tc::idesc_f16(128, kBN, false, false);
   static constexpr uint32_t IDESC_PV = tc::idesc_f16(128, D, false, true);
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(kTiles * (2 * kBN + D) <= 512, "tensor memory columns");
 };
 
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
@@ -72,14 +88,28 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
   return true;
 }
 
-// Warp-specialised: warps 0-7 run the softmax, two threads per query row
-// (warp w handles row 32*(w%4)+lane, score columns [64*(w/4), +64) and O
-// columns [(D/2)*(w/4), +D/2)); warp 8 stages Q/K/V with TMA and issues the
-// MMAs.  Barriers: 0 = Q, 1..2 = K ring, 3..4 = V ring, 6 = S(j) done
-// (commit), 7 = P.V(j) done (commit), 8 = S(j) read out of TMEM (8 arrivals,
-// one per softmax warp), 9 = P(j) written and O rescaled (8 arrivals).
-constexpr int kThreads = 288;
-constexpr int kSoftmaxWarps = 8;
+// Barriers (index: role):
+//   0 Q staged (tx) | 1..3 K stage full (tx) | 4..5 V stage full (tx)
+//   6..8 K stage free (commit after both tiles' S) | 9..10 V stage free
+//   (commit after both tiles' P.V) | per tile t at 11 + 8t: +0..1 S buffer
+//   full (commit), +2..3 S buffer read (4 softmax warps), +4..5 P buffer full
+//   (4 softmax warps), +6..7 P.V done, P buffer free (commit).
+// Block j uses K stage j % 3, V stage j % 2, S and P buffers j % 2; a waiter
+// never lags a barrier by two phases (each next phase needs an action of the
+// waiter itself first).
+constexpr int kBars = 11 + 8 * kTiles;
+
+#ifdef MEMOPT_PF_TRACE
+__device__ unsigned long long g_pf_trace[8][512];
+#define PF_TRACE(ev, j)                                                                   \
+  do {                                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 512) g_pf_trace[ev][(j)] = clock64(); \
+  } while (0)
+#else
+#define PF_TRACE(ev, j) \
+  do {                  \
+  } while (0)
+#endif
 
 template <int D, int BS>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -88,20 +118,26 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
                int32_t* __restrict__ err) {
   using C = Cfg<D, BS>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[10];
+  __shared__ __align__(8) uint64_t bars[kBars];
   __shared__ uint32_t tmem_slot;
   __shared__ int fail_flag;
-  __shared__ float red_max[2][2][128];  // [block parity][half][row]
-  __shared__ float red_sum[2][128];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(base);
-  const uint32_t sQ = sbase + C::Q_OFF, sP = sbase + C::P_OFF;
   auto bar_at = [&](int i) { return smem_u32(&bars[i]); };
-  const uint32_t bar_q = bar_at(0), bar_s = bar_at(6), bar_o = bar_at(7), bar_sfree = bar_at(8),
-                 bar_pready = bar_at(9);
+  auto bar_kfull = [&](int j) { return bar_at(1 + j % kNSK); };
+  auto bar_vfull = [&](int j) { return bar_at(4 + j % kNSV); };
+  auto bar_kfree = [&](int j) { return bar_at(6 + j % kNSK); };
+  auto bar_vfree = [&](int j) { return bar_at(9 + j % kNSV); };
+  auto bar_sfull = [&](int t, int j) { return bar_at(11 + 8 * t + (j & 1)); };
+  auto bar_sfree = [&](int t, int j) { return bar_at(13 + 8 * t + (j & 1)); };
+  auto bar_pfull = [&](int t, int j) { return bar_at(15 + 8 * t + (j & 1)); };
+  auto bar_pfree = [&](int t, int j) { return bar_at(17 + 8 * t + (j & 1)); };
+  auto ph_k = [](int j) { return static_cast<uint32_t>((j / kNSK) & 1); };
+  auto ph_v = [](int j) { return static_cast<uint32_t>((j / kNSV) & 1); };
+  auto ph_2 = [](int j) { return static_cast<uint32_t>((j >> 1) & 1); };
 
   const int ctx = __ldg(p.ctx + b);
   const int ws = (p.window < ctx) ? (ctx - p.window) : 0;
@@ -110,24 +146,29 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   const int nblocks = p_hi > p_lo ? (p_hi - p_lo + C::PPB - 1) / C::PPB : 0;
 
   if (tid == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(bar_at(i), 1);
-    mbar_init(bar_sfree, kSoftmaxWarps);
-    mbar_init(bar_pready, kSoftmaxWarps);
+    for (int i = 0; i < 11; ++i) mbar_init(bar_at(i), 1);
+    for (int t = 0; t < kTiles; ++t) {
+      for (int i = 0; i < 2; ++i) mbar_init(bar_at(11 + 8 * t + i), 1);
+      for (int i = 2; i < 6; ++i) mbar_init(bar_at(11 + 8 * t + i), 4);
+      for (int i = 6; i < 8; ++i) mbar_init(bar_at(11 + 8 * t + i), 1);
+    }
     fence_mbar_init();
     fail_flag = 0;
   }
   if (warp == 0) {
-    tc::tmem_alloc(smem_u32(&tmem_slot), 256);
+    tc::tmem_alloc(smem_u32(&tmem_slot), 512);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  // Tile t: score buffers at columns 256 t + {0, 64}, O at 256 t + 128.
+  auto tS = [&](int t, int j) { return tmem + 256u * t + (j & 1) * kBN; };
+  auto tO = [&](int t) { return tmem + 256u * t + 128u; };
 
   // The pages of this sequence's window are read once into smem (when they
-  // fit), so per-block validity checks never wait on global memory.
+  // fit), so per-block validity checks rarely wait on global memory.
   int32_t* s_bt = reinterpret_cast<int32_t*>(base + C::BT_OFF);
   const int npages = p_hi > p_lo ? p_hi - p_lo : 0;
   const bool bt_cached = npages <= kBtCache;
@@ -146,18 +187,17 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     return __ballot_sync(0xffffffffu, ok);
   };
 
-  if (warp == kSoftmaxWarps) {
-    // =========================== producer warp ===========================
+  if (warp == kLoadWarp) {
+    // ============================ TMA load warp ============================
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
-    // Stage the K (is_v = false) or V pages of block j, zero-filling skipped pages.
+    // Stage K (is_v = false) or V of block j, zero-filling skipped pages.
     auto stage = [&](int j, bool is_v) {
-      const int slot = j & 1;
-      const uint32_t bar = is_v ? bar_at(3 + slot) : bar_at(1 + slot);
-      const int off = (is_v ? C::V_OFF : C::K_OFF) + slot * C::TILE;
+      const uint32_t bar = is_v ? bar_vfull(j) : bar_kfull(j);
+      const int off = is_v ? C::V_OFF + (j % kNSV) * C::KV_STAGE : C::K_OFF + (j % kNSK) * C::KV_STAGE;
       int phys;
       const uint32_t mask = page_bits(j, phys);
       const uint32_t bad = ~mask & ((1u << C::PPB) - 1u);
@@ -165,7 +205,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         for (int pg = 0; pg < C::PPB; ++pg) {
           if (!((bad >> pg) & 1u)) continue;
           for (int hh = 0; hh < C::HALVES; ++hh) {
-            uint4* dst = reinterpret_cast<uint4*>(base + off + hh * kTileBytes + pg * BS * 128);
+            uint4* dst = reinterpret_cast<uint4*>(base + off + hh * C::KV_HALF + pg * BS * 128);
             for (int c = lane; c < BS * 8; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
           }
         }
@@ -176,136 +216,145 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       __syncwarp();  // the transaction count is armed before any copy can land
       if ((mask >> lane) & 1u) {
         for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sbase + off + hh * kTileBytes + lane * BS * 128, is_v ? &vmap : &kmap, hh * 64, h,
+          tma_load_3d(sbase + off + hh * C::KV_HALF + lane * BS * 128, is_v ? &vmap : &kmap, hh * 64, h,
                       phys * BS, bar);
       }
     };
-    auto issue_s = [&](int j) {
-      const uint32_t sK = sbase + C::K_OFF + (j & 1) * C::TILE;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk / 4) * kTileBytes + (kk % 4) * 32;
-        tc::mma_f16(tS, tc::sdesc_sw128(sQ + off, 16, 1024), tc::sdesc_sw128(sK + off, 16, 1024), C::IDESC_S,
-                    kk > 0);
-      }
-      tc::commit(bar_s);
-    };
-    auto issue_pv = [&](int j) {
-      const uint32_t sV = sbase + C::V_OFF + (j & 1) * C::TILE;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
-        tc::mma_f16(tO, tc::sdesc_sw128(sP + aoff, 16, 1024), tc::sdesc_sw128(sV + kk * 2048, kTileBytes, 1024),
-                    C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-      }
-      tc::commit(bar_o);
-    };
     bool ok = true;
-    if (nblocks > 0) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar_q, C::TILE);
+    if (nblocks > 0 && lane == 0) {
+      mbar_arrive_expect_tx(bar_at(0), kTiles * C::Q_TILE);
+      for (int t = 0; t < kTiles; ++t)
         for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sQ + hh * kTileBytes, &qmap, hh * 64, h, b * p.QL + qt * 128, bar_q);
-      }
-      stage(0, false);
-      stage(0, true);
-      if (nblocks > 1) {
-        stage(1, false);
-        stage(1, true);
-      }
-      if (lane == 0) {
-        ok = wait_bar(bar_q, 0) && wait_bar(bar_at(1), 0);
-        if (ok) {
-          tc::fence_after_sync();
-          issue_s(0);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+          tma_load_3d(sbase + C::Q_OFF + t * C::Q_TILE + hh * C::Q_HALF, &qmap, hh * 64, h,
+                      b * p.QL + qt * kRows + t * 128, bar_at(0));
     }
     for (int j = 0; j < nblocks && ok; ++j) {
-      if (j + 1 < nblocks) {
-        // S(j+1) needs S(j) read out of TMEM and K(j+1) staged.
-        if (lane == 0) {
-          ok = wait_bar(bar_sfree, j & 1) && wait_bar(bar_at(1 + ((j + 1) & 1)), ((j + 1) >> 1) & 1);
-          if (ok) {
-            tc::fence_after_sync();
-            issue_s(j + 1);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (j + 2 < nblocks) stage(j + 2, false);  // S(j) has completed: K slot j & 1 is free
-      }
-      // P.V(j) needs P(j) written (which implies P.V(j-1) completed) and V(j) staged.
-      if (lane == 0) {
-        ok = wait_bar(bar_pready, j & 1) && wait_bar(bar_at(3 + (j & 1)), (j >> 1) & 1);
-        if (ok) {
-          tc::fence_after_sync();
-          issue_pv(j);
-        }
-      }
+      // K stage j % 3 is free once both tiles' S(j-3) completed.
+      if (j >= kNSK && lane == 0) ok = wait_bar(bar_kfree(j - kNSK), ph_k(j - kNSK));
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
-      // P(j) ready implies P.V(j-1) completed: V slot (j+1)&1 is free for block j+1.
-      if (j >= 1 && j + 1 < nblocks) stage(j + 1, true);
+      stage(j, false);
+      if (lane == 0) PF_TRACE(3, j);
+      // V stage j % 2 is free once both tiles' P.V(j-2) completed.
+      if (j >= kNSV && lane == 0) ok = wait_bar(bar_vfree(j - kNSV), ph_v(j - kNSV));
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      stage(j, true);
+      if (lane == 0) PF_TRACE(2, j);
     }
     if (!ok && lane == 0) fail_flag = 1;
+  } else if (warp == kMmaWarp) {
+    // ============================== MMA warp ==============================
+    // Descriptors are built once; a k-step or stage advances the 14-bit start
+    // address field by (byte offset >> 4) (all offsets stay below 256 KB).
+    bool ok = true;
+    if (lane == 0 && nblocks > 0) {
+      uint64_t dq[kTiles];
+#pragma unroll
+      for (int t = 0; t < kTiles; ++t) dq[t] = tc::sdesc_sw128(sbase + C::Q_OFF + t * C::Q_TILE, 16, 1024);
+      const uint64_t dk0 = tc::sdesc_sw128(sbase + C::K_OFF, 16, 1024);
+      const uint64_t dv0 = tc::sdesc_sw128(sbase + C::V_OFF, C::KV_HALF, 1024);
+      const uint64_t dp0 = tc::sdesc_sw128(sbase + C::P_OFF, 16, 1024);
+      auto issue_s = [&](int t, int j) {
+        const uint64_t dk = dk0 + static_cast<uint64_t>(((j % kNSK) * C::KV_STAGE) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          tc::mma_f16(tS(t, j), dq[t] + static_cast<uint64_t>(((kk / 4) * C::Q_HALF + (kk % 4) * 32) >> 4),
+                      dk + static_cast<uint64_t>(((kk / 4) * C::KV_HALF + (kk % 4) * 32) >> 4), C::IDESC_S, kk > 0);
+        }
+        tc::commit(bar_sfull(t, j));
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint64_t dv = dv0 + static_cast<uint64_t>(((j % kNSV) * C::KV_STAGE) >> 4);
+        const uint64_t dp = dp0 + static_cast<uint64_t>(((t * 2 + (j & 1)) * C::P_BUF) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          tc::mma_f16(tO(t), dp + static_cast<uint64_t>((kk * 32) >> 4), dv + static_cast<uint64_t>((kk * 2048) >> 4),
+                      C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(bar_pfree(t, j));
+      };
+      // S(j) of both tiles into score buffer j % 2, the K stage released after.
+      auto issue_s_both = [&](int j) -> bool {
+        if (!wait_bar(bar_kfull(j), ph_k(j))) return false;
+        for (int t = 0; t < kTiles; ++t) {
+          if (j >= 2 && !wait_bar(bar_sfree(t, j - 2), ph_2(j - 2))) return false;  // buffer read
+          tc::fence_after_sync();
+          issue_s(t, j);
+        }
+        tc::commit(bar_kfree(j));
+        PF_TRACE(1, j);
+        return true;
+      };
+      ok = wait_bar(bar_at(0), 0);
+      if (ok) ok = issue_s_both(0);
+      if (ok && nblocks > 1) ok = issue_s_both(1);
+      for (int j = 0; j < nblocks && ok; ++j) {
+        ok = wait_bar(bar_vfull(j), ph_v(j));
+        for (int t = 0; t < kTiles && ok; ++t) {
+          ok = wait_bar(bar_pfull(t, j), ph_2(j));
+          if (ok) {
+            tc::fence_after_sync();
+            issue_pv(t, j);
+          }
+        }
+        if (!ok) break;
+        tc::commit(bar_vfree(j));
+        PF_TRACE(0, j);
+        if (j + 2 < nblocks) ok = issue_s_both(j + 2);
+      }
+      if (!ok) fail_flag = 1;
+    }
+    __syncwarp();
   } else {
     // =========================== softmax warps ===========================
-    const int row = (warp & 3) * 32 + lane;  // query row = TMEM lane
-    const int hf = warp >> 2;                // which half of the columns
+    const int t = warp >> 2;                 // query tile
+    const int row = (warp & 3) * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    auto sync_softmax = [] { asm volatile("bar.sync 1, 256;" ::: "memory"); };
+    const uint32_t sProw = sbase + C::P_OFF + t * 2 * C::P_BUF + row * 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    // Every softmax thread runs the same number of iterations (named barrier
-    // below); failures are published in fail_flag and read after the barrier.
-    for (int j = 0; j < nblocks; ++j) {
-      ok = wait_bar(bar_s, j & 1);
+    for (int j = 0; j < nblocks && ok; ++j) {
+      ok = wait_bar(bar_sfull(t, j), ph_2(j));
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (tid == 0) PF_TRACE(4, j);
+      if (tid == 128) PF_TRACE(7, j);
       tc::fence_after_sync();
-      float s[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      float s[kBN];
+      {
         float v[32];
-        tc::ld32(tS + lane_base + hf * 64 + c * 32, v);
+        tc::ld32(tS(t, j) + lane_base, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+        for (int i = 0; i < 32; ++i) s[i] = v[i];
+        tc::ld32(tS(t, j) + lane_base + 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 + i] = v[i];
       }
       tc::wait_ld();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_sfree);
-      ok = __all_sync(0xffffffffu, ok);
+      if (lane == 0) mbar_arrive(bar_sfree(t, j));
       int phys_unused;
       const uint32_t mask = page_bits(j, phys_unused);
-      const int tok0 = (p_lo + j * C::PPB) * BS + hf * 64;
-      const uint32_t hmask = (mask >> (hf * 64 / BS)) & ((1u << (64 / BS)) - 1u);
-      const bool edge = hmask != ((1u << (64 / BS)) - 1u) || tok0 < ws || tok0 + 64 > ctx;
-      float mx = -INFINITY;
+      const int tok0 = (p_lo + j * C::PPB) * BS;
+      const bool edge = mask != ((1u << C::PPB) - 1u) || tok0 < ws || tok0 + kBN > ctx;
       if (edge) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int t = tok0 + i;
-          const bool valid = ((hmask >> (i / BS)) & 1u) && t >= ws && t < ctx;
-          s[i] = valid ? s[i] * p.qscale : -INFINITY;
-          mx = fmaxf(mx, s[i]);
+        for (int i = 0; i < kBN; ++i) {
+          const int tk = tok0 + i;
+          const bool valid = ((mask >> (i / BS)) & 1u) && tk >= ws && tk < ctx;
+          s[i] = valid ? s[i] : -INFINITY;
         }
-      } else {
+      }
+      float mxp[8];  // eight independent partial maxima (short dependency chains)
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          s[i] *= p.qscale;
-          mx = fmaxf(mx, s[i]);
-        }
-      }
-      // Row max over both halves (the two threads of a row reach the same decision).
-      red_max[j & 1][hf][row] = mx;
-      if (!ok) fail_flag = 1;
-      sync_softmax();
-      if (fail_flag) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(red_max[j & 1][0][row], red_max[j & 1][1][row]);
+      for (int k = 0; k < 8; ++k) mxp[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < kBN; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], s[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      mx *= p.qscale;  // qscale > 0: the max of the scaled scores
       const float m_new = fmaxf(m_run, mx);
       float m_use = m_run, alpha = 1.f;
       bool rescale = false;
@@ -317,26 +366,30 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         rescale = true;
       }
       const float msub = (m_use == -INFINITY) ? 0.f : m_use;  // all-masked rows: every p = ex2(-inf) = 0
-      float psum = 0.f;
-      uint32_t ph[32];
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t ph[kBN / 2];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = tc::ex2(s[2 * i] - msub);
-        const float p1 = tc::ex2(s[2 * i + 1] - msub);
-        psum += p0 + p1;
+      for (int i = 0; i < kBN / 2; ++i) {
+        const float p0 = tc::ex2(fmaf(s[2 * i], p.qscale, -msub));
+        const float p1 = tc::ex2(fmaf(s[2 * i + 1], p.qscale, -msub));
+        ps[i & 7] += p0 + p1;
         const __half2 hv = __floats2half2_rn(p0, p1);
         ph[i] = *reinterpret_cast<const uint32_t*>(&hv);
       }
-      l_run = l_run * alpha + psum;  // partial row sum of this half
+      const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      l_run = l_run * alpha + psum;
       m_run = m_use;
-      // P.V(j-1) must be done before P and the O rows are touched.
-      if (j > 0 && !wait_bar(bar_o, (j - 1) & 1)) fail_flag = 1;  // seen at the next barrier
-      tc::fence_after_sync();
+      // P buffer j % 2 was last read by P.V(j-2).
+      if (tid == 0) PF_TRACE(6, j);
+      if (j >= 2) ok = wait_bar(bar_pfree(t, j - 2), ph_2(j - 2));
       if (__any_sync(0xffffffffu, rescale)) {
+        // O holds P.V up to block j-1 only after P.V(j-1) completed.
+        if (j >= 1 && ok) ok = wait_bar(bar_pfree(t, j - 1), ph_2(j - 1));
+        tc::fence_after_sync();
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           float v[32];
-          const uint32_t col = tO + lane_base + hf * (D / 2) + c * 32;
+          const uint32_t col = tO(t) + lane_base + c * 32;
           tc::ld32(col, v);
           tc::wait_ld();
 #pragma unroll
@@ -345,34 +398,35 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         }
         tc::wait_st();
       }
-      // This half's 64 P values -> smem half hf, K-major with 128-byte swizzle.
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      // 64 P values -> P buffer j % 2 of the tile, K-major with 128-byte swizzle.
+      const uint32_t dst0 = sProw + (j & 1) * C::P_BUF;
 #pragma unroll
       for (int chunk = 0; chunk < 8; ++chunk) {
-        uint8_t* dst = base + C::P_OFF + hf * kTileBytes + row * 128 + ((chunk ^ (row & 7)) * 16);
-        *reinterpret_cast<uint4*>(dst) =
-            make_uint4(ph[4 * chunk], ph[4 * chunk + 1], ph[4 * chunk + 2], ph[4 * chunk + 3]);
+        const uint32_t dst = dst0 + ((chunk ^ (row & 7)) * 16);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(ph[4 * chunk]), "r"(ph[4 * chunk + 1]),
+                     "r"(ph[4 * chunk + 2]), "r"(ph[4 * chunk + 3])
+                     : "memory");
       }
       fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_pready);
+      if (lane == 0) mbar_arrive(bar_pfull(t, j));
+      if (tid == 0) PF_TRACE(5, j);
     }
     // ---- epilogue ------------------------------------------------------------
-    red_sum[hf][row] = l_run;
-    sync_softmax();
-    ok = ok && !fail_flag;
-    const float l_tot = red_sum[0][row] + red_sum[1][row];
-    const int qi = qt * 128 + row;
-    __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D + hf * (D / 2);
-    if (nblocks > 0 && ok) ok = wait_bar(bar_o, (nblocks - 1) & 1);
+    const int qi = qt * kRows + t * 128 + row;
+    __half* orow = p.out + ((static_cast<int64_t>(b) * p.QL + qi) * p.H + h) * D;
+    if (nblocks > 0 && ok) ok = wait_bar(bar_pfree(t, nblocks - 1), ph_2(nblocks - 1));
     ok = __all_sync(0xffffffffu, ok);
     tc::fence_after_sync();
     if (nblocks > 0 && ok) {
-      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         float v[32];
-        tc::ld32(tO + lane_base + hf * (D / 2) + c * 32, v);
+        tc::ld32(tO(t) + lane_base + c * 32, v);
         tc::wait_ld();
         if (qi < p.QL) {
 #pragma unroll
@@ -388,14 +442,14 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
     } else if (qi < p.QL) {
       // No visible token (or a failed wait): zero row, as attention.cu:334 does for l == 0.
-      for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
     }
     if (!ok && lane == 0) fail_flag = 1;
   }
   tc::fence_before_sync();
   __syncthreads();
   if (fail_flag && tid == 0 && err) atomicExch(err, 2);
-  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
 }  // namespace prefill
@@ -446,13 +500,19 @@ int launch_prefill(const prefill::Params& p, const void* query, const void* kpoo
   auto kern = prefill::prefill_kernel<D, BS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
-  const dim3 grid((p.QL + 127) / 128, p.H, p.B);
+  const dim3 grid((p.QL + prefill::kRows - 1) / prefill::kRows, p.H, p.B);
   kern<<<grid, prefill::kThreads, C::SMEM, s>>>(p, qm, km, vm, nullptr);
   MEMOPT_LAUNCH_CHECK("prefill_kernel launch");
   return MEMOPT_OK;
 }
 
 }  // namespace
+
+#ifdef MEMOPT_PF_TRACE
+extern "C" __attribute__((visibility("default"))) int memopt_prefill_trace(unsigned long long* host) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, prefill::g_pf_trace, sizeof(prefill::g_pf_trace)));
+}
+#endif
 
 // Called by memopt_paged_attention_f16 for q_len >= kPrefillMinRows.
 int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,
