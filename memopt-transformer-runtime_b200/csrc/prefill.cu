@@ -55,8 +55,8 @@ constexpr int kRows = 128 * kTiles;    // query rows per CTA
 constexpr int kBtCache = 1024;         // block-table entries cached in smem per CTA
 constexpr int kNSK = 3, kNSV = 2;      // K and V ring depths
 constexpr int kSoftmaxWarps = 4 * kTiles;
-constexpr int kMmaWarp = kSoftmaxWarps, kLoadWarp = kSoftmaxWarps + 1;
-constexpr int kThreads = 32 * (kSoftmaxWarps + 2);  // + MMA warp + TMA load warp
+constexpr int kMmaWarp = kSoftmaxWarps, kLoadKWarp = kSoftmaxWarps + 1, kLoadVWarp = kSoftmaxWarps + 2;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 3);  // + MMA warp + K and V load warps
 
 template <int D, int BS>
 struct Cfg {
@@ -187,15 +187,17 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     return __ballot_sync(0xffffffffu, ok);
   };
 
-  if (warp == kLoadWarp) {
-    // ============================ TMA load warp ============================
+  if (warp == kLoadKWarp || warp == kLoadVWarp) {
+    // ======================= TMA load warps (K, V) =======================
+    // K and V are staged by separate warps so that a K stage never waits
+    // behind the release of a V stage (and the reverse).
+    const bool is_v = warp == kLoadVWarp;
     if (lane == 0) {
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
+      prefetch_tensormap(is_v ? &vmap : &kmap);
+      if (!is_v) prefetch_tensormap(&qmap);
     }
-    // Stage K (is_v = false) or V of block j, zero-filling skipped pages.
-    auto stage = [&](int j, bool is_v) {
+    // Stage K or V of block j, zero-filling skipped pages.
+    auto stage = [&](int j) {
       const uint32_t bar = is_v ? bar_vfull(j) : bar_kfull(j);
       const int off = is_v ? C::V_OFF + (j % kNSV) * C::KV_STAGE : C::K_OFF + (j % kNSK) * C::KV_STAGE;
       int phys;
@@ -221,26 +223,23 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
     };
     bool ok = true;
-    if (nblocks > 0 && lane == 0) {
+    if (!is_v && nblocks > 0 && lane == 0) {
       mbar_arrive_expect_tx(bar_at(0), kTiles * C::Q_TILE);
       for (int t = 0; t < kTiles; ++t)
         for (int hh = 0; hh < C::HALVES; ++hh)
           tma_load_3d(sbase + C::Q_OFF + t * C::Q_TILE + hh * C::Q_HALF, &qmap, hh * 64, h,
                       b * p.QL + qt * kRows + t * 128, bar_at(0));
     }
+    const int depth = is_v ? kNSV : kNSK;
     for (int j = 0; j < nblocks && ok; ++j) {
-      // K stage j % 3 is free once both tiles' S(j-3) completed.
-      if (j >= kNSK && lane == 0) ok = wait_bar(bar_kfree(j - kNSK), ph_k(j - kNSK));
+      // The stage of block j is free once both tiles' S(j-3) (K) or
+      // P.V(j-2) (V) completed.
+      if (j >= depth && lane == 0)
+        ok = is_v ? wait_bar(bar_vfree(j - kNSV), ph_v(j - kNSV)) : wait_bar(bar_kfree(j - kNSK), ph_k(j - kNSK));
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
-      stage(j, false);
-      if (lane == 0) PF_TRACE(3, j);
-      // V stage j % 2 is free once both tiles' P.V(j-2) completed.
-      if (j >= kNSV && lane == 0) ok = wait_bar(bar_vfree(j - kNSV), ph_v(j - kNSV));
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      stage(j, true);
-      if (lane == 0) PF_TRACE(2, j);
+      stage(j);
+      if (lane == 0) PF_TRACE(is_v ? 2 : 3, j);
     }
     if (!ok && lane == 0) fail_flag = 1;
   } else if (warp == kMmaWarp) {
