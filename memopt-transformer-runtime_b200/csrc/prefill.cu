@@ -244,10 +244,13 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     if (!ok && lane == 0) fail_flag = 1;
   } else if (warp == kMmaWarp) {
     // ============================== MMA warp ==============================
-    // Descriptors are built once; a k-step or stage advances the 14-bit start
-    // address field by (byte offset >> 4) (all offsets stay below 256 KB).
+    // The whole warp runs this loop (waits included) with warp-uniform
+    // operands; elect.sync inside mma_f16_elect / commit_elect issues each
+    // instruction once.  Descriptors are built once; a k-step or stage
+    // advances the 14-bit start address field by (byte offset >> 4) (all
+    // offsets stay below 256 KB).
     bool ok = true;
-    if (lane == 0 && nblocks > 0) {
+    if (nblocks > 0) {
       uint64_t dq[kTiles];
 #pragma unroll
       for (int t = 0; t < kTiles; ++t) dq[t] = tc::sdesc_sw128(sbase + C::Q_OFF + t * C::Q_TILE, 16, 1024);
@@ -258,51 +261,53 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         const uint64_t dk = dk0 + static_cast<uint64_t>(((j % kNSK) * C::KV_STAGE) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          tc::mma_f16(tS(t, j), dq[t] + static_cast<uint64_t>(((kk / 4) * C::Q_HALF + (kk % 4) * 32) >> 4),
-                      dk + static_cast<uint64_t>(((kk / 4) * C::KV_HALF + (kk % 4) * 32) >> 4), C::IDESC_S, kk > 0);
+          tc::mma_f16_elect(tS(t, j), dq[t] + static_cast<uint64_t>(((kk / 4) * C::Q_HALF + (kk % 4) * 32) >> 4),
+                            dk + static_cast<uint64_t>(((kk / 4) * C::KV_HALF + (kk % 4) * 32) >> 4), C::IDESC_S,
+                            kk > 0);
         }
-        tc::commit(bar_sfull(t, j));
+        tc::commit_elect(bar_sfull(t, j));
       };
       auto issue_pv = [&](int t, int j) {
         const uint64_t dv = dv0 + static_cast<uint64_t>(((j % kNSV) * C::KV_STAGE) >> 4);
         const uint64_t dp = dp0 + static_cast<uint64_t>(((t * 2 + (j & 1)) * C::P_BUF) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          tc::mma_f16(tO(t), dp + static_cast<uint64_t>((kk * 32) >> 4), dv + static_cast<uint64_t>((kk * 2048) >> 4),
-                      C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_elect(tO(t), dp + static_cast<uint64_t>((kk * 32) >> 4),
+                            dv + static_cast<uint64_t>((kk * 2048) >> 4), C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc::commit(bar_pfree(t, j));
+        tc::commit_elect(bar_pfree(t, j));
       };
+      auto wait_all = [&](uint32_t bar, uint32_t parity) { return __all_sync(0xffffffffu, wait_bar(bar, parity)); };
       // S(j) of both tiles into score buffer j % 2, the K stage released after.
       auto issue_s_both = [&](int j) -> bool {
-        if (!wait_bar(bar_kfull(j), ph_k(j))) return false;
+        if (!wait_all(bar_kfull(j), ph_k(j))) return false;
         for (int t = 0; t < kTiles; ++t) {
-          if (j >= 2 && !wait_bar(bar_sfree(t, j - 2), ph_2(j - 2))) return false;  // buffer read
+          if (j >= 2 && !wait_all(bar_sfree(t, j - 2), ph_2(j - 2))) return false;  // buffer read
           tc::fence_after_sync();
           issue_s(t, j);
         }
-        tc::commit(bar_kfree(j));
-        PF_TRACE(1, j);
+        tc::commit_elect(bar_kfree(j));
+        if (lane == 0) PF_TRACE(1, j);
         return true;
       };
-      ok = wait_bar(bar_at(0), 0);
+      ok = wait_all(bar_at(0), 0);
       if (ok) ok = issue_s_both(0);
       if (ok && nblocks > 1) ok = issue_s_both(1);
       for (int j = 0; j < nblocks && ok; ++j) {
-        ok = wait_bar(bar_vfull(j), ph_v(j));
+        ok = wait_all(bar_vfull(j), ph_v(j));
         for (int t = 0; t < kTiles && ok; ++t) {
-          ok = wait_bar(bar_pfull(t, j), ph_2(j));
+          ok = wait_all(bar_pfull(t, j), ph_2(j));
           if (ok) {
             tc::fence_after_sync();
             issue_pv(t, j);
           }
         }
         if (!ok) break;
-        tc::commit(bar_vfree(j));
-        PF_TRACE(0, j);
+        tc::commit_elect(bar_vfree(j));
+        if (lane == 0) PF_TRACE(0, j);
         if (j + 2 < nblocks) ok = issue_s_both(j + 2);
       }
-      if (!ok) fail_flag = 1;
+      if (!ok && lane == 0) fail_flag = 1;
     }
     __syncwarp();
   } else {

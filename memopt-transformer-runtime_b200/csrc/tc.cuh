@@ -42,6 +42,28 @@ __device__ __forceinline__ void commit(uint32_t bar) {
                : "memory");
 }
 
+// The same two operations issued from warp-uniform control flow: every lane
+// executes them, elect.sync picks one (always the lowest active lane, so an
+// MMA and the commit that tracks it come from the same thread).  Operands
+// stay warp-uniform, which keeps them in uniform registers.
+__device__ __forceinline__ void mma_f16_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
 // Instruction descriptor of kind::f16: fp16 A/B, fp32 accumulator, dense.
 // a_mn / b_mn select MN-major (transposed) operands.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn) {
