@@ -36,8 +36,9 @@ except ImportError as _e:  # pragma: no cover - exercised only on broken install
 
 from memopt.attention import DynamicAttention  # noqa: E402
 from memopt.scheduler import MemoryScheduler, SchedulerConfig  # noqa: E402
+from memopt.kv_cache import PagedKVCache, PageTable  # noqa: E402
 
-__all__ = ["DynamicAttention", "MemoryScheduler", "SchedulerConfig", "get_hello"]
+__all__ = ["DynamicAttention", "MemoryScheduler", "SchedulerConfig", "PagedKVCache", "PageTable", "get_hello"]
 
 
 def get_hello() -> str:

@@ -13,6 +13,11 @@ Same constructor, forward signature and routing as the reference module
   ``dynamic_sparse_attention_int4``;
 * without paged arguments it computes dense SDPA, keeping only the last
   ``window_size`` keys when ``S > window_size`` (reference :475-530);
+* ``forward(x, kv_cache=cache, seq_ids=ids)`` (addition) appends this
+  call's K/V to a :class:`memopt.kv_cache.PagedKVCache` and attends over each
+  sequence's whole cached context (incremental decode); with
+  ``scheduler=MemoryScheduler(...)`` the scheduler's ``retain_ratio`` /
+  ``use_int4`` are applied to the cache first (eviction, INT4 conversion);
 * an exception on the paged path is reported as a RuntimeWarning, counted
   in ``_fallback_count``, disables the paged path for the instance and the
   call is answered by SDPA — unless ``strict=True``, which re-raises.
@@ -54,6 +59,7 @@ class DynamicAttention(nn.Module):
         num_sink_tokens: int = 4,
         use_triton: bool = False,
         strict: bool = False,
+        scheduler=None,
     ) -> None:
         super().__init__()
         assert embed_dim % num_heads == 0, (
@@ -67,6 +73,7 @@ class DynamicAttention(nn.Module):
         self.num_sink_tokens = num_sink_tokens
         self.scale = self.head_dim ** -0.5
         self.strict = strict
+        self.scheduler = scheduler
 
         self.q_proj = nn.Linear(embed_dim, embed_dim, bias=False)
         self.k_proj = nn.Linear(embed_dim, embed_dim, bias=False)
@@ -93,12 +100,24 @@ class DynamicAttention(nn.Module):
         block_tables: Optional[torch.Tensor] = None,
         slot_mapping: Optional[torch.Tensor] = None,
         context_lens: Optional[torch.Tensor] = None,
+        kv_cache=None,
+        seq_ids=None,
     ) -> torch.Tensor:
         orig_dtype = x.dtype
-        _, seq_len, _ = x.shape
+        B, seq_len, _ = x.shape
         q = self.q_proj(x)
         k = self.k_proj(x)
         v = self.v_proj(x)
+        if kv_cache is not None:
+            # Incremental path: this call's tokens are appended to each
+            # sequence's cache and attend over its whole cached context.
+            H, D = self.num_heads, self.head_dim
+            q4 = q.reshape(B, seq_len, H, D)
+            kv_cache.append(seq_ids, k.reshape(B, seq_len, H, D), v.reshape(B, seq_len, H, D))
+            if self.scheduler is not None:
+                kv_cache.apply_policy(self.scheduler, q4, seq_ids, self.num_sink_tokens)
+            out = kv_cache.attend(q4, seq_ids, self.window_size)
+            return self.out_proj(out.reshape(B, seq_len, self.embed_dim).to(orig_dtype))
         paged = block_tables is not None and slot_mapping is not None and context_lens is not None
         if self._use_custom_kernel and paged:
             try:

@@ -1,0 +1,84 @@
+"""Incremental decode through PagedKVCache / DynamicAttention on the GPU, and
+the MemoryScheduler policy applied to a live cache."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import memopt
+from memopt import DynamicAttention, MemoryScheduler, PagedKVCache, SchedulerConfig
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _ref_attention(q, k, v):
+    # q [n, H, D], k/v [L, H, D] -> [n, H, D], non-causal, fp32
+    s = torch.einsum("nhd,lhd->hnl", q.float(), k.float()) / q.shape[-1] ** 0.5
+    return torch.einsum("hnl,lhd->nhd", torch.softmax(s, dim=-1), v.float())
+
+
+def test_incremental_decode_matches_full_attention():
+    torch.manual_seed(0)
+    H, D = 4, 64
+    cache = PagedKVCache(64, H, D, 16)
+    sids = [cache.add_sequence(), cache.add_sequence()]
+    ks, vs = [[], []], [[], []]
+    for step, n in enumerate([37, 1, 1, 1, 20, 1]):  # prefill-sized chunks and single tokens
+        k = torch.randn(2, n, H, D, device=DEV, dtype=torch.float16)
+        v = torch.randn(2, n, H, D, device=DEV, dtype=torch.float16)
+        q = torch.randn(2, n, H, D, device=DEV, dtype=torch.float16)
+        cache.append(sids, k, v)
+        for i in range(2):
+            ks[i].append(k[i])
+            vs[i].append(v[i])
+        out = cache.attend(q, sids)
+        for i in range(2):
+            ref = _ref_attention(q[i], torch.cat(ks[i]), torch.cat(vs[i]))
+            torch.testing.assert_close(out[i].float(), ref, atol=2e-3, rtol=1e-2)
+    assert cache.context_lens(sids).tolist() == [61, 61]
+    cache.free_sequence(sids[0])
+    assert memopt.memopt_C.free_blocks_count() == 64 - 4
+
+
+def test_dynamic_attention_with_cache_and_scheduler():
+    torch.manual_seed(1)
+    E, H = 256, 4
+    util = {"v": 0.1}
+    sched = MemoryScheduler(SchedulerConfig(drop_retain_ratio=0.75), sampler=lambda: util["v"])
+    layer = DynamicAttention(E, H, scheduler=sched, num_sink_tokens=0).to(DEV)
+    cache = PagedKVCache(32, H, E // H, 16)
+    sids = [cache.add_sequence()]
+    x = torch.randn(1, 40, E, device=DEV)
+    y0 = layer(x, kv_cache=cache, seq_ids=sids)
+    assert y0.shape == (1, 40, E) and torch.isfinite(y0).all() and cache.kv_format == "fp16"
+    # pressure: eviction on the fp16 pool, then conversion to INT4
+    util["v"] = 0.99
+    sched.adjust_policy()
+    y1 = layer(torch.randn(1, 1, E, device=DEV), kv_cache=cache, seq_ids=sids)
+    assert cache.kv_format == "int4" and torch.isfinite(y1).all()
+    assert cache.context_lens(sids).tolist() == [41]
+    # decode continues on the INT4 pool
+    for _ in range(3):
+        y = layer(torch.randn(1, 1, E, device=DEV), kv_cache=cache, seq_ids=sids)
+        assert torch.isfinite(y).all()
+    assert cache.context_lens(sids).tolist() == [44]
+
+
+def test_to_int4_keeps_tokens_and_pages():
+    torch.manual_seed(2)
+    H, D = 2, 128
+    cache = PagedKVCache(16, H, D, 16)
+    s = cache.add_sequence()
+    k = torch.randn(1, 50, H, D, device=DEV, dtype=torch.float16)
+    v = torch.randn(1, 50, H, D, device=DEV, dtype=torch.float16)
+    cache.append([s], k, v)
+    q = torch.randn(1, 1, H, D, device=DEV, dtype=torch.float16)
+    before = cache.attend(q, [s]).float()
+    pages = cache.table.pages(s)
+    free_before = memopt.memopt_C.free_blocks_count()
+    cache.to_int4()
+    assert cache.kv_format == "int4" and cache.table.pages(s) == pages
+    assert memopt.memopt_C.free_blocks_count() == free_before
+    after = cache.attend(q, [s]).float()
+    assert (after - before).abs().max().item() < 0.1  # INT4 g64 quantisation error only
