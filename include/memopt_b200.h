@@ -150,6 +150,34 @@ int memopt_evict_tokens(const float* scores, int num_seqs, int num_heads, int se
                         void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Exact sink-aware top-k eviction with compaction (new; the reference's      */
+/* evict_tokens frees no memory).  Per sequence b: token score = sum over     */
+/* heads of scores[b, h, t] (fp32, heads in order); tokens < num_sink_tokens  */
+/* are always kept; tokens at/after context_lens[b] or on a page whose entry  */
+/* is < 0 or >= pool_num_blocks are never kept; keep = max(1, min(L,         */
+/* ceil(r*L))) over the L valid tokens; the keep largest survive (ties: lower */
+/* index first; NaN lowest).  Their K/V rows (all heads) move in token order  */
+/* to positions 0..keep-1 over the sequence's valid pages; block_tables[b]    */
+/* becomes the first ceil(keep/block_size) valid pages then -1, the other     */
+/* valid pages are listed in freed_pages[b] (freed_count[b] of them, -1 pad)  */
+/* for the caller to release; context_lens[b] = keep.                          */
+/* scores fp32 [num_seqs, num_heads, max_len]; kept_idx int32 [num_seqs,      */
+/* max_len] (ascending original indices, -1 pad); kept_count int32            */
+/* [num_seqs]; freed_pages int32 [num_seqs, max_blocks_per_seq]; freed_count  */
+/* int32 [num_seqs].  max_len <= 32768, max_blocks_per_seq <= 2048; fp16      */
+/* pools in reference layout.  The workspace (16-byte aligned) holds the      */
+/* moved rows: memopt_evict_topk_workspace_size() bytes.                       */
+/* ------------------------------------------------------------------------ */
+size_t memopt_evict_topk_workspace_size(int num_seqs, int max_len, int num_heads, int head_dim);
+int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, int max_len,
+                              int32_t* block_tables, int max_blocks_per_seq, int32_t* context_lens,
+                              void* key_pool, void* value_pool, int pool_num_blocks, int block_size,
+                              int head_dim, float retain_ratio, int num_sink_tokens,
+                              int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
+                              int32_t* freed_count, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* evict_cache (kv_cache.cu:379-559): per (physical block, head) keep the     */
 /* max(1, (int)(r*block_size)) highest scores, zero the full head rows of the */
 /* rest.  scores fp32 [num_blocks, block_size, num_heads].                    */

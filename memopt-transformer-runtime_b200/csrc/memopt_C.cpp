@@ -286,6 +286,48 @@ pybind11::object evict_tokens(torch::Tensor attention_scores, torch::Tensor bloc
   return pybind11::none();
 }
 
+// Exact top-k eviction with compaction (new operator; see memopt_b200.h).
+// block_tables and context_lens must be contiguous CUDA int32 tensors: they
+// are updated in place.  Returns (kept_idx [S, L], kept_count [S],
+// freed_pages [S, MB], freed_count [S]).
+pybind11::tuple evict_topk_compact(torch::Tensor attention_scores, torch::Tensor block_tables,
+                                   torch::Tensor context_lens, float retain_ratio, int num_sink_tokens) {
+  TORCH_CHECK(P().live && memopt_pool_is_initialized(), "evict_topk_compact: pool not initialized");
+  auto& p = P();
+  TORCH_CHECK(!p.int4, "evict_topk_compact: needs the fp16 pool");
+  TORCH_CHECK(attention_scores.dim() == 3 && attention_scores.scalar_type() == torch::kFloat32,
+              "evict_topk_compact: attention_scores must be float32 [num_seqs, num_heads, max_len]");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.scalar_type() == torch::kInt32 && block_tables.is_contiguous(),
+              "evict_topk_compact: block_tables must be a contiguous int32 [num_seqs, max_blocks_per_seq] tensor");
+  TORCH_CHECK(context_lens.dim() == 1 && context_lens.scalar_type() == torch::kInt32 && context_lens.is_contiguous(),
+              "evict_topk_compact: context_lens must be a contiguous int32 [num_seqs] tensor");
+  TORCH_CHECK(attention_scores.is_cuda() && block_tables.is_cuda() && context_lens.is_cuda(),
+              "evict_topk_compact: inputs must be CUDA tensors");
+  const int S = static_cast<int>(attention_scores.size(0));
+  const int H = static_cast<int>(attention_scores.size(1));
+  const int L = static_cast<int>(attention_scores.size(2));
+  const int MB = static_cast<int>(block_tables.size(1));
+  TORCH_CHECK(H == p.h, "evict_topk_compact: num_heads != pool.num_heads");
+  TORCH_CHECK(block_tables.size(0) == S && context_lens.size(0) == S, "evict_topk_compact: batch size mismatch");
+  auto o = torch::TensorOptions().dtype(torch::kInt32).device(attention_scores.device());
+  auto kept = torch::full({S, L}, -1, o);
+  auto cnt = torch::zeros({S}, o);
+  auto freed = torch::full({S, MB}, -1, o);
+  auto fcnt = torch::zeros({S}, o);
+  if (S == 0 || L == 0) return pybind11::make_tuple(kept, cnt, freed, fcnt);
+  attention_scores = attention_scores.contiguous();
+  const at::cuda::CUDAGuard g(attention_scores.device());
+  const size_t wsb = memopt_evict_topk_workspace_size(S, L, H, p.d);
+  auto ws = torch::empty({static_cast<int64_t>(wsb)}, o.dtype(torch::kUInt8));
+  check(memopt_evict_topk_compact(attention_scores.data_ptr<float>(), S, H, L, block_tables.data_ptr<int32_t>(), MB,
+                                  context_lens.data_ptr<int32_t>(), p.k.data_ptr(), p.v.data_ptr(), p.nb, p.bs, p.d,
+                                  retain_ratio, num_sink_tokens, kept.data_ptr<int32_t>(), cnt.data_ptr<int32_t>(),
+                                  freed.data_ptr<int32_t>(), fcnt.data_ptr<int32_t>(), ws.data_ptr(), wsb,
+                                  cur_stream()),
+        "evict_topk_compact");
+  return pybind11::make_tuple(kept, cnt, freed, fcnt);
+}
+
 namespace {
 
 void attn_checks(const torch::Tensor& query, const torch::Tensor& block_tables, const torch::Tensor& context_lens) {
@@ -464,6 +506,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("evict_tokens", &evict_tokens, "Sequence-centric Ada-KV token eviction with block_table unlinking",
         py::arg("attention_scores"), py::arg("block_tables"), py::arg("is_block_free"), py::arg("retain_ratio"),
         py::arg("num_sink_tokens") = 4, py::arg("return_retained") = false);
+  m.def("evict_topk_compact", &evict_topk_compact,
+        "Exact sink-aware top-k eviction shared across heads, with compaction of the kept K/V rows",
+        py::arg("attention_scores"), py::arg("block_tables"), py::arg("context_lens"), py::arg("retain_ratio"),
+        py::arg("num_sink_tokens") = 4);
   m.def("dynamic_sparse_attention", &dynamic_sparse_attention, "Dynamic sparse/chunked attention over paged KV cache");
   m.def("dynamic_sparse_attention_int4", &dynamic_sparse_attention_int4,
         "Paged attention over an int4 pool with dequantisation fused into the loads");

@@ -93,6 +93,21 @@ class PageTable:
         seq.length += n_new
         return slots
 
+    def compact(self, sid: int, new_length: int) -> List[int]:
+        """After an in-place compaction of ``sid`` to its first ``new_length``
+        tokens: keeps the first ceil(new_length / block_size) pages, returns
+        the others to the allocator and lists them."""
+        seq = self._seqs[sid]
+        if not 0 <= new_length <= seq.length:
+            raise ValueError(f"compact: new length {new_length} outside [0, {seq.length}]")
+        need = (new_length + self.block_size - 1) // self.block_size
+        freed = seq.pages[need:]
+        seq.pages = seq.pages[:need]
+        seq.length = new_length
+        for p in freed:
+            self._free(p)
+        return freed
+
     def block_table(self, sids: Sequence[int], max_blocks: Optional[int] = None) -> List[List[int]]:
         """Rows of page ids, -1 padded to ``max_blocks`` (default: the longest)."""
         rows = [self._seqs[s].pages for s in sids]
@@ -104,7 +119,15 @@ class PagedKVCache:
     """Paged KV cache of one attention layer over the process-wide pool."""
 
     def __init__(self, num_blocks: int, num_heads: int, head_dim: int, block_size: int = 16,
-                 kv_format: str = "fp16", device: Optional[torch.device] = None) -> None:
+                 kv_format: str = "fp16", device: Optional[torch.device] = None,
+                 eviction: str = "reference") -> None:
+        """``eviction``: "reference" runs ``evict_tokens`` (the reference's
+        semantics: per-head threshold, rows zeroed, no page released);
+        "exact" runs ``evict_topk_compact`` (one exact top-k per sequence
+        shared by all heads, kept rows compacted, emptied pages freed)."""
+        if eviction not in ("reference", "exact"):
+            raise ValueError("eviction must be 'reference' or 'exact'")
+        self.eviction = eviction
         import memopt_C
 
         self._C = memopt_C
@@ -194,6 +217,26 @@ class PagedKVCache:
         return self._C.evict_tokens(scores.float().contiguous(), bt, ibf, float(retain_ratio), int(num_sink_tokens),
                                     return_retained=True)
 
+    def evict_exact(self, sids: Sequence[int], scores: torch.Tensor, retain_ratio: float,
+                    num_sink_tokens: int = 4) -> List[List[int]]:
+        """``evict_topk_compact`` over the sequences: the kept tokens (exact
+        top-k of the head-summed scores, sinks always kept) move to the front
+        of each sequence, lengths shrink, and the emptied pages return to the
+        pool.  Returns the kept original token indices per sequence."""
+        if self.kv_format != "fp16":
+            raise RuntimeError("evict_exact: works on the fp16 pool")
+        bt = self.block_tables(sids).contiguous()
+        ctx = self.context_lens(sids).contiguous()
+        kept, cnt, _, _ = self._C.evict_topk_compact(scores.float().contiguous(), bt, ctx, float(retain_ratio),
+                                                     int(num_sink_tokens))
+        counts = cnt.tolist()
+        kept_h = kept.cpu()
+        out = []
+        for i, s in enumerate(sids):
+            self.table.compact(s, counts[i])
+            out.append(kept_h[i, :counts[i]].tolist())
+        return out
+
     def to_int4(self) -> None:
         """Re-quantises every cached token into an INT4 pool with the same
         block ids (page tables and lengths are unchanged)."""
@@ -242,7 +285,11 @@ class PagedKVCache:
         self._applied = (retain, use_int4)
         result = None
         if retain < 1.0 and q is not None and sids and self.kv_format == "fp16":
-            result = self.evict(sids, self.token_scores(q, sids), retain, num_sink_tokens)
+            scores = self.token_scores(q, sids)
+            if self.eviction == "exact":
+                result = self.evict_exact(sids, scores, retain, num_sink_tokens)
+            else:
+                result = self.evict(sids, scores, retain, num_sink_tokens)
         if use_int4 and self.kv_format == "fp16":
             self.to_int4()
         return result

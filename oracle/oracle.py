@@ -167,3 +167,56 @@ def paged_attention_int4(q, pages, block_tables, context_lens, max_seq_len, wind
                                       I32(bt.shape[1]), I64(NB), I32(block_size), I32(max_seq_len),
                                       I32(window_size), _p(out))
     return out
+
+
+def evict_topk_compact(scores, block_tables, context_lens, kpool, vpool, retain_ratio, num_sink_tokens=4):
+    """Restatement of the exact top-k eviction with compaction (this build's
+    operator; no reference counterpart).  In place on block_tables,
+    context_lens and the fp16 pools; returns (kept_idx, kept_count,
+    freed_pages, freed_count).  Pure numpy: token score = fp32 sum over heads
+    in head order, sinks always kept, invalid tokens never kept, ties by lower
+    index, NaN lowest."""
+    S, H, L = scores.shape
+    NB, BS = kpool.shape[0], kpool.shape[1]
+    MB = block_tables.shape[1]
+    kept_idx = np.full((S, L), -1, np.int32)
+    kept_count = np.zeros(S, np.int32)
+    freed = np.full((S, MB), -1, np.int32)
+    freed_count = np.zeros(S, np.int32)
+    for b in range(S):
+        n = min(max(int(context_lens[b]), 0), L)
+        tot = np.zeros(L, np.float32)
+        for h in range(H):
+            tot = (tot + scores[b, h].astype(np.float32)).astype(np.float32)
+        row = block_tables[b].copy()
+        valid_pages = [int(p) for p in row if 0 <= p < NB]
+        cand = []
+        for t in range(n):
+            lb = t // BS
+            pg = int(row[lb]) if lb < MB else -1
+            if 0 <= pg < NB:
+                s = tot[t]
+                key = (3, 0.0) if t < num_sink_tokens else ((0, 0.0) if np.isnan(s) else (1, float(s)))
+                cand.append((key, t))
+        nv = len(cand)
+        keep = 0 if nv == 0 else max(1, min(nv, int(np.ceil(np.float32(retain_ratio) * np.float32(nv)))))
+        # largest first; ties: lower index first
+        order = sorted(cand, key=lambda kt: (-kt[0][0], -kt[0][1], kt[1]))
+        kept = sorted(t for _, t in order[:keep])
+        kept_idx[b, :keep] = kept
+        kept_count[b] = keep
+        old = row.copy()
+        rows_k = [kpool[old[t // BS], t % BS].copy() for t in kept]
+        rows_v = [vpool[old[t // BS], t % BS].copy() for t in kept]
+        need = (keep + BS - 1) // BS
+        new_row = np.full(MB, -1, np.int32)
+        new_row[:need] = valid_pages[:need]
+        fl = valid_pages[need:]
+        freed[b, :len(fl)] = fl
+        freed_count[b] = len(fl)
+        block_tables[b] = new_row
+        for i in range(keep):
+            kpool[new_row[i // BS], i % BS] = rows_k[i]
+            vpool[new_row[i // BS], i % BS] = rows_v[i]
+        context_lens[b] = keep
+    return kept_idx, kept_count, freed, freed_count

@@ -119,3 +119,21 @@ def attention_int4(q, pages, block_size, bt, ctx, msl, win, ws=None):
 def int4_page_bytes(block_size, head_dim):
     lib().memopt_int4_page_bytes.restype = SZ
     return int(lib().memopt_int4_page_bytes(I(block_size), I(head_dim)))
+
+
+def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
+    S, H, L = scores.shape
+    MB = bt.shape[1]
+    dev = scores.device
+    kept = torch.empty(S, L, dtype=torch.int32, device=dev)
+    cnt = torch.empty(S, dtype=torch.int32, device=dev)
+    freed = torch.empty(S, MB, dtype=torch.int32, device=dev)
+    fcnt = torch.empty(S, dtype=torch.int32, device=dev)
+    lib().memopt_evict_topk_workspace_size.restype = SZ
+    wsb = int(lib().memopt_evict_topk_workspace_size(I(S), I(L), I(H), I(kpool.shape[3])))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    ok(lib().memopt_evict_topk_compact(ptr(scores), I(S), I(H), I(L), ptr(bt), I(MB), ptr(ctx), ptr(kpool),
+                                       ptr(vpool), I(kpool.shape[0]), I(kpool.shape[1]), I(kpool.shape[3]),
+                                       F(retain_ratio), I(sinks), ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt),
+                                       ptr(ws), SZ(wsb), stream()))
+    return kept, cnt, freed, fcnt

@@ -82,3 +82,31 @@ def test_to_int4_keeps_tokens_and_pages():
     assert memopt.memopt_C.free_blocks_count() == free_before
     after = cache.attend(q, [s]).float()
     assert (after - before).abs().max().item() < 0.1  # INT4 g64 quantisation error only
+
+
+def test_exact_eviction_frees_pages_and_keeps_top_tokens():
+    torch.manual_seed(3)
+    H, D, BS = 2, 64, 16
+    cache = PagedKVCache(40, H, D, BS, eviction="exact")
+    sids = [cache.add_sequence(), cache.add_sequence()]
+    k = torch.randn(2, 200, H, D, device=DEV, dtype=torch.float16)
+    v = torch.randn(2, 200, H, D, device=DEV, dtype=torch.float16)
+    cache.append(sids, k, v)
+    free0 = memopt.memopt_C.free_blocks_count()
+    scores = torch.rand(2, H, 200, device=DEV)
+    kept = cache.evict_exact(sids, scores, 0.5, num_sink_tokens=4)
+    tot = scores.sum(1)
+    for i, s in enumerate(sids):
+        assert len(kept[i]) == 100 and cache.table.length(s) == 100
+        assert kept[i][:4] == [0, 1, 2, 3]  # sinks
+        rest = set(torch.argsort(tot[i, 4:], descending=True)[:96].add(4).tolist())
+        assert set(kept[i][4:]) == rest
+        # the compacted rows are the kept tokens, in order
+        q = torch.randn(1, 1, H, D, device=DEV, dtype=torch.float16)
+        out = cache.attend(q, [s])
+        ki = torch.tensor(kept[i], device=DEV)
+        s_ = torch.einsum("hd,lhd->hl", q[0, 0].float(), k[i, ki].float()) / D ** 0.5
+        ref = torch.einsum("hl,lhd->hd", torch.softmax(s_, -1), v[i, ki].float())
+        torch.testing.assert_close(out[0, 0].float(), ref, atol=2e-3, rtol=1e-2)
+    # 200 tokens = 13 pages each -> 100 tokens = 7 pages: 12 pages back in the pool
+    assert memopt.memopt_C.free_blocks_count() == free0 + 12

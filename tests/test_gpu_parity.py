@@ -186,6 +186,39 @@ def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     assert np.array_equal(np16(gv).view(np.uint16), vp.view(np.uint16))
 
 
+@pytest.mark.parametrize("S,H,L,BS,D,r,sinks,dist,holes", [
+    (2, 4, 512, 16, 64, 0.75, 4, "lognormal", False),
+    (3, 2, 1000, 16, 128, 0.5, 0, "normal", True),
+    (2, 2, 777, 32, 64, 0.3, 2, "ties", False),
+    (1, 2, 100, 16, 64, 1.0, 0, "normal", False),
+    (1, 2, 100, 16, 64, 0.01, 0, "normal", False),
+    (2, 3, 4097, 16, 64, 0.75, 3, "specials", True),
+    (1, 2, 32768, 16, 64, 0.75, 4, "lognormal", False),
+    (2, 2, 16384, 16, 64, 0.6, 0, "ties", True),
+])
+def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
+    sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + 7 * S, dist, holes=holes)
+    rng = np.random.default_rng(L)
+    ctx = np.array([L - int(rng.integers(0, min(L, 40))) for _ in range(S)], np.int32)
+    ctx[0] = L
+    gk, gv = torch.from_numpy(kp).to(DEV), torch.from_numpy(vp).to(DEV)
+    gbt, gctx = torch.from_numpy(bt).to(DEV), torch.from_numpy(ctx).to(DEV)
+    kept, cnt, freed, fcnt = capi.evict_topk_compact(torch.from_numpy(sc).to(DEV), gbt, gctx, gk, gv, r, sinks)
+    rk, rc, rf, rfc = O.evict_topk_compact(sc, bt, ctx, kp, vp, r, sinks)
+    assert np.array_equal(np16(cnt), rc)
+    assert np.array_equal(np16(kept), rk)
+    assert np.array_equal(np16(fcnt), rfc)
+    assert np.array_equal(np16(freed), rf)
+    assert np.array_equal(np16(gbt), bt)
+    assert np.array_equal(np16(gctx), ctx)
+    # every live row of every kept page is bit-identical (rows past the kept tokens are unspecified)
+    for b in range(S):
+        for i in range(int(rc[b])):
+            pg, pos = bt[b, i // BS], i % BS
+            assert np.array_equal(np16(gk[pg, pos]).view(np.uint16), kp[pg, pos].view(np.uint16))
+            assert np.array_equal(np16(gv[pg, pos]).view(np.uint16), vp[pg, pos].view(np.uint16))
+
+
 @pytest.mark.parametrize("NB,BS,H,D,r", [(10, 16, 4, 64, 0.75), (7, 32, 3, 128, 0.5), (5, 8, 2, 64, 0.9),
                                          (6, 5, 2, 64, 0.6), (3, 16, 2, 64, 0.01)])
 def test_evict_cache_bit_exact(NB, BS, H, D, r):

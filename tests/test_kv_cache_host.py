@@ -50,6 +50,7 @@ class StubCache(PagedKVCache):
 
     def __init__(self, fmt="fp16"):  # noqa: D107 - no pool
         self.fmt = fmt
+        self.eviction = "reference"
         self.calls = []
         self._applied = (1.0, fmt == "int4")
 
@@ -86,3 +87,15 @@ def test_apply_policy_follows_the_scheduler_once_per_change():
     sched.adjust_policy()
     cache.apply_policy(sched, q="q", sids=[0])
     assert cache.calls == [] and cache.kv_format == "int4"  # quantised tokens stay INT4
+
+
+def test_page_table_compact_frees_tail_pages():
+    pool = FifoPool(6)
+    t = PageTable(4, pool.alloc, pool.release)
+    s = t.add_sequence()
+    t.reserve(s, 15)  # pages 0..3
+    assert t.compact(s, 6) == [2, 3]
+    assert t.pages(s) == [0, 1] and t.length(s) == 6 and pool.free == [4, 5, 2, 3]
+    assert t.reserve(s, 3) == [6, 7, 16]  # continues after the compacted tokens
+    with pytest.raises(ValueError):
+        t.compact(s, 100)
