@@ -227,6 +227,29 @@ int memopt_paged_attention_f16(const void* query, const void* key_pool,
  * The first call on a device looks up the array's address (make it before
  * any stream capture).  All calls share the array: calls that overlap on the
  * GPU race.  The ticket region is cleared at the start of every call. */
+/* Extended attention (no reference counterpart for the options):          */
+/* num_kv_heads divides num_heads; the pools (fp16 [NB, BS, num_kv_heads, D]  */
+/* or INT4 pages [NB, num_kv_heads, page_bytes]) hold num_kv_heads heads and  */
+/* query head h reads KV head h / (num_heads / num_kv_heads) (grouped-query   */
+/* attention).  causal != 0: query row i of the q_len rows is the token at    */
+/* ctx - q_len + i and sees [max(0, c_i - W), c_i) with c_i = ctx - q_len +   */
+/* i + 1.  num_kv_heads == num_heads and causal == 0 is exactly the call      */
+/* above.  The workspace size is the same.                                    */
+int memopt_paged_attention_f16_ex(const void* query, const void* key_pool,
+                                  const void* value_pool, const int32_t* block_tables,
+                                  const int32_t* context_lens, int batch, int q_len,
+                                  int num_heads, int num_kv_heads, int head_dim,
+                                  int max_blocks_per_seq, int64_t num_blocks, int block_size,
+                                  int max_seq_len, int window_size, int causal, void* out,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+int memopt_paged_attention_int4_ex(const void* query, const uint8_t* kv_pages,
+                                   const int32_t* block_tables, const int32_t* context_lens,
+                                   int batch, int q_len, int num_heads, int num_kv_heads,
+                                   int head_dim, int max_blocks_per_seq, int64_t num_blocks,
+                                   int block_size, int max_seq_len, int window_size, int causal,
+                                   void* out, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 size_t memopt_paged_attention_noalloc_max_bytes(void);
 int memopt_paged_attention_f16_noalloc(const void* query, const void* key_pool,
                                        const void* value_pool,

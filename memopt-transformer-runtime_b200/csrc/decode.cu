@@ -17,8 +17,8 @@ namespace memopt {
 
 // prefill.cu: tcgen05 path for q_len >= kPrefillMinRows.
 int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,
-                int B, int QL, int H, int D, int MB, int64_t NB, int BS, int window_clamped, void* out,
-                cudaStream_t s);
+                int B, int QL, int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal,
+                void* out, cudaStream_t s);
 constexpr int kPrefillMinRows = 64;
 
 // One predicate for the workspace size and the dispatch: q_len >= 64 runs on
@@ -156,10 +156,12 @@ int dispatch(const Params& p, int D, int BS, const CUtensorMap& km, const CUtens
 }
 
 int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t* ctx, int batch,
-                 int q_len, int H, int D, int MB, int64_t NB, int BS, int max_seq_len, int window,
-                 void* out, void* ws, size_t ws_bytes) {
+                 int q_len, int H, int KVH, int D, int MB, int64_t NB, int BS, int max_seq_len, int window,
+                 int causal, void* out, void* ws, size_t ws_bytes) {
   if (batch < 0 || q_len < 0 || H < 0 || D < 0 || MB < 0 || NB < 0)
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: negative size");
+  if (KVH <= 0 || (H > 0 && H % KVH != 0))
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: num_kv_heads must divide num_heads");
   if (!((BS == 16 || BS == 32) && (D == 64 || D == 128))) return unsupported(BS, D);
   if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15u)
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: query/out must be 16-byte aligned");
@@ -170,6 +172,9 @@ int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t*
   p.B = batch;
   p.QL = q_len;
   p.H = H;
+  p.KVH = KVH;
+  p.group = H > 0 ? H / KVH : 1;
+  p.causal = causal ? 1 : 0;
   p.MB = MB;
   p.NB = NB;
   p.window = clamp_window(window, max_seq_len);
@@ -225,16 +230,16 @@ extern "C" size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int 
   return align256(static_cast<size_t>(batch) * q_len * num_heads * sizeof(int32_t));
 }
 
-extern "C" int memopt_paged_attention_f16(const void* query, const void* key_pool,
-                                          const void* value_pool, const int32_t* block_tables,
-                                          const int32_t* context_lens, int batch, int q_len,
-                                          int num_heads, int head_dim, int max_blocks_per_seq,
-                                          int64_t num_blocks, int block_size, int max_seq_len,
-                                          int window_size, void* out, void* workspace,
-                                          size_t workspace_bytes, void* stream) {
+extern "C" int memopt_paged_attention_f16_ex(const void* query, const void* key_pool,
+                                             const void* value_pool, const int32_t* block_tables,
+                                             const int32_t* context_lens, int batch, int q_len,
+                                             int num_heads, int num_kv_heads, int head_dim,
+                                             int max_blocks_per_seq, int64_t num_blocks, int block_size,
+                                             int max_seq_len, int window_size, int causal, void* out,
+                                             void* workspace, size_t workspace_bytes, void* stream) {
   Params p{};
-  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, head_dim,
-                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, out,
+  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, num_kv_heads, head_dim,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, out,
                         workspace, workspace_bytes);
   if (st != MEMOPT_OK) return st;
   if (p.total_items == 0) return MEMOPT_OK;
@@ -245,25 +250,39 @@ extern "C" int memopt_paged_attention_f16(const void* query, const void* key_poo
   if (num_blocks * block_size > 0x7fffffffLL)
     return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: pool has more than 2^31 token rows");
   if (use_prefill(q_len))
-    return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads, head_dim,
-                       max_blocks_per_seq, num_blocks, block_size, p.window, out, as_stream(stream));
+    return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads,
+                       num_kv_heads, head_dim, max_blocks_per_seq, num_blocks, block_size, p.window, causal, out,
+                       as_stream(stream));
   alignas(64) CUtensorMap km, vm;
-  st = make_pool_map(&km, key_pool, num_blocks * block_size, num_heads, head_dim, block_size);
+  st = make_pool_map(&km, key_pool, num_blocks * block_size, num_kv_heads, head_dim, block_size);
   if (st != MEMOPT_OK) return st;
-  st = make_pool_map(&vm, value_pool, num_blocks * block_size, num_heads, head_dim, block_size);
+  st = make_pool_map(&vm, value_pool, num_blocks * block_size, num_kv_heads, head_dim, block_size);
   if (st != MEMOPT_OK) return st;
   return dispatch<false>(p, head_dim, block_size, km, vm, nullptr, as_stream(stream));
 }
 
-extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* kv_pages,
-                                           const int32_t* block_tables, const int32_t* context_lens,
-                                           int batch, int q_len, int num_heads, int head_dim,
-                                           int max_blocks_per_seq, int64_t num_blocks, int block_size,
-                                           int max_seq_len, int window_size, void* out, void* workspace,
-                                           size_t workspace_bytes, void* stream) {
+extern "C" int memopt_paged_attention_f16(const void* query, const void* key_pool,
+                                          const void* value_pool, const int32_t* block_tables,
+                                          const int32_t* context_lens, int batch, int q_len,
+                                          int num_heads, int head_dim, int max_blocks_per_seq,
+                                          int64_t num_blocks, int block_size, int max_seq_len,
+                                          int window_size, void* out, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  return memopt_paged_attention_f16_ex(query, key_pool, value_pool, block_tables, context_lens, batch, q_len,
+                                       num_heads, num_heads, head_dim, max_blocks_per_seq, num_blocks, block_size,
+                                       max_seq_len, window_size, 0, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int memopt_paged_attention_int4_ex(const void* query, const uint8_t* kv_pages,
+                                              const int32_t* block_tables, const int32_t* context_lens,
+                                              int batch, int q_len, int num_heads, int num_kv_heads,
+                                              int head_dim, int max_blocks_per_seq, int64_t num_blocks,
+                                              int block_size, int max_seq_len, int window_size, int causal,
+                                              void* out, void* workspace, size_t workspace_bytes,
+                                              void* stream) {
   Params p{};
-  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, head_dim,
-                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, out,
+  int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, num_kv_heads, head_dim,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, out,
                         workspace, workspace_bytes);
   if (st != MEMOPT_OK) return st;
   if (p.total_items == 0) return MEMOPT_OK;
@@ -275,4 +294,15 @@ extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* kv_
   alignas(64) CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   return dispatch<true>(p, head_dim, block_size, dummy, dummy, nullptr, as_stream(stream));
+}
+
+extern "C" int memopt_paged_attention_int4(const void* query, const uint8_t* kv_pages,
+                                           const int32_t* block_tables, const int32_t* context_lens,
+                                           int batch, int q_len, int num_heads, int head_dim,
+                                           int max_blocks_per_seq, int64_t num_blocks, int block_size,
+                                           int max_seq_len, int window_size, void* out, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+  return memopt_paged_attention_int4_ex(query, kv_pages, block_tables, context_lens, batch, q_len, num_heads,
+                                        num_heads, head_dim, max_blocks_per_seq, num_blocks, block_size,
+                                        max_seq_len, window_size, 0, out, workspace, workspace_bytes, stream);
 }

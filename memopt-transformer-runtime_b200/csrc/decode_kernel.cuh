@@ -40,6 +40,9 @@ struct Params {
   float2* ml;        // [pairs * n_chunks]
   float* po;         // [pairs * n_chunks * D]
   int B, QL, H, MB;
+  int KVH;     // heads of the pool (divides H)
+  int group;   // H / KVH: query heads per KV head (grouped-query attention)
+  int causal;  // 1: query row i of QL sees tokens up to ctx - QL + i (extension)
   int64_t NB;
   int window;    // already clamped as in attention.cu:453-455
   float qscale;  // log2(e) / sqrt(D)
@@ -120,9 +123,12 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
                        int& win_start, int& ctx, bool& more) {
     const int64_t pair = item / p.n_chunks;
     const int chunk = static_cast<int>(item - pair * p.n_chunks);
-    h = static_cast<int>(pair % p.H);
-    const int b = static_cast<int>(pair / (static_cast<int64_t>(p.H) * p.QL));
+    h = static_cast<int>(pair % p.H) / p.group;  // the KV head this query head reads
+    const int64_t bq = pair / p.H;
+    const int b = static_cast<int>(bq / p.QL);
     ctx = __ldg(p.ctx + b);
+    // Causal rows: row i of the QL query rows is the token at ctx - QL + i.
+    if (p.causal) ctx = ctx - p.QL + static_cast<int>(bq - static_cast<int64_t>(b) * p.QL) + 1;
     win_start = (p.window < ctx) ? (ctx - p.window) : 0;
     int p_hi = 0;
     if (ctx > 0) p_hi = min((ctx + BS - 1) / BS, p.MB);
@@ -151,10 +157,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       tma_load_3d(dst + C::K_BYTES, &vmap, 0, h, phys * BS, bar);
     } else {
       mbar_arrive_expect_tx(bar, (C::PPS == 2 && phys2 >= 0) ? 2 * C::PAGE_RAW : C::PAGE_RAW);
-      bulk_g2s(dst, p.pages + (static_cast<int64_t>(phys) * p.H + h) * C::PAGE_RAW, C::PAGE_RAW, bar);
+      bulk_g2s(dst, p.pages + (static_cast<int64_t>(phys) * p.KVH + h) * C::PAGE_RAW, C::PAGE_RAW, bar);
       if (C::PPS == 2 && phys2 >= 0)
-        bulk_g2s(dst + C::PAGE_RAW, p.pages + (static_cast<int64_t>(phys2) * p.H + h) * C::PAGE_RAW, C::PAGE_RAW,
-                 bar);
+        bulk_g2s(dst + C::PAGE_RAW, p.pages + (static_cast<int64_t>(phys2) * p.KVH + h) * C::PAGE_RAW,
+                 C::PAGE_RAW, bar);
     }
   };
 

@@ -364,9 +364,12 @@ torch::Tensor attn_workspace(const torch::Tensor& query, int MB, int BS, int max
 
 }  // namespace
 
+// Additions beyond the reference: the pool may hold fewer heads than the
+// query (grouped-query attention: query head h reads pool head h / (H / KVH))
+// and causal=True makes query row i the token at context_len - q_len + i.
 torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_cache, torch::Tensor value_cache,
                                        torch::Tensor block_tables, torch::Tensor context_lens, int max_seq_len,
-                                       int window_size) {
+                                       int window_size, bool causal) {
   attn_checks(query, block_tables, context_lens);
   TORCH_CHECK(key_cache.is_cuda(), "key_cache must be a CUDA tensor");
   TORCH_CHECK(value_cache.is_cuda(), "value_cache must be a CUDA tensor");
@@ -380,11 +383,12 @@ torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_ca
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
   const int BS = static_cast<int>(key_cache.size(1));
   const int MB = static_cast<int>(block_tables.size(1));
-  TORCH_CHECK(key_cache.size(2) == H, "key_cache num_heads ", key_cache.size(2), " != query num_heads ", H);
+  const int KVH = static_cast<int>(key_cache.size(2));
+  TORCH_CHECK(KVH > 0 && H % KVH == 0, "key_cache num_heads ", KVH, " does not divide query num_heads ", H);
   TORCH_CHECK(key_cache.size(3) == D, "key_cache head_dim ", key_cache.size(3), " != query head_dim ", D);
   TORCH_CHECK(value_cache.size(0) == key_cache.size(0), "value_cache num_kv_blocks mismatch");
   TORCH_CHECK(value_cache.size(1) == BS, "value_cache block_size mismatch");
-  TORCH_CHECK(value_cache.size(2) == H, "value_cache num_heads mismatch");
+  TORCH_CHECK(value_cache.size(2) == KVH, "value_cache num_heads mismatch");
   TORCH_CHECK(value_cache.size(3) == D, "value_cache head_dim mismatch");
   auto out = torch::empty_like(query);
   if (B == 0 || QL == 0 || H == 0 || D == 0) return out;
@@ -392,23 +396,25 @@ torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_ca
   auto q = aligned_contig(query);
   size_t wsb = 0;
   auto ws = attn_workspace(q, MB, BS, max_seq_len, window_size, &wsb);
-  check(memopt_paged_attention_f16(q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
-                                   block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(), B, QL, H, D,
-                                   MB, key_cache.size(0), BS, max_seq_len, window_size, out.data_ptr(),
-                                   wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
+  check(memopt_paged_attention_f16_ex(q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+                                      block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(), B, QL, H,
+                                      KVH, D, MB, key_cache.size(0), BS, max_seq_len, window_size, causal ? 1 : 0,
+                                      out.data_ptr(), wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
         "dynamic_sparse_attention");
   return out;
 }
 
 torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor kv_pages, torch::Tensor block_tables,
-                                            torch::Tensor context_lens, int max_seq_len, int window_size) {
+                                            torch::Tensor context_lens, int max_seq_len, int window_size,
+                                            bool causal) {
   attn_checks(query, block_tables, context_lens);
   TORCH_CHECK(kv_pages.is_cuda() && kv_pages.dim() == 3 && kv_pages.scalar_type() == torch::kUInt8 &&
                   kv_pages.is_contiguous(),
               "kv_pages must be a contiguous CUDA uint8 tensor [num_blocks, num_heads, page_bytes]");
   const int B = static_cast<int>(query.size(0)), QL = static_cast<int>(query.size(1));
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
-  TORCH_CHECK(kv_pages.size(1) == H, "kv_pages num_heads ", kv_pages.size(1), " != query num_heads ", H);
+  const int KVH = static_cast<int>(kv_pages.size(1));
+  TORCH_CHECK(KVH > 0 && H % KVH == 0, "kv_pages num_heads ", KVH, " does not divide query num_heads ", H);
   TORCH_CHECK(D % 64 == 0, "dynamic_sparse_attention_int4: head_dim must be a multiple of 64");
   const int64_t per_token = D + 4 * (D / 64);
   TORCH_CHECK(kv_pages.size(2) % per_token == 0, "kv_pages page_bytes ", kv_pages.size(2),
@@ -421,10 +427,10 @@ torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor k
   auto q = aligned_contig(query);
   size_t wsb = 0;
   auto ws = attn_workspace(q, MB, BS, max_seq_len, window_size, &wsb);
-  check(memopt_paged_attention_int4(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
-                                    context_lens.data_ptr<int32_t>(), B, QL, H, D, MB, kv_pages.size(0), BS,
-                                    max_seq_len, window_size, out.data_ptr(), wsb ? ws.data_ptr() : nullptr, wsb,
-                                    cur_stream()),
+  check(memopt_paged_attention_int4_ex(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
+                                       context_lens.data_ptr<int32_t>(), B, QL, H, KVH, D, MB, kv_pages.size(0), BS,
+                                       max_seq_len, window_size, causal ? 1 : 0, out.data_ptr(),
+                                       wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
         "dynamic_sparse_attention_int4");
   return out;
 }
@@ -510,9 +516,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Exact sink-aware top-k eviction shared across heads, with compaction of the kept K/V rows",
         py::arg("attention_scores"), py::arg("block_tables"), py::arg("context_lens"), py::arg("retain_ratio"),
         py::arg("num_sink_tokens") = 4);
-  m.def("dynamic_sparse_attention", &dynamic_sparse_attention, "Dynamic sparse/chunked attention over paged KV cache");
+  m.def("dynamic_sparse_attention", &dynamic_sparse_attention, "Dynamic sparse/chunked attention over paged KV cache",
+        py::arg("query"), py::arg("key_cache"), py::arg("value_cache"), py::arg("block_tables"),
+        py::arg("context_lens"), py::arg("max_seq_len"), py::arg("window_size"), py::arg("causal") = false);
   m.def("dynamic_sparse_attention_int4", &dynamic_sparse_attention_int4,
-        "Paged attention over an int4 pool with dequantisation fused into the loads");
+        "Paged attention over an int4 pool with dequantisation fused into the loads", py::arg("query"),
+        py::arg("kv_pages"), py::arg("block_tables"), py::arg("context_lens"), py::arg("max_seq_len"),
+        py::arg("window_size"), py::arg("causal") = false);
   m.def("quantize_kv_cache_int4", &quantize_kv_cache_int4,
         "Quantize KV cache to packed INT4 (group-wise symmetric); returns [packed_uint8, scales_float32]",
         py::arg("cache"), py::arg("group_size"));

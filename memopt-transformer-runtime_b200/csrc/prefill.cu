@@ -47,6 +47,8 @@ struct Params {
   int64_t NB;
   int window;
   float qscale;  // log2(e) / sqrt(D)
+  int group;     // query heads per KV head (the pool has H / group heads)
+  int causal;    // 1: query row i of QL is the token at ctx - QL + i (extension)
 };
 
 constexpr int kBN = 64;                // key tokens per block
@@ -139,8 +141,15 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
   auto ph_v = [](int j) { return static_cast<uint32_t>((j / kNSV) & 1); };
   auto ph_2 = [](int j) { return static_cast<uint32_t>((j >> 1) & 1); };
 
-  const int ctx = __ldg(p.ctx + b);
-  const int ws = (p.window < ctx) ? (ctx - p.window) : 0;
+  const int hk = h / p.group;  // KV head of this query head
+  const int ctx_seq = __ldg(p.ctx + b);
+  // Visible tokens of query row qi: [ws_i, ctx_i), ctx_i = ctx (non-causal)
+  // or ctx - QL + qi + 1 (causal), ws_i = max(0, ctx_i - window).  The CTA
+  // stages the union over its rows; each softmax thread masks with its own.
+  auto row_ctx = [&](int qi) { return p.causal ? ctx_seq - p.QL + qi + 1 : ctx_seq; };
+  auto row_ws = [&](int c) { return (p.window < c) ? (c - p.window) : 0; };
+  const int ctx = row_ctx(min(qt * kRows + kRows - 1, p.QL - 1));
+  const int ws = row_ws(row_ctx(qt * kRows));
   const int p_hi = ctx > 0 ? min((ctx + BS - 1) / BS, p.MB) : 0;
   const int p_lo = ws / BS;
   const int nblocks = p_hi > p_lo ? (p_hi - p_lo + C::PPB - 1) / C::PPB : 0;
@@ -218,7 +227,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       __syncwarp();  // the transaction count is armed before any copy can land
       if ((mask >> lane) & 1u) {
         for (int hh = 0; hh < C::HALVES; ++hh)
-          tma_load_3d(sbase + off + hh * C::KV_HALF + lane * BS * 128, is_v ? &vmap : &kmap, hh * 64, h,
+          tma_load_3d(sbase + off + hh * C::KV_HALF + lane * BS * 128, is_v ? &vmap : &kmap, hh * 64, hk,
                       phys * BS, bar);
       }
     };
@@ -316,6 +325,8 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     const int row = (warp & 3) * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t sProw = sbase + C::P_OFF + t * 2 * C::P_BUF + row * 128;
+    const int ctx_r = row_ctx(qt * kRows + t * 128 + row);  // this row's visible tokens
+    const int ws_r = row_ws(ctx_r);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nblocks && ok; ++j) {
@@ -342,12 +353,12 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       int phys_unused;
       const uint32_t mask = page_bits(j, phys_unused);
       const int tok0 = (p_lo + j * C::PPB) * BS;
-      const bool edge = mask != ((1u << C::PPB) - 1u) || tok0 < ws || tok0 + kBN > ctx;
+      const bool edge = mask != ((1u << C::PPB) - 1u) || tok0 < ws_r || tok0 + kBN > ctx_r;
       if (edge) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i) {
           const int tk = tok0 + i;
-          const bool valid = ((mask >> (i / BS)) & 1u) && tk >= ws && tk < ctx;
+          const bool valid = ((mask >> (i / BS)) & 1u) && tk >= ws_r && tk < ctx_r;
           s[i] = valid ? s[i] : -INFINITY;
         }
       }
@@ -497,9 +508,9 @@ int launch_prefill(const prefill::Params& p, const void* query, const void* kpoo
   alignas(64) CUtensorMap qm, km, vm;
   int st = map_rows_sw128(&qm, query, static_cast<int64_t>(p.B) * p.QL, p.H, D, 128);
   if (st != MEMOPT_OK) return st;
-  st = map_rows_sw128(&km, kpool, p.NB * BS, p.H, D, BS);
+  st = map_rows_sw128(&km, kpool, p.NB * BS, p.H / p.group, D, BS);
   if (st != MEMOPT_OK) return st;
-  st = map_rows_sw128(&vm, vpool, p.NB * BS, p.H, D, BS);
+  st = map_rows_sw128(&vm, vpool, p.NB * BS, p.H / p.group, D, BS);
   if (st != MEMOPT_OK) return st;
   auto kern = prefill::prefill_kernel<D, BS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -520,8 +531,8 @@ extern "C" __attribute__((visibility("default"))) int memopt_prefill_trace(unsig
 
 // Called by memopt_paged_attention_f16 for q_len >= kPrefillMinRows.
 int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,
-                int B, int QL, int H, int D, int MB, int64_t NB, int BS, int window_clamped, void* out,
-                cudaStream_t s) {
+                int B, int QL, int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal,
+                void* out, cudaStream_t s) {
   prefill::Params p{};
   p.bt = bt;
   p.ctx = ctx;
@@ -533,6 +544,8 @@ int prefill_f16(const void* query, const void* kpool, const void* vpool, const i
   p.NB = NB;
   p.window = window_clamped;
   p.qscale = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  p.group = H / KVH;
+  p.causal = causal ? 1 : 0;
   if (static_cast<int64_t>(B) * QL > 0x7fffffffLL || NB * BS > 0x7fffffffLL)
     return fail(MEMOPT_ERR_UNSUPPORTED, "prefill: more than 2^31 rows");
   if (D == 128 && BS == 16) return launch_prefill<128, 16>(p, query, kpool, vpool, s);

@@ -328,23 +328,32 @@ static void fetch_row(const kv_src* s, int kv, int64_t phys, int pos, int h, dou
   }
 }
 
+/* H query heads over src->H pool (KV) heads: query head h reads KV head
+ * h / (H / src->H).  causal = 0: every row of sequence b sees [ctx - W, ctx)
+ * (attention.cu semantics); causal = 1: row i of the QL query rows is the
+ * token at ctx - QL + i and sees [max(0, c_i - W), c_i), c_i = ctx - QL + i + 1
+ * (an extension; the reference is non-causal). */
 static void attention_core(const uint16_t* q, const kv_src* src, const int32_t* bt,
-                           const int32_t* ctx_lens, int B, int QL, int MB, int64_t NB,
-                           int max_seq_len, int window, double* out) {
-  const int H = src->H, D = src->D, BS = src->BS;
+                           const int32_t* ctx_lens, int B, int QL, int H, int MB, int64_t NB,
+                           int max_seq_len, int window, int causal, double* out) {
+  const int KVH = src->H, D = src->D, BS = src->BS;
+  const int group = H / KVH;
   if (window <= 0 || window > max_seq_len) window = max_seq_len;
   const double scale = (double)(1.0f / sqrtf((float)D));
   const int64_t rows = (int64_t)B * QL * H;
 #pragma omp parallel for schedule(dynamic, 4)
   for (int64_t row = 0; row < rows; ++row) {
-    const int h = (int)(row % H);
+    const int hq = (int)(row % H);
+    const int h = hq / group;
     const int b = (int)(row / ((int64_t)QL * H));
+    const int qi = (int)((row / H) % QL);
     double qv[256], kr[256], vr[256], acc[256];
     for (int d = 0; d < D; ++d) {
       qv[d] = oracle_f16_to_f32(q[row * D + d]);
       acc[d] = 0.0;
     }
-    const int ctx = ctx_lens[b];
+    int ctx = ctx_lens[b];
+    if (causal) ctx = ctx - QL + qi + 1;
     const int ws = window < ctx ? ctx - window : 0;
     double m = -INFINITY, l = 0.0;
     for (int slot = 0; slot < MB; ++slot) {
@@ -370,17 +379,32 @@ static void attention_core(const uint16_t* q, const kv_src* src, const int32_t* 
   }
 }
 
+void oracle_paged_attention_f16_ex(const uint16_t* q, const uint16_t* kpool, const uint16_t* vpool,
+                                   const int32_t* bt, const int32_t* ctx, int B, int QL, int H, int KVH,
+                                   int D, int MB, int64_t NB, int BS, int max_seq_len, int window,
+                                   int causal, double* out) {
+  kv_src s = {0, kpool, vpool, 0, KVH, D, BS};
+  attention_core(q, &s, bt, ctx, B, QL, H, MB, NB, max_seq_len, window, causal, out);
+}
+
 void oracle_paged_attention_f16(const uint16_t* q, const uint16_t* kpool, const uint16_t* vpool,
                                 const int32_t* bt, const int32_t* ctx, int B, int QL, int H, int D,
                                 int MB, int64_t NB, int BS, int max_seq_len, int window,
                                 double* out) {
-  kv_src s = {0, kpool, vpool, 0, H, D, BS};
-  attention_core(q, &s, bt, ctx, B, QL, MB, NB, max_seq_len, window, out);
+  oracle_paged_attention_f16_ex(q, kpool, vpool, bt, ctx, B, QL, H, H, D, MB, NB, BS, max_seq_len, window, 0,
+                                out);
+}
+
+void oracle_paged_attention_int4_ex(const uint16_t* q, const uint8_t* pages, const int32_t* bt,
+                                    const int32_t* ctx, int B, int QL, int H, int KVH, int D, int MB,
+                                    int64_t NB, int BS, int max_seq_len, int window, int causal,
+                                    double* out) {
+  kv_src s = {1, 0, 0, pages, KVH, D, BS};
+  attention_core(q, &s, bt, ctx, B, QL, H, MB, NB, max_seq_len, window, causal, out);
 }
 
 void oracle_paged_attention_int4(const uint16_t* q, const uint8_t* pages, const int32_t* bt,
                                  const int32_t* ctx, int B, int QL, int H, int D, int MB, int64_t NB,
                                  int BS, int max_seq_len, int window, double* out) {
-  kv_src s = {1, 0, 0, pages, H, D, BS};
-  attention_core(q, &s, bt, ctx, B, QL, MB, NB, max_seq_len, window, out);
+  oracle_paged_attention_int4_ex(q, pages, bt, ctx, B, QL, H, H, D, MB, NB, BS, max_seq_len, window, 0, out);
 }

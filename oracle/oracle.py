@@ -144,28 +144,32 @@ def evict_cache(scores, kpool, vpool, retain_ratio) -> None:
                              F32(retain_ratio))
 
 
-def paged_attention_f16(q, kpool, vpool, block_tables, context_lens, max_seq_len, window_size):
-    """fp64 output [B, QL, H, D]."""
+def paged_attention_f16(q, kpool, vpool, block_tables, context_lens, max_seq_len, window_size, causal=False):
+    """fp64 output [B, QL, H, D].  The pool's head count (kpool.shape[2]) may
+    divide H (grouped-query attention: query head h reads KV head h / (H/KVH));
+    causal=True: row i is the token at ctx - QL + i (an extension)."""
     q = _c(q, np.float16)
     B, QL, H, D = q.shape
-    NB, BS = kpool.shape[0], kpool.shape[1]
+    NB, BS, KVH = kpool.shape[0], kpool.shape[1], kpool.shape[2]
     bt, cl = _c(block_tables, np.int32), _c(context_lens, np.int32)
     out = np.zeros((B, QL, H, D), np.float64)
-    lib().oracle_paged_attention_f16(_p(q), _p(_c(kpool)), _p(_c(vpool)), _p(bt), _p(cl), I32(B),
-                                     I32(QL), I32(H), I32(D), I32(bt.shape[1]), I64(NB), I32(BS),
-                                     I32(max_seq_len), I32(window_size), _p(out))
+    lib().oracle_paged_attention_f16_ex(_p(q), _p(_c(kpool)), _p(_c(vpool)), _p(bt), _p(cl), I32(B),
+                                        I32(QL), I32(H), I32(KVH), I32(D), I32(bt.shape[1]), I64(NB), I32(BS),
+                                        I32(max_seq_len), I32(window_size), I32(int(causal)), _p(out))
     return out
 
 
-def paged_attention_int4(q, pages, block_tables, context_lens, max_seq_len, window_size, block_size):
+def paged_attention_int4(q, pages, block_tables, context_lens, max_seq_len, window_size, block_size,
+                         causal=False):
+    """pages [NB, KVH, page_bytes]; KVH may divide H as in paged_attention_f16."""
     q = _c(q, np.float16)
     B, QL, H, D = q.shape
-    NB = pages.shape[0]
+    NB, KVH = pages.shape[0], pages.shape[1]
     bt, cl = _c(block_tables, np.int32), _c(context_lens, np.int32)
     out = np.zeros((B, QL, H, D), np.float64)
-    lib().oracle_paged_attention_int4(_p(q), _p(_c(pages)), _p(bt), _p(cl), I32(B), I32(QL), I32(H), I32(D),
-                                      I32(bt.shape[1]), I64(NB), I32(block_size), I32(max_seq_len),
-                                      I32(window_size), _p(out))
+    lib().oracle_paged_attention_int4_ex(_p(q), _p(_c(pages)), _p(bt), _p(cl), I32(B), I32(QL), I32(H), I32(KVH),
+                                         I32(D), I32(bt.shape[1]), I64(NB), I32(block_size), I32(max_seq_len),
+                                         I32(window_size), I32(int(causal)), _p(out))
     return out
 
 

@@ -137,3 +137,26 @@ def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
                                        F(retain_ratio), I(sinks), ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt),
                                        ptr(ws), SZ(wsb), stream()))
     return kept, cnt, freed, fcnt
+
+
+def attention_f16_ex(q, kpool, vpool, bt, ctx, msl, win, causal=False):
+    """memopt_paged_attention_f16_ex: the pool's head count may divide H."""
+    B, QL, H, D = q.shape
+    MB = bt.shape[1]
+    out = torch.empty_like(q)
+    ws, n = workspace(B, QL, H, D, MB, kpool.shape[1], msl, win)
+    ok(lib().memopt_paged_attention_f16_ex(ptr(q), ptr(kpool), ptr(vpool), ptr(bt), ptr(ctx), I(B), I(QL), I(H),
+                                           I(kpool.shape[2]), I(D), I(MB), I64(kpool.shape[0]), I(kpool.shape[1]),
+                                           I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))
+    return out
+
+
+def attention_int4_ex(q, pages, block_size, bt, ctx, msl, win, causal=False):
+    B, QL, H, D = q.shape
+    MB = bt.shape[1]
+    out = torch.empty_like(q)
+    ws, n = workspace(B, QL, H, D, MB, block_size, msl, win)
+    ok(lib().memopt_paged_attention_int4_ex(ptr(q), ptr(pages), ptr(bt), ptr(ctx), I(B), I(QL), I(H),
+                                            I(pages.shape[1]), I(D), I(MB), I64(pages.shape[0]), I(block_size),
+                                            I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))
+    return out

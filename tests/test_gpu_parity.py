@@ -318,6 +318,58 @@ def test_attention_int4_long_context_stress(qmul, vmean, win):
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
 
 
+GQA_CASES = [
+    # B, QL, H, KVH, D, BS, ctx, MB, max_seq_len, window, causal, holes
+    (2, 1, 8, 2, 128, 16, [700, 1000], 64, 1024, 1024, False, 0.0),     # decode, GQA 4
+    (2, 3, 8, 8, 64, 16, [300, 301], 20, 320, 320, True, 0.1),          # multi-row decode, causal
+    (2, 5, 8, 1, 128, 32, [400, 90], 16, 512, 100, True, 0.0),          # MQA, causal, window
+    (1, 1, 4, 2, 128, 16, [40000], 2500, 40000, 40000, False, 0.0),     # split-K, GQA
+    (1, 200, 4, 2, 128, 16, [777], 64, 1024, 1024, True, 0.0),          # prefill, causal, GQA
+    (2, 130, 8, 2, 64, 16, [300, 1000], 64, 1024, 256, True, 0.1),      # prefill, causal window, holes
+    (1, 512, 2, 1, 128, 32, [4096], 128, 4096, 4096, False, 0.0),       # prefill, MQA, non-causal
+    (1, 300, 2, 2, 128, 16, [300], 32, 512, 512, True, 0.0),            # prefill: rows == context
+]
+
+
+def _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, seed):
+    rng = np.random.default_rng(seed)
+    NB = B * MB + 5
+    bt = rng.permutation(NB)[: B * MB].astype(np.int32).reshape(B, MB)
+    if holes:
+        bt[rng.random(bt.shape) < holes] = -1
+    kp = rng.standard_normal((NB, BS, KVH, D)).astype(np.float16)
+    vp = rng.standard_normal((NB, BS, KVH, D)).astype(np.float16)
+    q = rng.standard_normal((B, QL, H, D)).astype(np.float16)
+    return q, kp, vp, bt, np.asarray(ctx, np.int32)
+
+
+@pytest.mark.parametrize("case", GQA_CASES)
+def test_attention_gqa_causal_f16_vs_oracle(case):
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = case
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, QL * 7 + H)
+    got = capi.attention_f16_ex(torch.from_numpy(q).to(DEV), torch.from_numpy(kp).to(DEV),
+                                torch.from_numpy(vp).to(DEV), torch.from_numpy(bt).to(DEV),
+                                torch.from_numpy(cl).to(DEV), msl, win, causal)
+    ref = O.paged_attention_f16(q, kp, vp, bt, cl, msl, win, causal=causal)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("case", [c for c in GQA_CASES if c[1] < 64])
+def test_attention_gqa_causal_int4_vs_oracle(case):
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = case
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, QL * 11 + H)
+    NB = kp.shape[0]
+    T = NB * BS
+    pages = torch.zeros(NB, KVH, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(torch.from_numpy(kp.reshape(T, KVH, D)).to(DEV),
+                          torch.from_numpy(vp.reshape(T, KVH, D)).to(DEV),
+                          torch.from_numpy(np.arange(T, dtype=np.int32)).to(DEV), pages, BS)
+    got = capi.attention_int4_ex(torch.from_numpy(q).to(DEV), pages, BS, torch.from_numpy(bt).to(DEV),
+                                 torch.from_numpy(cl).to(DEV), msl, win, causal)
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS, causal=causal)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
 def test_attention_deterministic_and_workspace_reuse():
     B, QL, H, D, BS, ctx, MB, msl, win, holes = ATTN_CASES[7]
     q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, 11, holes)
