@@ -409,6 +409,10 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       }
     } else {
       using namespace int4mma;
+      // Whether every token of the pages in this sub-window is visible (the
+      // usual case): then no tile needs per-token masking.
+      const bool sub_interior = mask != 0 && (c_lo + __ffs(mask) - 1) * BS >= win_start &&
+                                (c_lo + 32 - __clz(mask)) * BS <= ctx;
       // Two 16-token tiles per softmax step: both halves of a 32-token page,
       // or two consecutive 16-token pages of the item.
       while (mask != 0) {
@@ -470,8 +474,13 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           }
           // Lanes mt4 >= G compute a value that is never used: the group sum
           // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
+#ifdef MEMOPT_XP_NOEPI
+          float a_lo = __int_as_float(c[0] ^ c[1]) * 1e-30f;
+          float a_hi = __int_as_float(c[2] ^ c[3]) * 1e-30f;
+#else
           float a_lo = ks_lo * static_cast<float>(c[0] * 256 + c[1]);
           float a_hi = ks_hi * static_cast<float>(c[2] * 256 + c[3]);
+#endif
           if constexpr (G > 1) {
             a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
             a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
@@ -482,22 +491,40 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           a_lo *= sfac;
           a_hi *= sfac;
           const int tl = ttok[ti] + mg;
-          const bool interior = ttok[ti] >= win_start && ttok[ti] + 16 <= ctx;
+          const bool interior = sub_interior || (ttok[ti] >= win_start && ttok[ti] + 16 <= ctx);
+#ifdef MEMOPT_XP_NOMASK
+          slo[ti] = a_lo; shi[ti] = a_hi; (void)interior; (void)tl;
+#else
           slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
           shi[ti] = (interior || (tl + 8 >= win_start && tl + 8 < ctx)) ? a_hi : -INFINITY;
+#endif
         }
+#ifdef MEMOPT_XP_NOSMX
+        const float m_new = 0.f;
+#else
+        // Step max over the lanes that own scores (mt4 == 0), in one warp
+        // reduction on an order-preserving integer image of the floats
+        // (f >= 0: its bits; f < 0: bits ^ 0x7fffffff; the map is its own inverse).
         float mp = fmaxf(fmaxf(slo[0], shi[0]), fmaxf(slo[1], shi[1]));
-#pragma unroll
-        for (int mk = 16; mk >= 4; mk >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, mk));
-        mp = __shfl_sync(0xffffffffu, mp, 0);
+        int mk = __float_as_int(mt4 == 0 ? mp : -INFINITY);
+        mk ^= (mk >> 31) & 0x7fffffff;
+        mk = __reduce_max_sync(0xffffffffu, mk);
+        mk ^= (mk >> 31) & 0x7fffffff;
+        mp = __int_as_float(mk);
         const float m_new = fmaxf(m, mp);
+#endif
         if (m_new != -INFINITY) {
           const float alpha = ex2_approx(m - m_new);
           m = m_new;
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
+#ifdef MEMOPT_XP_NOSMX
+            slo[ti] = slo[ti] - m_new;
+            shi[ti] = shi[ti] - m_new;
+#else
             slo[ti] = ex2_approx(slo[ti] - m_new);
             shi[ti] = ex2_approx(shi[ti] - m_new);
+#endif
           }
           const float psum = (slo[0] + shi[0]) + (slo[1] + shi[1]);
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
@@ -531,8 +558,12 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             const uint32_t vs8c = lds_u32(vsa + 16);
             const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
             const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
+#ifdef MEMOPT_XP_NOBB
+            const uint32_t b0 = pk, b1 = pk ^ 0x00010001u; (void)b0h; (void)b1h;
+#else
             const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
             const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
+#endif
             const uint32_t vr = tb[ti] + tt[ti] * 16 * (D / 2) + o_v;
             uint32_t T0[2], T4[2], Y0[2], Y4[2];
             if constexpr (D == 128) {
