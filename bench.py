@@ -543,16 +543,22 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
     ev_bytes = 2 * eb * H * ectx * 4  # scores read + kept-index list written (no row is evicted with sinks)
     # Exact top-k eviction with compaction (this build's operator), one call
     # on the same scores: head sums, select, and the kept rows moved.
-    bt_c = bt.clone()
-    ctx_c = torch.full((eb,), ectx, dtype=torch.int32, device=dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    barrier()
-    e0.record(stream)
-    _, kcnt, _, _ = memopt_C.evict_topk_compact(scores, bt_c, ctx_c, 0.75, 4)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_topk = max_over_ranks(e0.elapsed_time(e1))
+    # (an untimed first call takes the workspace allocation; every call works
+    # on fresh copies of the tables and lengths: the same work each time)
+    topk_ms = []
+    for it in range(4):
+        bt_c = bt.clone()
+        ctx_c = torch.full((eb,), ectx, dtype=torch.int32, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        _, kcnt, _, _ = memopt_C.evict_topk_compact(scores, bt_c, ctx_c, 0.75, 4)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if it > 0:
+            topk_ms.append(e0.elapsed_time(e1))
+    ms_topk = max_over_ranks(statistics.median(topk_ms))
     kept_rows = int(kcnt.sum().item())
     topk_bytes = eb * H * ectx * 4 + 2 * 2 * kept_rows * H * D * 2  # scores + K/V rows read and written once
     q = torch.randn(eb, 1, H, D, dtype=torch.float16, device=dev, generator=g)
@@ -577,7 +583,7 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
                                                "(retain 0.75, 4 sinks), kept K/V rows compacted, pages released",
                                    "value": round(topk_bytes * ws_n / (ms_topk * 1e-3) / 1e9, 2), "unit": "GB/s",
                                    "ms_per_call": round(ms_topk, 4), "kept_rows": kept_rows,
-                                   "note": "one call, after the pool was filled; rows move through a workspace "
+                                   "note": "median of 3 calls after an untimed one; rows move through a workspace "
                                            "(read and written twice), the value counts them once"},
             "window_decode": {"workload": "BASELINE configs[3]: decode batch 8, ctx 32768, window 4096",
                               "value": round(dbytes * ws_n / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",

@@ -472,36 +472,24 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             a[3] = s8x16_odd(w1[kb], kS8);
             mma_s8(c, a, qb[kb][0], qb[kb][1]);
           }
-          // Lanes mt4 >= G compute a value that is never used: the group sum
-          // is exchanged between lanes mt4 = 0, 1 and broadcast from lane 0.
-#ifdef MEMOPT_XP_NOEPI
-          float a_lo = __int_as_float(c[0] ^ c[1]) * 1e-30f;
-          float a_hi = __int_as_float(c[2] ^ c[3]) * 1e-30f;
-#else
+          // Lanes mt4 >= G compute a value that is never used: the two group
+          // sums meet in lanes mt4 = 0, 1.
           float a_lo = ks_lo * static_cast<float>(c[0] * 256 + c[1]);
           float a_hi = ks_hi * static_cast<float>(c[2] * 256 + c[3]);
-#endif
           if constexpr (G > 1) {
             a_lo += __shfl_xor_sync(0xffffffffu, a_lo, 1);
             a_hi += __shfl_xor_sync(0xffffffffu, a_hi, 1);
           }
           // Only lanes mt4 == 0 hold the scores from here on: they are the
-          // only sources of the P.V operand and of l (other lanes' values are
-          // never read; the running max is taken from lane 0).
+          // only sources of the P.V operand, of l and of the step max (other
+          // lanes' values are never read).
           a_lo *= sfac;
           a_hi *= sfac;
           const int tl = ttok[ti] + mg;
           const bool interior = sub_interior || (ttok[ti] >= win_start && ttok[ti] + 16 <= ctx);
-#ifdef MEMOPT_XP_NOMASK
-          slo[ti] = a_lo; shi[ti] = a_hi; (void)interior; (void)tl;
-#else
           slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
           shi[ti] = (interior || (tl + 8 >= win_start && tl + 8 < ctx)) ? a_hi : -INFINITY;
-#endif
         }
-#ifdef MEMOPT_XP_NOSMX
-        const float m_new = 0.f;
-#else
         // Step max over the lanes that own scores (mt4 == 0), in one warp
         // reduction on an order-preserving integer image of the floats
         // (f >= 0: its bits; f < 0: bits ^ 0x7fffffff; the map is its own inverse).
@@ -512,19 +500,13 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         mk ^= (mk >> 31) & 0x7fffffff;
         mp = __int_as_float(mk);
         const float m_new = fmaxf(m, mp);
-#endif
         if (m_new != -INFINITY) {
           const float alpha = ex2_approx(m - m_new);
           m = m_new;
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
-#ifdef MEMOPT_XP_NOSMX
-            slo[ti] = slo[ti] - m_new;
-            shi[ti] = shi[ti] - m_new;
-#else
             slo[ti] = ex2_approx(slo[ti] - m_new);
             shi[ti] = ex2_approx(shi[ti] - m_new);
-#endif
           }
           const float psum = (slo[0] + shi[0]) + (slo[1] + shi[1]);
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
@@ -558,12 +540,8 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             const uint32_t vs8c = lds_u32(vsa + 16);
             const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
             const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
-#ifdef MEMOPT_XP_NOBB
-            const uint32_t b0 = pk, b1 = pk ^ 0x00010001u; (void)b0h; (void)b1h;
-#else
             const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
             const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
-#endif
             const uint32_t vr = tb[ti] + tt[ti] * 16 * (D / 2) + o_v;
             uint32_t T0[2], T4[2], Y0[2], Y4[2];
             if constexpr (D == 128) {
