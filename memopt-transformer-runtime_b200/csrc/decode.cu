@@ -13,6 +13,10 @@
 
 #include "decode_kernel.cuh"
 
+#ifndef MEMOPT_SPLIT_F16
+#define MEMOPT_SPLIT_F16 3
+#endif
+
 namespace memopt {
 
 // prefill.cu: tcgen05 path for q_len >= kPrefillMinRows.
@@ -76,18 +80,23 @@ struct Split {
   int n_chunks = 1;
 };
 
-// Chooses the page-chunk size so that the item count fills every warp slot of
-// the machine several times over (the tail wave stays small).  A chunk may
-// span any number of pages (the kernel walks it in 32-page sub-windows), so
-// calls with many query rows need no split-K partials at all.
-Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window) {
+// Chooses the page-chunk size: the item count is aimed at `twice_target` / 2
+// items per fp16 warp slot of the machine (8 warps per SM), balancing the
+// tail wave against per-item cost (split-K partials and their merge).  A
+// chunk may span any number of pages (the kernel walks it in 32-page
+// sub-windows), so calls with many query rows need no partials at all.
+// Measured on B200: fp16 decode is fastest near 1.5 items per slot, the INT4
+// kernel (16 warps per SM, cheaper items) near 4.
+constexpr int kSplitF16 = MEMOPT_SPLIT_F16;
+constexpr int kSplitInt4 = 8;
+Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window, int twice_target) {
   Split s;
   const int64_t wpages =
       window > 0 ? (static_cast<int64_t>(window) + block_size - 1) / block_size + 1 : 0;
   int max_pages = static_cast<int>(wpages < max_blocks_per_seq ? wpages : max_blocks_per_seq);
   if (max_pages < 1) max_pages = 1;
   const int64_t warp_slots = static_cast<int64_t>(sm_count()) * 2 * 4;
-  const int64_t target = warp_slots * 4;
+  const int64_t target = warp_slots * twice_target / 2;
   int64_t n = (target + pairs - 1) / pairs;
   // Keep at least 4 pages per item so partials stay a small share of traffic.
   const int max_chunks = max_pages >= 4 ? max_pages / 4 : 1;
@@ -157,7 +166,7 @@ int dispatch(const Params& p, int D, int BS, const CUtensorMap& km, const CUtens
 
 int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t* ctx, int batch,
                  int q_len, int H, int KVH, int D, int MB, int64_t NB, int BS, int max_seq_len, int window,
-                 int causal, void* out, void* ws, size_t ws_bytes) {
+                 int causal, bool int4, void* out, void* ws, size_t ws_bytes) {
   if (batch < 0 || q_len < 0 || H < 0 || D < 0 || MB < 0 || NB < 0)
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: negative size");
   if (KVH <= 0 || (H > 0 && H % KVH != 0))
@@ -182,7 +191,7 @@ int common_setup(Params& p, const void* query, const int32_t* bt, const int32_t*
   p.magic_f16 = 0x64006400u;
   p.magic_s8 = 0x80808080u;
   const int64_t pairs = static_cast<int64_t>(batch) * q_len * H;
-  const Split sp = choose_split(pairs, MB, BS, p.window);
+  const Split sp = choose_split(pairs, MB, BS, p.window, int4 ? kSplitInt4 : kSplitF16);
   p.chunk_pages = sp.chunk_pages;
   p.n_chunks = sp.n_chunks;
   p.total_items = pairs * sp.n_chunks;
@@ -220,9 +229,13 @@ extern "C" size_t memopt_paged_attention_workspace_size(int batch, int q_len, in
                                                         int window_size) {
   if (batch <= 0 || q_len <= 0 || num_heads <= 0 || head_dim <= 0 || block_size <= 0) return 0;
   const int64_t pairs = static_cast<int64_t>(batch) * q_len * num_heads;
-  const Split sp =
-      choose_split(pairs, max_blocks_per_seq, block_size, clamp_window(window_size, max_seq_len));
-  return ws_layout(pairs, sp.n_chunks, head_dim).total;
+  // One size serves both formats (they split differently): the larger need.
+  const int w = clamp_window(window_size, max_seq_len);
+  const size_t a = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitF16).n_chunks,
+                             head_dim).total;
+  const size_t b = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitInt4).n_chunks,
+                             head_dim).total;
+  return a > b ? a : b;
 }
 
 extern "C" size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads) {
@@ -239,7 +252,7 @@ extern "C" int memopt_paged_attention_f16_ex(const void* query, const void* key_
                                              void* workspace, size_t workspace_bytes, void* stream) {
   Params p{};
   int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, num_kv_heads, head_dim,
-                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, out,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, false, out,
                         workspace, workspace_bytes);
   if (st != MEMOPT_OK) return st;
   if (p.total_items == 0) return MEMOPT_OK;
@@ -282,7 +295,7 @@ extern "C" int memopt_paged_attention_int4_ex(const void* query, const uint8_t* 
                                               void* stream) {
   Params p{};
   int st = common_setup(p, query, block_tables, context_lens, batch, q_len, num_heads, num_kv_heads, head_dim,
-                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, out,
+                        max_blocks_per_seq, num_blocks, block_size, max_seq_len, window_size, causal, true, out,
                         workspace, workspace_bytes);
   if (st != MEMOPT_OK) return st;
   if (p.total_items == 0) return MEMOPT_OK;
