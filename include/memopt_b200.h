@@ -165,8 +165,10 @@ int memopt_evict_tokens(const float* scores, int num_seqs, int num_heads, int se
 /* max_len] (ascending original indices, -1 pad); kept_count int32            */
 /* [num_seqs]; freed_pages int32 [num_seqs, max_blocks_per_seq]; freed_count  */
 /* int32 [num_seqs].  max_len <= 32768, max_blocks_per_seq <= 2048; fp16      */
-/* pools in reference layout.  The workspace (16-byte aligned) holds the      */
-/* moved rows: memopt_evict_topk_workspace_size() bytes.                       */
+/* pools in reference layout; a physical page appears at most once in the   */
+/* tables.  Rows move in place.  The workspace (16-byte aligned,               */
+/* memopt_evict_topk_workspace_size() bytes: about 16 B per token plus 8 B    */
+/* per 4 tokens, no K/V rows) holds tables, ordinals and move flags.          */
 /* ------------------------------------------------------------------------ */
 size_t memopt_evict_topk_workspace_size(int num_seqs, int max_len, int num_heads, int head_dim);
 int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, int max_len,
@@ -176,6 +178,25 @@ int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, 
                               int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
                               int32_t* freed_count, void* workspace, size_t workspace_bytes,
                               void* stream);
+
+/* Head-sharded form of the same operator (the one cross-GPU exchange of the  */
+/* data plane): with the heads of every sequence split over G ranks, rank r   */
+/* writes the fp32 sum of its own heads' scores (heads in order) with         */
+/* memopt_evict_topk_head_sum -> sums [num_seqs, max_len]; the G rows are      */
+/* exchanged (an all-gather) into partial_sums [G, num_seqs, max_len] in rank */
+/* order, and memopt_evict_topk_compact_parts ranks tokens by the fp32 sum of */
+/* the G parts in rank order, then compacts this rank's pool (num_heads =     */
+/* the heads this rank holds).  All ranks reach the same decision; with G = 1 */
+/* the result equals memopt_evict_topk_compact's bit for bit.                  */
+int memopt_evict_topk_head_sum(const float* scores, int num_seqs, int num_heads, int max_len,
+                               float* sums, void* stream);
+int memopt_evict_topk_compact_parts(const float* partial_sums, int num_parts, int num_seqs, int max_len,
+                                    int32_t* block_tables, int max_blocks_per_seq, int32_t* context_lens,
+                                    void* key_pool, void* value_pool, int pool_num_blocks, int block_size,
+                                    int num_heads, int head_dim, float retain_ratio, int num_sink_tokens,
+                                    int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
+                                    int32_t* freed_count, void* workspace, size_t workspace_bytes,
+                                    void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* evict_cache (kv_cache.cu:379-559): per (physical block, head) keep the     */

@@ -18,10 +18,19 @@
 //     0..keep-1 over the sequence's valid pages; the block-table row becomes
 //     those first ceil(keep / block_size) valid pages (then -1), the others
 //     are reported as freed, and context_lens[b] becomes keep.
-// Four launches: head sums (parallel over tokens), one CTA per sequence for
-// the select + compaction indices, then a gather of the kept rows into the
-// workspace and a scatter back (in place the moves would race: a token's
-// destination can be an earlier token's source).
+// With heads sharded over G ranks, each rank sums its own heads
+// (memopt_evict_topk_head_sum), the G partial rows are exchanged, and
+// memopt_evict_topk_compact_parts ranks tokens by the fp32 sum of the parts in
+// rank order: every rank takes the same decision and compacts the rows of
+// its own heads.  With G = 1 this is exactly memopt_evict_topk_compact.
+// Three launches: head sums (parallel over tokens), one CTA per sequence for
+// the selection, the new block-table row and each kept row's source ordinal
+// (its slot's position among the sequence's valid pages), then the kept rows
+// move in place.  A row only moves forward (destination ordinal <= source
+// ordinal), so the one hazard is overwriting a slot before the row that
+// lives there has been read; the move kernel orders exactly those pairs.
+#include <climits>
+
 #include "common.cuh"
 #include "memopt_b200.h"
 
@@ -31,14 +40,25 @@ namespace {
 constexpr int kSelThreads = 1024;
 constexpr int kMaxLen = 32768;
 constexpr int kVPT = kMaxLen / kSelThreads;  // 32 tokens per thread
+// Kept rows moved by one CTA.  At 8 sequences x 32768 tokens x 8 KB rows
+// (retain 0.75) one row per CTA moved the rows in 1.17 ms, 2 in 1.19 ms,
+// 4 in 1.29 ms and 8 in 1.73 ms: small CTAs keep more copies in flight.
+constexpr int kSegRows = 1;
+constexpr int kMaxSegs = kMaxLen / kSegRows;
+constexpr int kMoveSmemLimit = 200 * 1024;       // 2 * kSegRows rows staged in shared memory
 
-__global__ void head_sum_kernel(const float* __restrict__ scores, int H, int max_len, float* __restrict__ sums) {
+// sums[b, t] = fp32 sum over i in order of src[b * b_stride + i * i_stride + t].
+// Per-head scores [B, H, L] are (b_stride, i_stride) = (H*L, L); the partial
+// sums of G ranks stacked as [G, B, L] are (L, B*L).  The sum starts at +0, so
+// it is never -0 (the integer keys below order -0 below +0).
+__global__ void head_sum_kernel(const float* __restrict__ src, int64_t b_stride, int64_t i_stride, int n_terms,
+                                int max_len, float* __restrict__ sums) {
   const int b = blockIdx.y;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= max_len) return;
-  const float* src = scores + static_cast<int64_t>(b) * H * max_len + t;
+  const float* p = src + static_cast<int64_t>(b) * b_stride + t;
   float s = 0.f;
-  for (int h = 0; h < H; ++h) s += __ldg(src + static_cast<int64_t>(h) * max_len);
+  for (int i = 0; i < n_terms; ++i) s += __ldg(p + static_cast<int64_t>(i) * i_stride);
   sums[static_cast<int64_t>(b) * max_len + t] = s;
 }
 
@@ -76,9 +96,11 @@ __global__ void __launch_bounds__(kSelThreads, 1)
 topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restrict__ bt, int MB,
                    int32_t* __restrict__ ctx_lens, int NB, int BS, float retain_ratio, int num_sinks,
                    int32_t* __restrict__ kept_idx, int32_t* __restrict__ kept_count,
-                   int32_t* __restrict__ freed, int32_t* __restrict__ freed_count) {
+                   int32_t* __restrict__ freed, int32_t* __restrict__ freed_count,
+                   int32_t* __restrict__ src_ord, int32_t* __restrict__ seg_dep) {
   __shared__ int hist[256];
   __shared__ int warp_sums[32];
+  __shared__ int page_rank[2 * kSelThreads];  // rank of each valid page among the row's valid pages
   __shared__ uint32_t sh_prefix;
   __shared__ int sh_remaining;
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -183,17 +205,10 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
   }
   int total = 0;
   int pos = block_excl_scan(__popc(kept), warp_sums, &total);
-  int32_t* kout = kept_idx + static_cast<int64_t>(b) * max_len;
-#pragma unroll
-  for (int i = 0; i < kVPT; ++i)
-    if ((kept >> i) & 1u) kout[pos++] = t0 + i;
-  for (int t = total + tid; t < max_len; t += kSelThreads) kout[t] = -1;
 
-  // New block-table row: the first ceil(total / BS) valid pages, in order;
-  // every other valid page is reported as freed.  (The table entries are
-  // read into registers before any is rewritten.)
-  const int need_pages = (total + BS - 1) / BS;
-  int32_t* frow = freed + static_cast<int64_t>(b) * MB;
+  // Ranks of the valid pages (the new row is the first ceil(total / BS) of
+  // them, in order).  The table entries are read into registers here, before
+  // any is rewritten.
   constexpr int kPPT = 2;  // MB <= 2048 = kSelThreads * kPPT
   int pg[kPPT];
   int pvalid = 0;
@@ -204,11 +219,47 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
     if (pg[k] >= 0 && pg[k] < NB) ++pvalid;
   }
   int nvp = 0;
-  int vrank = block_excl_scan(pvalid, warp_sums, &nvp);
-  __syncthreads();  // all entries read
+  const int vrank0 = block_excl_scan(pvalid, warp_sums, &nvp);
+  {
+    int v = vrank0;
+#pragma unroll
+    for (int k = 0; k < kPPT; ++k) {
+      const int lb = tid * kPPT + k;
+      if (lb < MB) page_rank[lb] = (pg[k] >= 0 && pg[k] < NB) ? v++ : -1;
+    }
+  }
+  const int nseg = (total + kSegRows - 1) / kSegRows;
+  int32_t* dep = seg_dep + static_cast<int64_t>(b) * kMaxSegs;
+  for (int k = tid; k < nseg; k += kSelThreads) dep[k] = INT_MAX;
+  __syncthreads();
+
+  // Kept rows in token order.  Row `pos` moves from ordinal src (the token's
+  // position among the valid pages' slots) to ordinal pos <= src.  A segment
+  // of kSegRows destination rows may only be written after every row whose
+  // source lies in it has been read: dep[segment] = the lowest segment with
+  // such a row (those rows are consecutive, so they span at most that
+  // segment and the next one).
+  int32_t* kout = kept_idx + static_cast<int64_t>(b) * max_len;
+  int32_t* oout = src_ord + static_cast<int64_t>(b) * max_len;
+#pragma unroll
+  for (int i = 0; i < kVPT; ++i) {
+    if ((kept >> i) & 1u) {
+      const int t = t0 + i;
+      const int so = page_rank[t / BS] * BS + t % BS;
+      kout[pos] = t;
+      oout[pos] = so;
+      if (so / kSegRows != pos / kSegRows) atomicMin(&dep[so / kSegRows], pos / kSegRows);
+      ++pos;
+    }
+  }
+  for (int t = total + tid; t < max_len; t += kSelThreads) kout[t] = -1;
+
+  const int need_pages = (total + BS - 1) / BS;
+  int32_t* frow = freed + static_cast<int64_t>(b) * MB;
   for (int lb = tid; lb < MB; lb += kSelThreads) btrow[lb] = -1;
   for (int lb = tid; lb < MB; lb += kSelThreads) frow[lb] = -1;
   __syncthreads();
+  int vrank = vrank0;
 #pragma unroll
   for (int k = 0; k < kPPT; ++k) {
     if (pg[k] >= 0 && pg[k] < NB) {
@@ -224,102 +275,220 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
   }
 }
 
-// One warp per kept row: gather (dir = 0: pool -> workspace) or scatter
-// (dir = 1: workspace -> pool).  Rows are H*D fp16 = `chunks` 16-byte pieces.
-__global__ void move_rows_kernel(const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ kept_count,
-                                 const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB,
-                                 int max_len, int BS, uint4* __restrict__ kpool, uint4* __restrict__ vpool,
-                                 uint4* __restrict__ ktmp, uint4* __restrict__ vtmp, int chunks, int dir) {
-  const int b = blockIdx.y;
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= kept_count[b]) return;
-  const int64_t trow = static_cast<int64_t>(b) * max_len + row;
-  int64_t slot;
-  if (dir == 0) {
-    const int t = kept_idx[trow];
-    slot = static_cast<int64_t>(old_bt[static_cast<int64_t>(b) * MB + t / BS]) * BS + t % BS;
-  } else {
-    slot = static_cast<int64_t>(new_bt[static_cast<int64_t>(b) * MB + row / BS]) * BS + row % BS;
-  }
-  uint4* kp = kpool + slot * chunks;
-  uint4* vp = vpool + slot * chunks;
-  uint4* kt = ktmp + trow * chunks;
-  uint4* vt = vtmp + trow * chunks;
-  for (int c = lane; c < chunks; c += 32) {
-    if (dir == 0) {
-      kt[c] = kp[c];
-      vt[c] = vp[c];
-    } else {
-      kp[c] = kt[c];
-      vp[c] = vt[c];
+// In-place move of the kept rows, kSegRows rows per CTA (one thread issues
+// bulk copies).  Segments are handed out in order by a ticket counter, so
+// every lower segment of the same sequence is already resident or finished
+// when a segment waits on it.  A segment bulk-loads its moving rows (K and V)
+// into shared memory, publishes "read" in flags[ticket], waits until the
+// (at most two) segments whose rows read its destination slots have
+// published, then bulk-stores its rows.  Reads never wait, so every wait
+// ends; each is still bounded, recording 1 in ctrl[1] if it gives up.
+// Rows whose source is already their destination are not touched.
+__global__ void __launch_bounds__(32) move_rows_inplace_kernel(
+    const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ src_ord,
+    const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
+    const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
+    int nseg, uint8_t* __restrict__ kpool, uint8_t* __restrict__ vpool, uint32_t row_bytes, int* ctrl,
+    int* flags) {
+  if (threadIdx.x != 0) return;
+  extern __shared__ __align__(128) uint8_t stage[];
+  __shared__ __align__(8) uint64_t bar;
+  const int ticket = atomicAdd(&ctrl[0], 1);
+  const int b = ticket / nseg, k = ticket % nseg;
+  const int cnt = kept_count[b];
+  const int r0 = k * kSegRows;
+  if (r0 >= cnt) return;  // no segment waits on one past the kept rows
+  const int nr = min(kSegRows, cnt - r0);
+  const int64_t rb = static_cast<int64_t>(b) * max_len;
+  const int32_t* obt = old_bt + static_cast<int64_t>(b) * MB;
+  const int32_t* nbt = new_bt + static_cast<int64_t>(b) * MB;
+  int64_t src[kSegRows], dst[kSegRows];
+  uint32_t moving = 0, bytes = 0;
+  for (int i = 0; i < nr; ++i) {
+    const int row = r0 + i;
+    const int t = kept_idx[rb + row];
+    src[i] = (static_cast<int64_t>(obt[t / BS]) * BS + t % BS) * row_bytes;
+    dst[i] = (static_cast<int64_t>(nbt[row / BS]) * BS + row % BS) * row_bytes;
+    if (src_ord[rb + row] != row) {
+      moving |= 1u << i;
+      bytes += 2 * row_bytes;
     }
   }
+  const uint32_t sbar = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+  const uint32_t sstage = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+  if (moving) {
+    mbar_init(sbar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(sbar, bytes);
+    for (int i = 0; i < nr; ++i) {
+      if (!((moving >> i) & 1u)) continue;
+      bulk_g2s(sstage + (2 * i) * row_bytes, kpool + src[i], row_bytes, sbar);
+      bulk_g2s(sstage + (2 * i + 1) * row_bytes, vpool + src[i], row_bytes, sbar);
+    }
+    uint32_t polls = 0;
+    while (!mbar_try_wait(sbar, 0)) {
+      if (++polls > kMaxPolls) {
+        atomicExch(&ctrl[1], 1);
+        break;
+      }
+    }
+  }
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flags + static_cast<int64_t>(b) * kMaxSegs + k), "r"(1) : "memory");
+  if (!moving) return;
+  const int d = seg_dep[static_cast<int64_t>(b) * kMaxSegs + k];
+  for (int m = d; m < k && m <= d + 1; ++m) {
+    const int* f = flags + static_cast<int64_t>(b) * kMaxSegs + m;
+    uint32_t polls = 0;
+    int v = 0;
+    while (true) {
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (v) break;
+      if (++polls > kMaxPolls) {
+        atomicExch(&ctrl[1], 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  for (int i = 0; i < nr; ++i) {
+    if (!((moving >> i) & 1u)) continue;
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(kpool + dst[i]),
+                 "r"(sstage + (2 * i) * row_bytes), "r"(row_bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(vpool + dst[i]),
+                 "r"(sstage + (2 * i + 1) * row_bytes), "r"(row_bytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 }  // namespace
 
-extern "C" __attribute__((visibility("default"))) size_t memopt_evict_topk_workspace_size(int num_seqs, int max_len, int num_heads, int head_dim) {
-  if (num_seqs <= 0 || max_len <= 0 || num_heads <= 0 || head_dim <= 0) return 0;
-  const size_t rows = static_cast<size_t>(num_seqs) * max_len;
-  const size_t mb = static_cast<size_t>(num_seqs) * (kMaxLen);  // old block-table copy (upper bound)
-  return rows * 4 + mb * 4 + 2 * rows * num_heads * head_dim * 2 + 256;
+// Workspace: old block tables, token sums, source ordinals, segment
+// dependencies and flags, and the ticket / status words.  No K/V rows: the
+// moves are in place.
+static size_t topk_ws_layout(int num_seqs, int max_len, size_t* off_sums, size_t* off_ord, size_t* off_dep,
+                             size_t* off_flags, size_t* off_ctrl) {
+  const size_t S = static_cast<size_t>(num_seqs);
+  size_t o = S * 2 * kSelThreads * 4;  // old block-table copy (max_blocks_per_seq <= 2048)
+  *off_sums = o;
+  o += S * max_len * 4;
+  *off_ord = o;
+  o += S * max_len * 4;
+  *off_dep = o;
+  o += S * kMaxSegs * 4;
+  *off_flags = o;
+  o += S * kMaxSegs * 4;
+  *off_ctrl = o;
+  return o + 256;
 }
 
-extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, int max_len,
-                                         int32_t* block_tables, int max_blocks_per_seq, int32_t* context_lens,
-                                         void* key_pool, void* value_pool, int pool_num_blocks, int block_size,
-                                         int head_dim, float retain_ratio, int num_sink_tokens,
-                                         int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
-                                         int32_t* freed_count, void* workspace, size_t workspace_bytes,
-                                         void* stream) {
+extern "C" __attribute__((visibility("default"))) size_t memopt_evict_topk_workspace_size(int num_seqs, int max_len, int num_heads, int head_dim) {
+  if (num_seqs <= 0 || max_len <= 0 || num_heads <= 0 || head_dim <= 0) return 0;
+  size_t a, b, c, d, e;
+  return topk_ws_layout(num_seqs, max_len, &a, &b, &c, &d, &e);
+}
+
+static int topk_compact(const char* who, const float* src, int64_t b_stride, int64_t i_stride, int n_terms,
+                        int num_seqs, int num_heads, int max_len, int32_t* block_tables, int max_blocks_per_seq,
+                        int32_t* context_lens, void* key_pool, void* value_pool, int pool_num_blocks,
+                        int block_size, int head_dim, float retain_ratio, int num_sink_tokens, int32_t* kept_idx,
+                        int32_t* kept_count, int32_t* freed_pages, int32_t* freed_count, void* workspace,
+                        size_t workspace_bytes, void* stream) {
   if (!(retain_ratio > 0.f && retain_ratio <= 1.f))
-    return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_compact: retain_ratio must be in (0, 1]");
-  if (num_seqs < 0 || num_heads <= 0 || max_len < 0 || max_blocks_per_seq < 0 || pool_num_blocks < 0 ||
+    return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": retain_ratio must be in (0, 1]");
+  if (n_terms <= 0 || num_seqs < 0 || num_heads <= 0 || max_len < 0 || max_blocks_per_seq < 0 || pool_num_blocks < 0 ||
       block_size <= 0 || head_dim <= 0)
-    return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_compact: invalid geometry");
-  if (max_len > kMaxLen) return fail(MEMOPT_ERR_UNSUPPORTED, "evict_topk_compact: max_len exceeds 32768");
+    return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": invalid geometry");
+  if (max_len > kMaxLen) return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": max_len exceeds 32768");
   if (max_blocks_per_seq > 2 * kSelThreads)
-    return fail(MEMOPT_ERR_UNSUPPORTED, "evict_topk_compact: more than 2048 blocks per sequence");
+    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": more than 2048 blocks per sequence");
   if ((num_heads * head_dim) % 8 != 0)
-    return fail(MEMOPT_ERR_UNSUPPORTED, "evict_topk_compact: num_heads * head_dim must be a multiple of 8");
+    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim must be a multiple of 8");
   if (num_seqs == 0 || max_len == 0) return MEMOPT_OK;
-  if (!scores || !block_tables || !context_lens || !key_pool || !value_pool || !kept_idx || !kept_count ||
+  if (!src || !block_tables || !context_lens || !key_pool || !value_pool || !kept_idx || !kept_count ||
       !freed_pages || !freed_count || !workspace)
-    return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_compact: null pointer");
+    return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": null pointer");
   if ((reinterpret_cast<uintptr_t>(key_pool) | reinterpret_cast<uintptr_t>(value_pool) |
        reinterpret_cast<uintptr_t>(workspace)) & 15u)
-    return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_compact: pools and workspace must be 16-byte aligned");
+    return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": pools and workspace must be 16-byte aligned");
   const size_t need = memopt_evict_topk_workspace_size(num_seqs, max_len, num_heads, head_dim);
-  if (workspace_bytes < need) return fail(MEMOPT_ERR_WORKSPACE, "evict_topk_compact: workspace too small");
+  if (workspace_bytes < need) return fail(MEMOPT_ERR_WORKSPACE, std::string(who) + ": workspace too small");
   cudaStream_t s = as_stream(stream);
-  const size_t rows = static_cast<size_t>(num_seqs) * max_len;
-  const int chunks = num_heads * head_dim / 8;
+  const uint32_t row_bytes = static_cast<uint32_t>(num_heads) * head_dim * 2;
+  const size_t stage_bytes = static_cast<size_t>(2 * kSegRows) * row_bytes;
+  if (stage_bytes > static_cast<size_t>(kMoveSmemLimit))
+    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim above " +
+                                             std::to_string(kMoveSmemLimit / (4 * kSegRows)));
+  cudaError_t ea = cudaFuncSetAttribute(move_rows_inplace_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        kMoveSmemLimit);
+  if (ea != cudaSuccess) return cuda_fail(ea, "evict_topk: shared-memory attribute");
+  size_t o_sums, o_ord, o_dep, o_flags, o_ctrl;
+  topk_ws_layout(num_seqs, max_len, &o_sums, &o_ord, &o_dep, &o_flags, &o_ctrl);
   uint8_t* w = static_cast<uint8_t*>(workspace);
-  uint4* ktmp = reinterpret_cast<uint4*>(w);
-  uint4* vtmp = ktmp + rows * chunks;
-  float* sums = reinterpret_cast<float*>(vtmp + rows * chunks);
-  int32_t* old_bt = reinterpret_cast<int32_t*>(sums + rows);
+  int32_t* old_bt = reinterpret_cast<int32_t*>(w);
+  float* sums = reinterpret_cast<float*>(w + o_sums);
+  int32_t* ord = reinterpret_cast<int32_t*>(w + o_ord);
+  int32_t* dep = reinterpret_cast<int32_t*>(w + o_dep);
+  int* flags = reinterpret_cast<int*>(w + o_flags);
+  int* ctrl = reinterpret_cast<int*>(w + o_ctrl);
   const size_t bt_bytes = static_cast<size_t>(num_seqs) * max_blocks_per_seq * 4;
   cudaError_t e = cudaMemcpyAsync(old_bt, block_tables, bt_bytes, cudaMemcpyDeviceToDevice, s);
-  if (e != cudaSuccess) return cuda_fail(e, "evict_topk_compact: block-table copy");
-  head_sum_kernel<<<dim3((max_len + 255) / 256, num_seqs), 256, 0, s>>>(scores, num_heads, max_len, sums);
+  if (e != cudaSuccess) return cuda_fail(e, (std::string(who) + ": block-table copy").c_str());
+  e = cudaMemsetAsync(flags, 0, static_cast<size_t>(num_seqs) * kMaxSegs * 4 + 256, s);
+  if (e != cudaSuccess) return cuda_fail(e, (std::string(who) + ": clearing flags").c_str());
+  head_sum_kernel<<<dim3((max_len + 255) / 256, num_seqs), 256, 0, s>>>(src, b_stride, i_stride, n_terms, max_len, sums);
   MEMOPT_LAUNCH_CHECK("head_sum_kernel launch");
   const int sinks = num_sink_tokens < 0 ? 0 : num_sink_tokens;
   topk_select_kernel<<<num_seqs, kSelThreads, 0, s>>>(sums, max_len, block_tables, max_blocks_per_seq, context_lens,
                                                       pool_num_blocks, block_size, retain_ratio, sinks, kept_idx,
-                                                      kept_count, freed_pages, freed_count);
+                                                      kept_count, freed_pages, freed_count, ord, dep);
   MEMOPT_LAUNCH_CHECK("topk_select_kernel launch");
-  const dim3 mgrid((max_len + 7) / 8, num_seqs);
-  move_rows_kernel<<<mgrid, 256, 0, s>>>(kept_idx, kept_count, old_bt, block_tables, max_blocks_per_seq, max_len,
-                                         block_size, static_cast<uint4*>(key_pool), static_cast<uint4*>(value_pool),
-                                         ktmp, vtmp, chunks, 0);
-  MEMOPT_LAUNCH_CHECK("move_rows_kernel (gather) launch");
-  move_rows_kernel<<<mgrid, 256, 0, s>>>(kept_idx, kept_count, old_bt, block_tables, max_blocks_per_seq, max_len,
-                                         block_size, static_cast<uint4*>(key_pool), static_cast<uint4*>(value_pool),
-                                         ktmp, vtmp, chunks, 1);
-  MEMOPT_LAUNCH_CHECK("move_rows_kernel (scatter) launch");
+  const int nseg = (max_len + kSegRows - 1) / kSegRows;
+  move_rows_inplace_kernel<<<num_seqs * nseg, 32, stage_bytes, s>>>(
+      kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
+      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags);
+  MEMOPT_LAUNCH_CHECK("move_rows_inplace_kernel launch");
   return MEMOPT_OK;
+}
+
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact(
+    const float* scores, int num_seqs, int num_heads, int max_len, int32_t* block_tables, int max_blocks_per_seq,
+    int32_t* context_lens, void* key_pool, void* value_pool, int pool_num_blocks, int block_size, int head_dim,
+    float retain_ratio, int num_sink_tokens, int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
+    int32_t* freed_count, void* workspace, size_t workspace_bytes, void* stream) {
+  return topk_compact("evict_topk_compact", scores, static_cast<int64_t>(num_heads) * max_len, max_len, num_heads,
+                      num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens, key_pool,
+                      value_pool, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens, kept_idx,
+                      kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
+}
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_head_sum(const float* scores, int num_seqs,
+                                                                                int num_heads, int max_len,
+                                                                                float* sums, void* stream) {
+  if (num_seqs < 0 || num_heads <= 0 || max_len < 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_head_sum: invalid geometry");
+  if (num_seqs == 0 || max_len == 0) return MEMOPT_OK;
+  if (!scores || !sums) return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_head_sum: null pointer");
+  head_sum_kernel<<<dim3((max_len + 255) / 256, num_seqs), 256, 0, as_stream(stream)>>>(
+      scores, static_cast<int64_t>(num_heads) * max_len, max_len, num_heads, max_len, sums);
+  MEMOPT_LAUNCH_CHECK("head_sum_kernel launch");
+  return MEMOPT_OK;
+}
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact_parts(
+    const float* partial_sums, int num_parts, int num_seqs, int max_len, int32_t* block_tables,
+    int max_blocks_per_seq, int32_t* context_lens, void* key_pool, void* value_pool, int pool_num_blocks,
+    int block_size, int num_heads, int head_dim, float retain_ratio, int num_sink_tokens, int32_t* kept_idx,
+    int32_t* kept_count, int32_t* freed_pages, int32_t* freed_count, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  return topk_compact("evict_topk_compact_parts", partial_sums, max_len, static_cast<int64_t>(num_seqs) * max_len,
+                      num_parts, num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens,
+                      key_pool, value_pool, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens,
+                      kept_idx, kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
 }
 
 }  // namespace memopt

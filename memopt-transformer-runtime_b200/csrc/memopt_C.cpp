@@ -328,6 +328,69 @@ pybind11::tuple evict_topk_compact(torch::Tensor attention_scores, torch::Tensor
   return pybind11::make_tuple(kept, cnt, freed, fcnt);
 }
 
+// Head-sharded exact eviction, step 1: this rank's partial token scores
+// (fp32 sum of its heads, in order), float32 [num_seqs, max_len].
+torch::Tensor evict_topk_head_sum(torch::Tensor attention_scores) {
+  TORCH_CHECK(attention_scores.is_cuda() && attention_scores.dim() == 3 &&
+                  attention_scores.scalar_type() == torch::kFloat32,
+              "evict_topk_head_sum: attention_scores must be a CUDA float32 [num_seqs, num_heads, max_len] tensor");
+  attention_scores = attention_scores.contiguous();
+  const int S = static_cast<int>(attention_scores.size(0));
+  const int H = static_cast<int>(attention_scores.size(1));
+  const int L = static_cast<int>(attention_scores.size(2));
+  TORCH_CHECK(H > 0, "evict_topk_head_sum: no heads");
+  const at::cuda::CUDAGuard g(attention_scores.device());
+  auto sums = torch::empty({S, L}, attention_scores.options());
+  check(memopt_evict_topk_head_sum(attention_scores.data_ptr<float>(), S, H, L, sums.data_ptr<float>(),
+                                   cur_stream()),
+        "evict_topk_head_sum");
+  return sums;
+}
+
+// Head-sharded exact eviction, step 2: partial_sums float32 [G, num_seqs,
+// max_len] (every rank's evict_topk_head_sum, in rank order) decide; this
+// rank's pool (its heads) is compacted.  Same outputs and in-place updates as
+// evict_topk_compact.
+pybind11::tuple evict_topk_compact_parts(torch::Tensor partial_sums, torch::Tensor block_tables,
+                                         torch::Tensor context_lens, float retain_ratio, int num_sink_tokens) {
+  TORCH_CHECK(P().live && memopt_pool_is_initialized(), "evict_topk_compact_parts: pool not initialized");
+  auto& p = P();
+  TORCH_CHECK(!p.int4, "evict_topk_compact_parts: needs the fp16 pool");
+  TORCH_CHECK(partial_sums.dim() == 3 && partial_sums.scalar_type() == torch::kFloat32,
+              "evict_topk_compact_parts: partial_sums must be float32 [num_parts, num_seqs, max_len]");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.scalar_type() == torch::kInt32 && block_tables.is_contiguous(),
+              "evict_topk_compact_parts: block_tables must be a contiguous int32 [num_seqs, max_blocks_per_seq] "
+              "tensor");
+  TORCH_CHECK(context_lens.dim() == 1 && context_lens.scalar_type() == torch::kInt32 && context_lens.is_contiguous(),
+              "evict_topk_compact_parts: context_lens must be a contiguous int32 [num_seqs] tensor");
+  TORCH_CHECK(partial_sums.is_cuda() && block_tables.is_cuda() && context_lens.is_cuda(),
+              "evict_topk_compact_parts: inputs must be CUDA tensors");
+  const int G = static_cast<int>(partial_sums.size(0));
+  const int S = static_cast<int>(partial_sums.size(1));
+  const int L = static_cast<int>(partial_sums.size(2));
+  const int MB = static_cast<int>(block_tables.size(1));
+  TORCH_CHECK(G > 0, "evict_topk_compact_parts: no parts");
+  TORCH_CHECK(block_tables.size(0) == S && context_lens.size(0) == S,
+              "evict_topk_compact_parts: batch size mismatch");
+  auto o = torch::TensorOptions().dtype(torch::kInt32).device(partial_sums.device());
+  auto kept = torch::full({S, L}, -1, o);
+  auto cnt = torch::zeros({S}, o);
+  auto freed = torch::full({S, MB}, -1, o);
+  auto fcnt = torch::zeros({S}, o);
+  if (S == 0 || L == 0) return pybind11::make_tuple(kept, cnt, freed, fcnt);
+  partial_sums = partial_sums.contiguous();
+  const at::cuda::CUDAGuard g(partial_sums.device());
+  const size_t wsb = memopt_evict_topk_workspace_size(S, L, p.h, p.d);
+  auto ws = torch::empty({static_cast<int64_t>(wsb)}, o.dtype(torch::kUInt8));
+  check(memopt_evict_topk_compact_parts(partial_sums.data_ptr<float>(), G, S, L, block_tables.data_ptr<int32_t>(),
+                                        MB, context_lens.data_ptr<int32_t>(), p.k.data_ptr(), p.v.data_ptr(), p.nb,
+                                        p.bs, p.h, p.d, retain_ratio, num_sink_tokens, kept.data_ptr<int32_t>(),
+                                        cnt.data_ptr<int32_t>(), freed.data_ptr<int32_t>(),
+                                        fcnt.data_ptr<int32_t>(), ws.data_ptr(), wsb, cur_stream()),
+        "evict_topk_compact_parts");
+  return pybind11::make_tuple(kept, cnt, freed, fcnt);
+}
+
 namespace {
 
 void attn_checks(const torch::Tensor& query, const torch::Tensor& block_tables, const torch::Tensor& context_lens) {
@@ -515,6 +578,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("evict_topk_compact", &evict_topk_compact,
         "Exact sink-aware top-k eviction shared across heads, with compaction of the kept K/V rows",
         py::arg("attention_scores"), py::arg("block_tables"), py::arg("context_lens"), py::arg("retain_ratio"),
+        py::arg("num_sink_tokens") = 4);
+  m.def("evict_topk_head_sum", &evict_topk_head_sum,
+        "Partial token scores of this rank's heads for head-sharded exact eviction", py::arg("attention_scores"));
+  m.def("evict_topk_compact_parts", &evict_topk_compact_parts,
+        "Exact top-k eviction on the rank-ordered sum of partial token scores, compacting this rank's pool",
+        py::arg("partial_sums"), py::arg("block_tables"), py::arg("context_lens"), py::arg("retain_ratio"),
         py::arg("num_sink_tokens") = 4);
   m.def("dynamic_sparse_attention", &dynamic_sparse_attention, "Dynamic sparse/chunked attention over paged KV cache",
         py::arg("query"), py::arg("key_cache"), py::arg("value_cache"), py::arg("block_tables"),

@@ -218,17 +218,26 @@ class PagedKVCache:
                                     return_retained=True)
 
     def evict_exact(self, sids: Sequence[int], scores: torch.Tensor, retain_ratio: float,
-                    num_sink_tokens: int = 4) -> List[List[int]]:
+                    num_sink_tokens: int = 4, group=None) -> List[List[int]]:
         """``evict_topk_compact`` over the sequences: the kept tokens (exact
         top-k of the head-summed scores, sinks always kept) move to the front
         of each sequence, lengths shrink, and the emptied pages return to the
-        pool.  Returns the kept original token indices per sequence."""
+        pool.  Returns the kept original token indices per sequence.
+
+        ``group`` (a :class:`memopt.sharding.RankGroup`): this cache holds one
+        head shard of every sequence and ``scores`` are its heads; the ranks
+        exchange partial token scores and take one shared decision."""
         if self.kv_format != "fp16":
             raise RuntimeError("evict_exact: works on the fp16 pool")
         bt = self.block_tables(sids).contiguous()
         ctx = self.context_lens(sids).contiguous()
-        kept, cnt, _, _ = self._C.evict_topk_compact(scores.float().contiguous(), bt, ctx, float(retain_ratio),
-                                                     int(num_sink_tokens))
+        sc = scores.float().contiguous()
+        if group is not None and group.world_size > 1:
+            from .sharding import evict_exact_head_sharded
+
+            kept, cnt, _, _ = evict_exact_head_sharded(group, sc, bt, ctx, retain_ratio, num_sink_tokens, self._C)
+        else:
+            kept, cnt, _, _ = self._C.evict_topk_compact(sc, bt, ctx, float(retain_ratio), int(num_sink_tokens))
         counts = cnt.tolist()
         kept_h = kept.cpu()
         out = []

@@ -9,6 +9,13 @@ The only cross-rank traffic is host-side bookkeeping: a barrier around timed
 regions and the max over ranks of a device time (the job finishes when its
 slowest shard does).  The reference runs on one device only (its README lists
 multi-GPU pools as future work), so this module has no reference counterpart.
+
+Heads can be sharded instead (each rank's pool holds H/N heads of every
+sequence, for batches smaller than the GPU count).  Everything stays local
+then too, except the exact eviction whose decision is shared across heads:
+:func:`evict_exact_head_sharded` exchanges one fp32 row of partial token
+scores per sequence and rank (an all-gather, 1 MB per rank at 8 sequences of
+32768 tokens) and every rank ranks tokens by the same rank-ordered sum.
 """
 from __future__ import annotations
 
@@ -95,6 +102,47 @@ class RankGroup:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def all_gather_rows(self, t):
+        """Every rank's ``t`` (same shape on all ranks), stacked in rank order
+        into ``[world_size, *t.shape]`` on every rank."""
+        if self.dist is None:
+            return t.unsqueeze(0)
+        t = t.contiguous()
+        out = t.new_empty((self.world_size,) + tuple(t.shape))
+        if t.is_cuda:
+            self.dist.all_gather_into_tensor(out, t)
+        else:
+            self.dist.all_gather(list(out.unbind(0)), t)
+        return out
+
     def destroy(self) -> None:
         if self.dist is not None and self.dist.is_initialized():
             self.dist.destroy_process_group()
+
+
+def head_range(num_heads: int, world_size: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [start, stop) of the heads a rank holds under head sharding."""
+    if num_heads % world_size:
+        raise ValueError(f"{num_heads} heads do not split evenly over {world_size} ranks")
+    return shard_range(num_heads, world_size, rank)
+
+
+def evict_exact_head_sharded(group: RankGroup, scores, block_tables, context_lens, retain_ratio: float,
+                             num_sink_tokens: int = 4, ops=None):
+    """Exact top-k eviction shared across heads when the heads are sharded.
+
+    ``scores`` [S, H_local, L] are this rank's heads; ``block_tables`` /
+    ``context_lens`` are the sequences' (the same on every rank) and are
+    updated in place.  Each rank sums its own heads, the partial rows are
+    all-gathered in rank order, and ``evict_topk_compact_parts`` ranks tokens
+    by their fp32 sum in rank order and compacts this rank's pool, so every
+    rank keeps the same tokens and frees the same pages.  With one rank this
+    is ``evict_topk_compact``.  ``ops`` is the operator module (``memopt_C``).
+    Returns ``(kept_idx, kept_count, freed_pages, freed_count)``.
+    """
+    if ops is None:
+        import memopt_C as ops
+    part = ops.evict_topk_head_sum(scores)
+    parts = group.all_gather_rows(part)
+    return ops.evict_topk_compact_parts(parts, block_tables, context_lens, float(retain_ratio),
+                                        int(num_sink_tokens))

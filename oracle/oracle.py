@@ -173,6 +173,16 @@ def paged_attention_int4(q, pages, block_tables, context_lens, max_seq_len, wind
     return out
 
 
+def evict_topk_head_sum(scores):
+    """fp32 sum over heads, in head order, of scores [S, H, L] -> [S, L]
+    (starting from +0, as the device kernel does)."""
+    S, H, L = scores.shape
+    tot = np.zeros((S, L), np.float32)
+    for h in range(H):
+        tot = (tot + scores[:, h].astype(np.float32)).astype(np.float32)
+    return tot
+
+
 def evict_topk_compact(scores, block_tables, context_lens, kpool, vpool, retain_ratio, num_sink_tokens=4):
     """Restatement of the exact top-k eviction with compaction (this build's
     operator; no reference counterpart).  In place on block_tables,
@@ -180,18 +190,27 @@ def evict_topk_compact(scores, block_tables, context_lens, kpool, vpool, retain_
     freed_pages, freed_count).  Pure numpy: token score = fp32 sum over heads
     in head order, sinks always kept, invalid tokens never kept, ties by lower
     index, NaN lowest."""
-    S, H, L = scores.shape
+    return evict_topk_compact_parts(evict_topk_head_sum(scores)[None], block_tables, context_lens, kpool, vpool,
+                                    retain_ratio, num_sink_tokens)
+
+
+def evict_topk_compact_parts(parts, block_tables, context_lens, kpool, vpool, retain_ratio, num_sink_tokens=4):
+    """The head-sharded form: parts [G, S, L] are the ranks' partial token
+    scores (evict_topk_head_sum of each rank's heads) in rank order; the token
+    score is their fp32 sum in rank order.  kpool/vpool hold this rank's heads."""
+    G, S, L = parts.shape
     NB, BS = kpool.shape[0], kpool.shape[1]
     MB = block_tables.shape[1]
     kept_idx = np.full((S, L), -1, np.int32)
     kept_count = np.zeros(S, np.int32)
     freed = np.full((S, MB), -1, np.int32)
     freed_count = np.zeros(S, np.int32)
+    total = np.zeros((S, L), np.float32)
+    for g in range(G):
+        total = (total + parts[g].astype(np.float32)).astype(np.float32)
     for b in range(S):
         n = min(max(int(context_lens[b]), 0), L)
-        tot = np.zeros(L, np.float32)
-        for h in range(H):
-            tot = (tot + scores[b, h].astype(np.float32)).astype(np.float32)
+        tot = total[b]
         row = block_tables[b].copy()
         valid_pages = [int(p) for p in row if 0 <= p < NB]
         cand = []

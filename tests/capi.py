@@ -139,6 +139,32 @@ def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
     return kept, cnt, freed, fcnt
 
 
+def evict_topk_head_sum(scores):
+    S, H, L = scores.shape
+    out = torch.empty(S, L, dtype=torch.float32, device=scores.device)
+    ok(lib().memopt_evict_topk_head_sum(ptr(scores), I(S), I(H), I(L), ptr(out), stream()))
+    return out
+
+
+def evict_topk_compact_parts(parts, bt, ctx, kpool, vpool, retain_ratio, sinks):
+    G, S, L = parts.shape
+    MB = bt.shape[1]
+    dev = parts.device
+    H, D = kpool.shape[2], kpool.shape[3]
+    kept = torch.empty(S, L, dtype=torch.int32, device=dev)
+    cnt = torch.empty(S, dtype=torch.int32, device=dev)
+    freed = torch.empty(S, MB, dtype=torch.int32, device=dev)
+    fcnt = torch.empty(S, dtype=torch.int32, device=dev)
+    lib().memopt_evict_topk_workspace_size.restype = SZ
+    wsb = int(lib().memopt_evict_topk_workspace_size(I(S), I(L), I(H), I(D)))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    ok(lib().memopt_evict_topk_compact_parts(ptr(parts), I(G), I(S), I(L), ptr(bt), I(MB), ptr(ctx), ptr(kpool),
+                                             ptr(vpool), I(kpool.shape[0]), I(kpool.shape[1]), I(H), I(D),
+                                             F(retain_ratio), I(sinks), ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt),
+                                             ptr(ws), SZ(wsb), stream()))
+    return kept, cnt, freed, fcnt
+
+
 def attention_f16_ex(q, kpool, vpool, bt, ctx, msl, win, causal=False):
     """memopt_paged_attention_f16_ex: the pool's head count may divide H."""
     B, QL, H, D = q.shape

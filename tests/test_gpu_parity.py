@@ -195,6 +195,8 @@ def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     (2, 3, 4097, 16, 64, 0.75, 3, "specials", True),
     (1, 2, 32768, 16, 64, 0.75, 4, "lognormal", False),
     (2, 2, 16384, 16, 64, 0.6, 0, "ties", True),
+    (2, 32, 4096, 16, 128, 0.75, 4, "lognormal", True),  # 8 KB rows, the bench's geometry
+    (1, 4, 20000, 16, 64, 0.05, 0, "normal", False),     # long forward moves
 ])
 def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + 7 * S, dist, holes=holes)
@@ -217,6 +219,55 @@ def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
             pg, pos = bt[b, i // BS], i % BS
             assert np.array_equal(np16(gk[pg, pos]).view(np.uint16), kp[pg, pos].view(np.uint16))
             assert np.array_equal(np16(gv[pg, pos]).view(np.uint16), vp[pg, pos].view(np.uint16))
+
+
+@pytest.mark.parametrize("S,H,G,L,BS,D,r,sinks,dist,holes", [
+    (2, 4, 2, 512, 16, 64, 0.75, 4, "lognormal", False),
+    (3, 4, 4, 1000, 16, 128, 0.5, 0, "normal", True),
+    (2, 6, 3, 777, 32, 64, 0.3, 2, "ties", False),
+    (2, 4, 2, 4097, 16, 64, 0.75, 3, "specials", True),
+    (1, 8, 8, 32768, 16, 64, 0.75, 4, "lognormal", False),
+])
+def test_evict_topk_head_sharded_bit_exact(S, H, G, L, BS, D, r, sinks, dist, holes):
+    """Heads split over G shards: partial sums per shard, decision on their
+    rank-ordered sum; each shard's pool (its heads) compacted identically."""
+    sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + 7 * S, dist, holes=holes)
+    rng = np.random.default_rng(L + G)
+    ctx = np.array([L - int(rng.integers(0, min(L, 40))) for _ in range(S)], np.int32)
+    ctx[0] = L
+    hs = H // G
+    gsc = torch.from_numpy(sc).to(DEV)
+    parts = torch.stack([capi.evict_topk_head_sum(gsc[:, g * hs:(g + 1) * hs].contiguous()) for g in range(G)])
+    rparts = np.stack([O.evict_topk_head_sum(sc[:, g * hs:(g + 1) * hs]) for g in range(G)])
+    assert np.array_equal(np16(parts), rparts, equal_nan=True)  # NaN payloads may differ
+    rbt, rctx = bt.copy(), ctx.copy()
+    rkp, rvp = kp.copy(), vp.copy()
+    rk, rc, rf, rfc = O.evict_topk_compact_parts(rparts, rbt, rctx, rkp, rvp, r, sinks)
+    for g in range(G):
+        gk = torch.from_numpy(np.ascontiguousarray(kp[:, :, g * hs:(g + 1) * hs])).to(DEV)
+        gv = torch.from_numpy(np.ascontiguousarray(vp[:, :, g * hs:(g + 1) * hs])).to(DEV)
+        gbt, gctx = torch.from_numpy(bt).to(DEV), torch.from_numpy(ctx).to(DEV)
+        kept, cnt, freed, fcnt = capi.evict_topk_compact_parts(parts, gbt, gctx, gk, gv, r, sinks)
+        assert np.array_equal(np16(cnt), rc) and np.array_equal(np16(kept), rk)
+        assert np.array_equal(np16(fcnt), rfc) and np.array_equal(np16(freed), rf)
+        assert np.array_equal(np16(gbt), rbt) and np.array_equal(np16(gctx), rctx)
+        for b in range(S):
+            for i in range(int(rc[b])):
+                pg, pos = rbt[b, i // BS], i % BS
+                assert np.array_equal(np16(gk[pg, pos]).view(np.uint16), rkp[pg, pos, g * hs:(g + 1) * hs].view(np.uint16))
+                assert np.array_equal(np16(gv[pg, pos]).view(np.uint16), rvp[pg, pos, g * hs:(g + 1) * hs].view(np.uint16))
+
+
+def test_evict_topk_one_part_equals_unsharded():
+    sc, bt, kp, vp = _evict_case(2, 4, 3000, 16, 64, 0.6, 4, 3000 + 14, "lognormal", holes=True)
+    ctx = np.array([3000, 2980], np.int32)
+    gsc = torch.from_numpy(sc).to(DEV)
+    a = [torch.from_numpy(x).to(DEV) for x in (kp, vp, bt, ctx)]
+    b = [torch.from_numpy(x.copy()).to(DEV) for x in (kp, vp, bt, ctx)]
+    r1 = capi.evict_topk_compact(gsc, a[2], a[3], a[0], a[1], 0.6, 4)
+    r2 = capi.evict_topk_compact_parts(capi.evict_topk_head_sum(gsc)[None], b[2], b[3], b[0], b[1], 0.6, 4)
+    for x, y in zip(list(r1) + a, list(r2) + b):
+        assert torch.equal(x, y)
 
 
 @pytest.mark.parametrize("NB,BS,H,D,r", [(10, 16, 4, 64, 0.75), (7, 32, 3, 128, 0.5), (5, 8, 2, 64, 0.9),

@@ -67,3 +67,58 @@ def test_two_rank_gloo_sharded_decode(tmp_path):
         assert float(z["mx"]) == 10.0 + world - 1  # max over ranks reached every rank
     assert sorted(seen) == list(range(W.S))
     assert np.array_equal(got, ref)
+
+
+def _spawn(worker: str, world: int, args, extra_env=None, timeout=240):
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world),
+                   RANK=str(r), LOCAL_RANK=str(r), **(extra_env or {}))
+        procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, worker), *map(str, args)],
+                                      env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
+    for p in procs:
+        out, _ = p.communicate(timeout=timeout)
+        assert p.returncode == 0, out.decode()[-3000:]
+
+
+def check_head_sharded_evict(out_dir, world: int) -> None:
+    """Every rank's outputs equal the oracle's decision on the rank-ordered
+    partial sums, and its pool rows equal its head slice of the compacted pool."""
+    sys.path.insert(0, HERE)
+    import multirank_evict_worker as W
+
+    sc, bt, ctx, kp, vp = W.global_workload()
+    hs = W.H // world
+    parts = np.stack([O.evict_topk_head_sum(sc[:, r * hs:(r + 1) * hs]) for r in range(world)])
+    rbt, rctx, rkp, rvp = bt.copy(), ctx.copy(), kp.copy(), vp.copy()
+    rk, rc, rf, rfc = O.evict_topk_compact_parts(parts, rbt, rctx, rkp, rvp, W.RETAIN, W.SINKS)
+    assert 0 < rc.sum() < ctx.sum()  # the case evicts something
+    for r in range(world):
+        z = np.load(os.path.join(out_dir, f"rank{r}.npz"))
+        assert (int(z["h0"]), int(z["h1"])) == (r * hs, (r + 1) * hs)
+        for name, ref in (("kept", rk), ("cnt", rc), ("freed", rf), ("fcnt", rfc), ("bt", rbt), ("ctx", rctx)):
+            assert np.array_equal(z[name], ref), (r, name)
+        for b in range(W.S):
+            for i in range(int(rc[b])):
+                pg, pos = rbt[b, i // W.BS], i % W.BS
+                assert np.array_equal(z["k"][pg, pos].view(np.uint16), rkp[pg, pos, r * hs:(r + 1) * hs].view(np.uint16))
+                assert np.array_equal(z["v"][pg, pos].view(np.uint16), rvp[pg, pos, r * hs:(r + 1) * hs].view(np.uint16))
+
+
+def test_two_rank_gloo_head_sharded_exact_eviction(tmp_path):
+    _spawn("multirank_evict_worker.py", 2, [tmp_path, "gloo"])
+    check_head_sharded_evict(tmp_path, 2)
+
+
+def test_head_range_and_single_rank_gather():
+    from memopt.sharding import RankGroup, head_range
+
+    assert [head_range(32, 4, r) for r in range(4)] == [(0, 8), (8, 16), (16, 24), (24, 32)]
+    with pytest.raises(ValueError):
+        head_range(6, 4, 0)
+    import torch
+
+    t = torch.arange(6.0).reshape(2, 3)
+    g = RankGroup()
+    assert torch.equal(g.all_gather_rows(t), t[None])
