@@ -224,6 +224,10 @@ size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads
                                              int head_dim, int max_blocks_per_seq,
                                              int block_size, int max_seq_len,
                                              int window_size);
+/* The same for the _ex entry points: pools holding num_kv_heads heads.      */
+size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len, int num_heads, int num_kv_heads,
+                                                int head_dim, int max_blocks_per_seq, int block_size,
+                                                int max_seq_len, int window_size);
 /* Bytes at the start of the workspace that hold tickets (must start zeroed). */
 size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads);
 

@@ -12,6 +12,7 @@
 #include <cudaTypedefs.h>
 
 #include "decode_kernel.cuh"
+#include "decode_mq.cuh"
 
 #ifndef MEMOPT_SPLIT_F16
 #define MEMOPT_SPLIT_F16 3
@@ -71,6 +72,24 @@ int make_pool_map(CUtensorMap* map, const void* base, int64_t rows, int H, int D
   return MEMOPT_OK;
 }
 
+// The same view with 64-dim boxes of 16 rows and 128-byte swizzle (the
+// multi-query kernel's ldmatrix layout).
+int make_pool_map_sw(CUtensorMap* map, const void* base, int64_t rows, int H, int D) {
+  auto fn = encode_fn();
+  if (!fn) return fail(MEMOPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2};
+  cuuint32_t box[3] = {64, 1, 16};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MEMOPT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+  return MEMOPT_OK;
+}
+
 int clamp_window(int window_size, int max_seq_len) {
   return (window_size <= 0 || window_size > max_seq_len) ? max_seq_len : window_size;
 }
@@ -121,6 +140,92 @@ WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
   w.po = w.ml + align256(pairs * n_chunks * sizeof(float2));
   w.total = w.po + align256(static_cast<size_t>(pairs) * n_chunks * D * sizeof(float));
   return w;
+}
+
+// Multi-query decode (fp16 pool, q_len below the prefill threshold, at least
+// two query rows per KV head): rows per (sequence, KV head) and their tiles.
+bool use_mq(bool int4, int q_len, int H, int KVH) {
+  return !int4 && !use_prefill(q_len) && KVH > 0 && (H / KVH) * q_len >= 2;
+}
+int64_t mq_groups(int batch, int q_len, int H, int KVH) {
+  const int rows = (H / KVH) * q_len;
+  return static_cast<int64_t>(batch) * KVH * ((rows + 15) / 16);
+}
+// A tile's rows may span q_len - 1 extra tokens (causal rows end at their own
+// token), so its chunks cover window + q_len - 1 tokens.
+Split mq_split(int batch, int q_len, int H, int KVH, int MB, int BS, int window) {
+  return choose_split(mq_groups(batch, q_len, H, KVH), MB, BS, window + q_len - 1, kSplitF16);
+}
+
+template <int D, int BS>
+int launch_mq(const decode_mq::Params& p, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
+  using C = decode_mq::Cfg<D>;
+  auto kern = decode_mq::paged_decode_mq_kernel<D, BS>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_mq)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t ctas_needed = (p.total_items + C::NW - 1) / C::NW;
+  int per_sm = (227 * 1024) / C::SMEM;
+  if (per_sm > C::MIN_BLOCKS) per_sm = C::MIN_BLOCKS;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  kern<<<grid, C::NW * 32, C::SMEM, s>>>(p, km, vm, nullptr);
+  MEMOPT_LAUNCH_CHECK("paged_decode_mq_kernel launch");
+  return MEMOPT_OK;
+}
+
+// Runs the multi-query kernel with the checks common_setup already made.
+int run_mq(const Params& one, const void* key_pool, const void* value_pool, int D, int BS, void* ws,
+           size_t ws_bytes, cudaStream_t s) {
+  decode_mq::Params p{};
+  p.q = one.q;
+  p.out = one.out;
+  p.bt = one.bt;
+  p.ctx = one.ctx;
+  p.B = one.B;
+  p.QL = one.QL;
+  p.H = one.H;
+  p.KVH = one.KVH;
+  p.group = one.group;
+  p.MB = one.MB;
+  p.causal = one.causal;
+  p.NB = one.NB;
+  p.window = one.window;
+  p.qscale = one.qscale;
+  p.rows = one.group * one.QL;
+  p.tiles = (p.rows + 15) / 16;
+  const Split sp = mq_split(one.B, one.QL, one.H, one.KVH, one.MB, BS, one.window);
+  p.chunk_pages = sp.chunk_pages;
+  p.n_chunks = sp.n_chunks;
+  p.total_items = mq_groups(one.B, one.QL, one.H, one.KVH) * sp.n_chunks;
+  const int64_t pairs = static_cast<int64_t>(one.B) * one.QL * one.H;
+  const WsLayout w = ws_layout(pairs, sp.n_chunks, D);
+  if (w.total > 0) {
+    if (ws == nullptr || ws_bytes < w.total)
+      return fail(MEMOPT_ERR_WORKSPACE, "dynamic_sparse_attention: workspace too small (need " +
+                                            std::to_string(w.total) + " bytes)");
+    uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+    p.tickets = reinterpret_cast<int32_t*>(base + w.tickets);
+    p.ml = reinterpret_cast<float2*>(base + w.ml);
+    p.po = reinterpret_cast<float*>(base + w.po);
+  }
+  alignas(64) CUtensorMap km, vm;
+  const int64_t rows = one.NB * BS;
+  int st = make_pool_map_sw(&km, key_pool, rows, one.KVH, D);
+  if (st != MEMOPT_OK) return st;
+  st = make_pool_map_sw(&vm, value_pool, rows, one.KVH, D);
+  if (st != MEMOPT_OK) return st;
+  if (D == 128 && BS == 16) return launch_mq<128, 16>(p, km, vm, s);
+  if (D == 128 && BS == 32) return launch_mq<128, 32>(p, km, vm, s);
+  if (D == 64 && BS == 16) return launch_mq<64, 16>(p, km, vm, s);
+  if (D == 64 && BS == 32) return launch_mq<64, 32>(p, km, vm, s);
+  return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: unsupported geometry");
 }
 
 template <int D, int BS, bool INT4>
@@ -223,19 +328,35 @@ int zero_output(void* out, int batch, int q_len, int H, int D, void* stream) {
 
 using namespace memopt;
 
+extern "C" size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len, int num_heads, int num_kv_heads,
+                                                           int head_dim, int max_blocks_per_seq, int block_size,
+                                                           int max_seq_len, int window_size) {
+  if (batch <= 0 || q_len <= 0 || num_heads <= 0 || head_dim <= 0 || block_size <= 0) return 0;
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return 0;
+  const int64_t pairs = static_cast<int64_t>(batch) * q_len * num_heads;
+  // One size serves every path the call can take (fp16 one-row, INT4,
+  // fp16 multi-query): the largest need.
+  const int w = clamp_window(window_size, max_seq_len);
+  size_t need = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitF16).n_chunks,
+                          head_dim).total;
+  const size_t b = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitInt4).n_chunks,
+                             head_dim).total;
+  if (b > need) need = b;
+  if (use_mq(false, q_len, num_heads, num_kv_heads)) {
+    const size_t c =
+        ws_layout(pairs, mq_split(batch, q_len, num_heads, num_kv_heads, max_blocks_per_seq, block_size, w).n_chunks,
+                  head_dim).total;
+    if (c > need) need = c;
+  }
+  return need;
+}
+
 extern "C" size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads,
                                                         int head_dim, int max_blocks_per_seq,
                                                         int block_size, int max_seq_len,
                                                         int window_size) {
-  if (batch <= 0 || q_len <= 0 || num_heads <= 0 || head_dim <= 0 || block_size <= 0) return 0;
-  const int64_t pairs = static_cast<int64_t>(batch) * q_len * num_heads;
-  // One size serves both formats (they split differently): the larger need.
-  const int w = clamp_window(window_size, max_seq_len);
-  const size_t a = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitF16).n_chunks,
-                             head_dim).total;
-  const size_t b = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitInt4).n_chunks,
-                             head_dim).total;
-  return a > b ? a : b;
+  return memopt_paged_attention_workspace_size_ex(batch, q_len, num_heads, num_heads, head_dim, max_blocks_per_seq,
+                                                  block_size, max_seq_len, window_size);
 }
 
 extern "C" size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads) {
@@ -266,6 +387,8 @@ extern "C" int memopt_paged_attention_f16_ex(const void* query, const void* key_
     return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads,
                        num_kv_heads, head_dim, max_blocks_per_seq, num_blocks, block_size, p.window, causal, out,
                        as_stream(stream));
+  if (use_mq(false, q_len, num_heads, num_kv_heads))
+    return run_mq(p, key_pool, value_pool, head_dim, block_size, workspace, workspace_bytes, as_stream(stream));
   alignas(64) CUtensorMap km, vm;
   st = make_pool_map(&km, key_pool, num_blocks * block_size, num_kv_heads, head_dim, block_size);
   if (st != MEMOPT_OK) return st;

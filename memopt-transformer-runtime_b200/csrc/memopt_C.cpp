@@ -412,11 +412,11 @@ void attn_checks(const torch::Tensor& query, const torch::Tensor& block_tables, 
 }
 
 // Split-K scratch from the caching allocator; only the ticket prefix is zeroed.
-torch::Tensor attn_workspace(const torch::Tensor& query, int MB, int BS, int max_seq_len, int window_size,
-                             size_t* bytes) {
+torch::Tensor attn_workspace(const torch::Tensor& query, int KVH, int MB, int BS, int max_seq_len,
+                             int window_size, size_t* bytes) {
   const int B = static_cast<int>(query.size(0)), QL = static_cast<int>(query.size(1));
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
-  *bytes = memopt_paged_attention_workspace_size(B, QL, H, D, MB, BS, max_seq_len, window_size);
+  *bytes = memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, max_seq_len, window_size);
   if (*bytes == 0) return torch::Tensor();
   auto ws = torch::empty({static_cast<int64_t>(*bytes)},
                          torch::TensorOptions().dtype(torch::kUInt8).device(query.device()));
@@ -458,7 +458,7 @@ torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_ca
   const at::cuda::CUDAGuard g(query.device());
   auto q = aligned_contig(query);
   size_t wsb = 0;
-  auto ws = attn_workspace(q, MB, BS, max_seq_len, window_size, &wsb);
+  auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb);
   check(memopt_paged_attention_f16_ex(q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
                                       block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(), B, QL, H,
                                       KVH, D, MB, key_cache.size(0), BS, max_seq_len, window_size, causal ? 1 : 0,
@@ -489,7 +489,7 @@ torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor k
   const at::cuda::CUDAGuard g(query.device());
   auto q = aligned_contig(query);
   size_t wsb = 0;
-  auto ws = attn_workspace(q, MB, BS, max_seq_len, window_size, &wsb);
+  auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb);
   check(memopt_paged_attention_int4_ex(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
                                        context_lens.data_ptr<int32_t>(), B, QL, H, KVH, D, MB, kv_pages.size(0), BS,
                                        max_seq_len, window_size, causal ? 1 : 0, out.data_ptr(),

@@ -80,8 +80,9 @@ def evict_cache(scores, kpool, vpool, r):
                                 F(r), stream()))
 
 
-def workspace(B, QL, H, D, MB, BS, msl, win, device="cuda"):
-    n = lib().memopt_paged_attention_workspace_size(B, QL, H, D, MB, BS, msl, win)
+def workspace(B, QL, H, D, MB, BS, msl, win, device="cuda", kvh=None):
+    lib().memopt_paged_attention_workspace_size_ex.restype = SZ
+    n = lib().memopt_paged_attention_workspace_size_ex(B, QL, H, H if kvh is None else kvh, D, MB, BS, msl, win)
     if n == 0:
         return None, 0
     ws = torch.zeros(n, dtype=torch.uint8, device=device)
@@ -170,7 +171,7 @@ def attention_f16_ex(q, kpool, vpool, bt, ctx, msl, win, causal=False):
     B, QL, H, D = q.shape
     MB = bt.shape[1]
     out = torch.empty_like(q)
-    ws, n = workspace(B, QL, H, D, MB, kpool.shape[1], msl, win)
+    ws, n = workspace(B, QL, H, D, MB, kpool.shape[1], msl, win, kvh=kpool.shape[2])
     ok(lib().memopt_paged_attention_f16_ex(ptr(q), ptr(kpool), ptr(vpool), ptr(bt), ptr(ctx), I(B), I(QL), I(H),
                                            I(kpool.shape[2]), I(D), I(MB), I64(kpool.shape[0]), I(kpool.shape[1]),
                                            I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))
@@ -181,7 +182,7 @@ def attention_int4_ex(q, pages, block_size, bt, ctx, msl, win, causal=False):
     B, QL, H, D = q.shape
     MB = bt.shape[1]
     out = torch.empty_like(q)
-    ws, n = workspace(B, QL, H, D, MB, block_size, msl, win)
+    ws, n = workspace(B, QL, H, D, MB, block_size, msl, win, kvh=pages.shape[1])
     ok(lib().memopt_paged_attention_int4_ex(ptr(q), ptr(pages), ptr(bt), ptr(ctx), I(B), I(QL), I(H),
                                             I(pages.shape[1]), I(D), I(MB), I64(pages.shape[0]), I(block_size),
                                             I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))

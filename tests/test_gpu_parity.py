@@ -421,6 +421,43 @@ def test_attention_gqa_causal_int4_vs_oracle(case):
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
 
 
+# Multi-query decode (fp16, >= 2 query rows per KV head, q_len < 64): one page
+# load serves the group's query heads x the q_len rows (tiles of 16 rows).
+MQ_CASES = [
+    # B, QL, H, KVH, D, BS, ctx, MB, max_seq_len, window, causal, holes
+    (3, 1, 32, 8, 128, 16, [4096, 1000, 17], 256, 4096, 4096, False, 0.0),   # GQA 4, ragged
+    (2, 1, 16, 2, 128, 16, [3000, 2999], 200, 3200, 3200, False, 0.05),     # GQA 8, holes
+    (2, 1, 4, 2, 64, 32, [511, 64], 16, 512, 512, False, 0.0),              # GQA 2, D 64, 32-token pages
+    (2, 4, 8, 8, 128, 16, [900, 4], 64, 1024, 1024, True, 0.0),             # MHA q_len 4, causal (4 <= q_len ctx)
+    (2, 4, 32, 4, 128, 16, [1200, 700], 80, 1280, 1280, True, 0.1),         # 32 rows per KV head: 2 tiles
+    (1, 3, 6, 2, 64, 16, [333], 24, 384, 100, True, 0.0),                   # 9 rows (partial tile), window
+    (2, 2, 16, 1, 128, 32, [2048, 1500], 64, 2048, 300, False, 0.0),        # MQA 32 rows, window
+    (1, 1, 8, 2, 128, 16, [40000], 2500, 40000, 40000, False, 0.0),         # split-K, GQA 4
+    (2, 8, 8, 2, 128, 16, [20000, 5], 1250, 20000, 1024, True, 0.0),        # split-K, causal window, q_len > ctx
+    (1, 1, 8, 2, 128, 16, [0], 4, 64, 64, False, 0.0),                      # empty context
+]
+
+
+@pytest.mark.parametrize("case", MQ_CASES)
+def test_attention_multi_query_f16_vs_oracle(case):
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = case
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, QL * 13 + H + KVH)
+    got = capi.attention_f16_ex(torch.from_numpy(q).to(DEV), torch.from_numpy(kp).to(DEV),
+                                torch.from_numpy(vp).to(DEV), torch.from_numpy(bt).to(DEV),
+                                torch.from_numpy(cl).to(DEV), msl, win, causal)
+    ref = O.paged_attention_f16(q, kp, vp, bt, cl, msl, win, causal=causal)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_attention_multi_query_deterministic_and_tickets_reset():
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = MQ_CASES[7]
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, 5)
+    args = [torch.from_numpy(a).to(DEV) for a in (q, kp, vp, bt, cl)]
+    o1 = capi.attention_f16_ex(*args, msl, win, causal)
+    o2 = capi.attention_f16_ex(*args, msl, win, causal)
+    assert torch.equal(o1, o2)
+
+
 def test_attention_deterministic_and_workspace_reuse():
     B, QL, H, D, BS, ctx, MB, msl, win, holes = ATTN_CASES[7]
     q, kp, vp, bt, cl = _attn_case(B, QL, H, D, BS, ctx, MB, 11, holes)
