@@ -142,10 +142,11 @@ WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
   return w;
 }
 
-// Multi-query decode (fp16 pool, q_len below the prefill threshold, at least
-// two query rows per KV head): rows per (sequence, KV head) and their tiles.
+// Multi-query decode: at least two query rows per KV head, and for the fp16
+// pool a q_len below the prefill threshold (the INT4 pool has no prefill
+// kernel: every q_len runs here).
 bool use_mq(bool int4, int q_len, int H, int KVH) {
-  return !int4 && !use_prefill(q_len) && KVH > 0 && (H / KVH) * q_len >= 2;
+  return (int4 || !use_prefill(q_len)) && KVH > 0 && (H / KVH) * q_len >= 2;
 }
 int64_t mq_groups(int batch, int q_len, int H, int KVH) {
   const int rows = (H / KVH) * q_len;
@@ -157,10 +158,10 @@ Split mq_split(int batch, int q_len, int H, int KVH, int MB, int BS, int window)
   return choose_split(mq_groups(batch, q_len, H, KVH), MB, BS, window + q_len - 1, kSplitF16);
 }
 
-template <int D, int BS>
+template <int D, int BS, bool INT4>
 int launch_mq(const decode_mq::Params& p, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
-  using C = decode_mq::Cfg<D>;
-  auto kern = decode_mq::paged_decode_mq_kernel<D, BS>;
+  using C = decode_mq::Cfg<D, BS, INT4>;
+  auto kern = decode_mq::paged_decode_mq_kernel<D, BS, INT4>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -181,9 +182,12 @@ int launch_mq(const decode_mq::Params& p, const CUtensorMap& km, const CUtensorM
 }
 
 // Runs the multi-query kernel with the checks common_setup already made.
+// key_pool == nullptr: the INT4 pool, pages in value_pool.
 int run_mq(const Params& one, const void* key_pool, const void* value_pool, int D, int BS, void* ws,
            size_t ws_bytes, cudaStream_t s) {
+  const bool int4 = key_pool == nullptr;
   decode_mq::Params p{};
+  p.pages = int4 ? static_cast<const uint8_t*>(value_pool) : nullptr;
   p.q = one.q;
   p.out = one.out;
   p.bt = one.bt;
@@ -216,15 +220,24 @@ int run_mq(const Params& one, const void* key_pool, const void* value_pool, int 
     p.po = reinterpret_cast<float*>(base + w.po);
   }
   alignas(64) CUtensorMap km, vm;
+  if (int4) {
+    std::memset(&km, 0, sizeof(km));
+    std::memset(&vm, 0, sizeof(vm));
+    if (D == 128 && BS == 16) return launch_mq<128, 16, true>(p, km, vm, s);
+    if (D == 128 && BS == 32) return launch_mq<128, 32, true>(p, km, vm, s);
+    if (D == 64 && BS == 16) return launch_mq<64, 16, true>(p, km, vm, s);
+    if (D == 64 && BS == 32) return launch_mq<64, 32, true>(p, km, vm, s);
+    return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention_int4: unsupported geometry");
+  }
   const int64_t rows = one.NB * BS;
   int st = make_pool_map_sw(&km, key_pool, rows, one.KVH, D);
   if (st != MEMOPT_OK) return st;
   st = make_pool_map_sw(&vm, value_pool, rows, one.KVH, D);
   if (st != MEMOPT_OK) return st;
-  if (D == 128 && BS == 16) return launch_mq<128, 16>(p, km, vm, s);
-  if (D == 128 && BS == 32) return launch_mq<128, 32>(p, km, vm, s);
-  if (D == 64 && BS == 16) return launch_mq<64, 16>(p, km, vm, s);
-  if (D == 64 && BS == 32) return launch_mq<64, 32>(p, km, vm, s);
+  if (D == 128 && BS == 16) return launch_mq<128, 16, false>(p, km, vm, s);
+  if (D == 128 && BS == 32) return launch_mq<128, 32, false>(p, km, vm, s);
+  if (D == 64 && BS == 16) return launch_mq<64, 16, false>(p, km, vm, s);
+  if (D == 64 && BS == 32) return launch_mq<64, 32, false>(p, km, vm, s);
   return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: unsupported geometry");
 }
 
@@ -342,7 +355,7 @@ extern "C" size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len,
   const size_t b = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitInt4).n_chunks,
                              head_dim).total;
   if (b > need) need = b;
-  if (use_mq(false, q_len, num_heads, num_kv_heads)) {
+  if (use_mq(false, q_len, num_heads, num_kv_heads) || use_mq(true, q_len, num_heads, num_kv_heads)) {
     const size_t c =
         ws_layout(pairs, mq_split(batch, q_len, num_heads, num_kv_heads, max_blocks_per_seq, block_size, w).n_chunks,
                   head_dim).total;
@@ -427,6 +440,8 @@ extern "C" int memopt_paged_attention_int4_ex(const void* query, const uint8_t* 
   if (reinterpret_cast<uintptr_t>(kv_pages) & 15u)
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: pages must be 16-byte aligned");
   p.pages = kv_pages;
+  if (use_mq(true, q_len, num_heads, num_kv_heads))
+    return run_mq(p, nullptr, kv_pages, head_dim, block_size, workspace, workspace_bytes, as_stream(stream));
   alignas(64) CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   return dispatch<true>(p, head_dim, block_size, dummy, dummy, nullptr, as_stream(stream));

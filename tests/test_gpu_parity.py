@@ -449,6 +449,25 @@ def test_attention_multi_query_f16_vs_oracle(case):
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("case", MQ_CASES + [
+    (2, 70, 4, 2, 128, 16, [200, 90], 16, 256, 256, True, 0.0),    # INT4 has no prefill kernel: q_len 70
+    (1, 2, 2, 2, 64, 16, [50], 4, 64, 64, False, 0.0),             # MHA q_len 2, D 64
+])
+def test_attention_multi_query_int4_vs_oracle(case):
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = case
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, QL * 17 + H + KVH)
+    NB = kp.shape[0]
+    T = NB * BS
+    pages = torch.zeros(NB, KVH, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(torch.from_numpy(kp.reshape(T, KVH, D)).to(DEV),
+                          torch.from_numpy(vp.reshape(T, KVH, D)).to(DEV),
+                          torch.from_numpy(np.arange(T, dtype=np.int32)).to(DEV), pages, BS)
+    got = capi.attention_int4_ex(torch.from_numpy(q).to(DEV), pages, BS, torch.from_numpy(bt).to(DEV),
+                                 torch.from_numpy(cl).to(DEV), msl, win, causal)
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS, causal=causal)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
 def test_attention_multi_query_deterministic_and_tickets_reset():
     B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = MQ_CASES[7]
     q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, 5)
