@@ -301,6 +301,7 @@ def run_ours(args) -> None:
         extra.update(prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         extra.update(evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         extra.update(long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
+        extra.update(multi_query_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         if ws_n > 1:
             extra.update(evict_head_sharded_extra(torch, memopt_C, dev, stream, group, ws_n))
 
@@ -421,6 +422,8 @@ def run_only(args) -> None:
         res = evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "prefill":
         res = prefill_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
+    elif args.only == "mq":
+        res = multi_query_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "long":
         res = long_decode_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     else:
@@ -594,6 +597,61 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
                               "decode_tokens_per_s": round(eb * ws_n / (ms * 1e-3), 1)}}
 
 
+def multi_query_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """Decode shapes where several query rows read each KV head (the
+    multi-query kernel): grouped-query attention with 32 query heads over 8 KV
+    heads (batch 128, ctx 4096; fp16 and INT4 pools) and the configs[1] shape
+    with 4 query rows per sequence (speculative decoding).  Bytes are the
+    pool pages read once per (sequence, KV head) plus q/out; every sequence
+    has its own pages (inputs larger than L2)."""
+    peak, _ = peaks()
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(61 + rank)
+    cases = [("gqa_decode_f16", 128, 1, 32, 8, "f16"), ("gqa_decode_int4", 128, 1, 32, 8, "int4"),
+             ("multi_row_decode_f16", 32, 4, 32, 32, "f16")]
+    ctx_len = CTX
+    mb = ctx_len // BS
+    for name, b, ql, h, kvh, fmt in cases:
+        nb = b * mb
+        bt = torch.randperm(nb, generator=torch.Generator().manual_seed(5 + rank)).to(torch.int32)
+        bt = bt.reshape(b, mb).to(dev)
+        q = torch.randn(b, ql, h, D, dtype=torch.float16, device=dev, generator=g)
+        ctx = torch.full((b,), ctx_len, dtype=torch.int32, device=dev)
+        out = torch.empty_like(q)
+        wsb = _capi.workspace_size_ex(b, ql, h, kvh, D, mb, BS, ctx_len, ctx_len)
+        wsp = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+        if fmt == "f16":
+            kp = torch.randn(nb, BS, kvh, D, dtype=torch.float16, device=dev, generator=g)
+            vp = torch.randn_like(kp)
+            pool_bytes = 2 * b * ctx_len * kvh * D * 2
+
+            def step():
+                _capi.paged_attention_f16_ex(q, kp, vp, bt, ctx, out, ctx_len, ctx_len, False, wsp, wsb, sp)
+        else:
+            pb = BS * D + 2 * BS * (D // 64) * 2
+            pages = torch.randint(0, 256, (nb, kvh, pb), dtype=torch.uint8, device=dev, generator=g)
+            sc = pages[:, :, BS * D:].view(torch.float16)
+            sc.uniform_(0.05, 0.55, generator=g)
+            pool_bytes = b * mb * kvh * pb
+
+            def step():
+                _capi.paged_attention_int4_ex(q, pages, BS, bt, ctx, out, ctx_len, ctx_len, False, wsp, wsb, sp)
+        ms = max_over_ranks(time_loop(torch, step, max(args.steps // 4, 20), args.warmup, barrier, stream))
+        sbytes = pool_bytes + 2 * b * ql * h * D * 2 + b * mb * 4
+        res[name] = {"workload": f"batch {b}/GPU, {ql} query row(s), {h} query heads over {kvh} KV heads x {D}, "
+                                 f"ctx {ctx_len}, {fmt} pool",
+                     "value": round(sbytes * ws_n / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                     "ms_per_step": round(ms, 5), "frac_of_hbm_peak": round(sbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                     "decode_tokens_per_s": round(b * ql * ws_n / (ms * 1e-3), 1),
+                     "kernel": "paged_decode_mq_kernel"}
+        del bt, q, out, wsp
+        if fmt == "f16":
+            del kp, vp
+        else:
+            del pages, sc
+    return res
+
+
 def evict_head_sharded_extra(torch, memopt_C, dev, stream, group, ws_n):
     """configs[3] eviction with the HEADS sharded (N > 1): every rank holds
     32/N heads of all 8 sequences (same block tables on every rank), sums its
@@ -646,7 +704,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
-    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict", "long"], help="time one kernel family alone (profiling)")
+    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict", "long", "mq"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -13,6 +13,7 @@
 
 #include "decode_kernel.cuh"
 #include "decode_mq.cuh"
+#include "decode_mq4.cuh"
 
 #ifndef MEMOPT_SPLIT_F16
 #define MEMOPT_SPLIT_F16 3
@@ -148,20 +149,47 @@ WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
 bool use_mq(bool int4, int q_len, int H, int KVH) {
   return (int4 || !use_prefill(q_len)) && KVH > 0 && (H / KVH) * q_len >= 2;
 }
-int64_t mq_groups(int batch, int q_len, int H, int KVH) {
+// Query rows per tile: 16 on the fp16 pool, 8 on the INT4 pool (whose score
+// mma holds each row's two integer halves as separate rows).
+int mq_tile_rows(bool int4) { return int4 ? 8 : 16; }
+int64_t mq_groups(int batch, int q_len, int H, int KVH, int tile_rows) {
   const int rows = (H / KVH) * q_len;
-  return static_cast<int64_t>(batch) * KVH * ((rows + 15) / 16);
+  return static_cast<int64_t>(batch) * KVH * ((rows + tile_rows - 1) / tile_rows);
 }
 // A tile's rows may span q_len - 1 extra tokens (causal rows end at their own
 // token), so its chunks cover window + q_len - 1 tokens.
-Split mq_split(int batch, int q_len, int H, int KVH, int MB, int BS, int window) {
-  return choose_split(mq_groups(batch, q_len, H, KVH), MB, BS, window + q_len - 1, kSplitF16);
+Split mq_split(bool int4, int batch, int q_len, int H, int KVH, int MB, int BS, int window) {
+  return choose_split(mq_groups(batch, q_len, H, KVH, mq_tile_rows(int4)), MB, BS, window + q_len - 1,
+                      int4 ? kSplitInt4 : kSplitF16);
 }
 
-template <int D, int BS, bool INT4>
+template <int D, int BS>
+int launch_mq4(const decode_mq::Params& p, cudaStream_t s) {
+  using C = decode_mq4::Cfg<D, BS>;
+  auto kern = decode_mq4::paged_decode_mq4_kernel<D, BS>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_mq4)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t ctas_needed = (p.total_items + C::NW - 1) / C::NW;
+  int per_sm = (227 * 1024) / C::SMEM;
+  if (per_sm > C::MIN_BLOCKS) per_sm = C::MIN_BLOCKS;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  kern<<<grid, C::NW * 32, C::SMEM, s>>>(p, nullptr);
+  MEMOPT_LAUNCH_CHECK("paged_decode_mq4_kernel launch");
+  return MEMOPT_OK;
+}
+
+template <int D, int BS>
 int launch_mq(const decode_mq::Params& p, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
-  using C = decode_mq::Cfg<D, BS, INT4>;
-  auto kern = decode_mq::paged_decode_mq_kernel<D, BS, INT4>;
+  using C = decode_mq::Cfg<D>;
+  auto kern = decode_mq::paged_decode_mq_kernel<D, BS>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -202,12 +230,14 @@ int run_mq(const Params& one, const void* key_pool, const void* value_pool, int 
   p.NB = one.NB;
   p.window = one.window;
   p.qscale = one.qscale;
+  p.magic_f16 = one.magic_f16;
+  p.magic_s8 = one.magic_s8;
   p.rows = one.group * one.QL;
-  p.tiles = (p.rows + 15) / 16;
-  const Split sp = mq_split(one.B, one.QL, one.H, one.KVH, one.MB, BS, one.window);
+  p.tiles = (p.rows + mq_tile_rows(int4) - 1) / mq_tile_rows(int4);
+  const Split sp = mq_split(int4, one.B, one.QL, one.H, one.KVH, one.MB, BS, one.window);
   p.chunk_pages = sp.chunk_pages;
   p.n_chunks = sp.n_chunks;
-  p.total_items = mq_groups(one.B, one.QL, one.H, one.KVH) * sp.n_chunks;
+  p.total_items = mq_groups(one.B, one.QL, one.H, one.KVH, mq_tile_rows(int4)) * sp.n_chunks;
   const int64_t pairs = static_cast<int64_t>(one.B) * one.QL * one.H;
   const WsLayout w = ws_layout(pairs, sp.n_chunks, D);
   if (w.total > 0) {
@@ -221,12 +251,10 @@ int run_mq(const Params& one, const void* key_pool, const void* value_pool, int 
   }
   alignas(64) CUtensorMap km, vm;
   if (int4) {
-    std::memset(&km, 0, sizeof(km));
-    std::memset(&vm, 0, sizeof(vm));
-    if (D == 128 && BS == 16) return launch_mq<128, 16, true>(p, km, vm, s);
-    if (D == 128 && BS == 32) return launch_mq<128, 32, true>(p, km, vm, s);
-    if (D == 64 && BS == 16) return launch_mq<64, 16, true>(p, km, vm, s);
-    if (D == 64 && BS == 32) return launch_mq<64, 32, true>(p, km, vm, s);
+    if (D == 128 && BS == 16) return launch_mq4<128, 16>(p, s);
+    if (D == 128 && BS == 32) return launch_mq4<128, 32>(p, s);
+    if (D == 64 && BS == 16) return launch_mq4<64, 16>(p, s);
+    if (D == 64 && BS == 32) return launch_mq4<64, 32>(p, s);
     return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention_int4: unsupported geometry");
   }
   const int64_t rows = one.NB * BS;
@@ -234,10 +262,10 @@ int run_mq(const Params& one, const void* key_pool, const void* value_pool, int 
   if (st != MEMOPT_OK) return st;
   st = make_pool_map_sw(&vm, value_pool, rows, one.KVH, D);
   if (st != MEMOPT_OK) return st;
-  if (D == 128 && BS == 16) return launch_mq<128, 16, false>(p, km, vm, s);
-  if (D == 128 && BS == 32) return launch_mq<128, 32, false>(p, km, vm, s);
-  if (D == 64 && BS == 16) return launch_mq<64, 16, false>(p, km, vm, s);
-  if (D == 64 && BS == 32) return launch_mq<64, 32, false>(p, km, vm, s);
+  if (D == 128 && BS == 16) return launch_mq<128, 16>(p, km, vm, s);
+  if (D == 128 && BS == 32) return launch_mq<128, 32>(p, km, vm, s);
+  if (D == 64 && BS == 16) return launch_mq<64, 16>(p, km, vm, s);
+  if (D == 64 && BS == 32) return launch_mq<64, 32>(p, km, vm, s);
   return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: unsupported geometry");
 }
 
@@ -355,10 +383,12 @@ extern "C" size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len,
   const size_t b = ws_layout(pairs, choose_split(pairs, max_blocks_per_seq, block_size, w, kSplitInt4).n_chunks,
                              head_dim).total;
   if (b > need) need = b;
-  if (use_mq(false, q_len, num_heads, num_kv_heads) || use_mq(true, q_len, num_heads, num_kv_heads)) {
-    const size_t c =
-        ws_layout(pairs, mq_split(batch, q_len, num_heads, num_kv_heads, max_blocks_per_seq, block_size, w).n_chunks,
-                  head_dim).total;
+  for (int f = 0; f < 2; ++f) {
+    if (!use_mq(f == 1, q_len, num_heads, num_kv_heads)) continue;
+    const size_t c = ws_layout(pairs,
+                               mq_split(f == 1, batch, q_len, num_heads, num_kv_heads, max_blocks_per_seq,
+                                        block_size, w).n_chunks,
+                               head_dim).total;
     if (c > need) need = c;
   }
   return need;

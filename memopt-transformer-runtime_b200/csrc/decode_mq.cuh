@@ -38,7 +38,7 @@ struct Params {
   __half* out;         // [B, QL, H, D]
   const int32_t* bt;   // [B, MB]
   const int32_t* ctx;  // [B]
-  const uint8_t* pages;  // INT4 pool: [NB, KVH, page bytes]
+  const uint8_t* pages;  // INT4 pool [NB, KVH, page bytes] (decode_mq4.cuh)
   int32_t* tickets;    // [B * KVH * tiles]
   float2* ml;          // [B * QL * H * n_chunks]  (per query row, as the one-row kernel)
   float* po;           // [B * QL * H * n_chunks * D]
@@ -46,34 +46,27 @@ struct Params {
   int64_t NB;
   int window;          // clamped
   float qscale;        // log2(e) / sqrt(D)
+  uint32_t magic_f16;  // INT4 conversion constants kept in registers (0x64006400, 0x80808080)
+  uint32_t magic_s8;
   int rows;            // group * QL query rows per (sequence, KV head)
-  int tiles;           // ceil(rows / 16)
+  int tiles;           // ceil(rows / rows per tile)
   int chunk_pages;
   int n_chunks;
   int64_t total_items;
 };
 
-template <int D, int BS, bool INT4>
+template <int D>
 struct Cfg {
-  static constexpr int G = D / 64;              // 64-dim regions (and INT4 scale groups)
   static constexpr int REG = 16 * 128;          // one 64-dim region of 16 tokens (128-byte rows)
-  // fp16: a stage is one 16-token tile, K regions then V regions (TMA, swizzled).
-  // INT4: a stage is one whole page (one bulk copy); its V codes are expanded
-  // per 16-token tile into a per-warp fp16 scratch tile of G swizzled regions.
-  static constexpr int PAGE_RAW = BS * D + 2 * BS * G * 2;  // INT4 page bytes
-  static constexpr int STAGE = INT4 ? (PAGE_RAW + 127) / 128 * 128 : 2 * G * REG;
-  static constexpr int SCRATCH = INT4 ? G * REG : 0;
-  static constexpr int V_CODES = BS * D / 2;           // INT4 page: V code rows
-  static constexpr int K_SCALE = BS * D;               // [BS][G] fp16
-  static constexpr int V_SCALE = BS * D + BS * G * 2;  // per 16-token tile [G][16] fp16, permuted
+  static constexpr int NREG = D / 64;           // regions per K (and per V) stage half
+  static constexpr int STAGE = 2 * NREG * REG;  // K regions then V regions
   static constexpr int NW = 4;                  // warps per CTA
-  static constexpr int WARP_BUDGET = INT4 ? 16384 : 24576;
+  static constexpr int WARP_BUDGET = 24576;
   static constexpr int NS_RAW = WARP_BUDGET / STAGE;
   static constexpr int NS = NS_RAW > 8 ? 8 : NS_RAW;
   static constexpr int MIN_BLOCKS = 2;
   static constexpr int BAR_BYTES = 1024;
-  static constexpr int WARP_BYTES = (NS * STAGE + SCRATCH + 1023) / 1024 * 1024;
-  static constexpr int SMEM = BAR_BYTES + NW * WARP_BYTES;
+  static constexpr int SMEM = BAR_BYTES + NW * NS * STAGE;
   static_assert(NS >= 2, "ring too shallow");
   static_assert(NW * NS * 8 <= BAR_BYTES, "barrier area too small");
 };
@@ -91,15 +84,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "memory");
 }
 
-template <int D, int BS, bool INT4>
-__global__ void __launch_bounds__(Cfg<D, BS, INT4>::NW * 32, Cfg<D, BS, INT4>::MIN_BLOCKS)
+template <int D, int BS>
+__global__ void __launch_bounds__(Cfg<D>::NW * 32, Cfg<D>::MIN_BLOCKS)
 paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, int32_t* __restrict__ err) {
-  using C = Cfg<D, BS, INT4>;
+  using C = Cfg<D>;
   constexpr int NS = C::NS;
-  constexpr int G = C::G;
-  constexpr int HALVES = BS / 16;             // 16-token tiles per page
-  constexpr int SPP = INT4 ? 1 : HALVES;      // ring stages per page
+  constexpr int HALVES = BS / 16;  // 16-token stages per page
   constexpr int KK = D / 16;       // k-steps of Q.K^T
   constexpr int NT = D / 8;        // n-tiles of P.V
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -107,16 +98,13 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
   const int wid = threadIdx.x >> 5;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + wid * NS;
   const uint32_t bar0 = smem_u32(bars);
-  const uint32_t st0 = smem_u32(smem + C::BAR_BYTES + wid * C::WARP_BYTES);
-  const uint32_t scr = st0 + NS * C::STAGE;  // INT4: this warp's fp16 V tile
+  const uint32_t st0 = smem_u32(smem + C::BAR_BYTES + wid * NS * C::STAGE);
 
   if (lane == 0) {
     for (int s = 0; s < NS; ++s) mbar_init(bar0 + 8 * s, 1);
     fence_mbar_init();
-    if (!INT4) {
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-    }
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
   }
   __syncwarp();
 
@@ -155,30 +143,24 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
     mask = __ballot_sync(0xffffffffu, ok);
   };
 
-  // fp16: one 16-token stage, K then V, each as D/64 swizzled 64-dim boxes.
-  // INT4: the whole (block, head) page in one bulk copy.
+  // One 16-token stage: K then V, each as D/64 swizzled 64-dim boxes.
   auto issue = [&](uint32_t seq, int phys, int half, int kvh) {
     const int s = static_cast<int>(seq % NS);
     const uint32_t bar = bar0 + 8 * s;
     const uint32_t dst = st0 + s * C::STAGE;
+    const int row = phys * BS + half * 16;
     fence_proxy_async_smem();
-    if constexpr (INT4) {
-      mbar_arrive_expect_tx(bar, C::PAGE_RAW);
-      bulk_g2s(dst, p.pages + (static_cast<int64_t>(phys) * p.KVH + kvh) * C::PAGE_RAW, C::PAGE_RAW, bar);
-    } else {
-      const int row = phys * BS + half * 16;
-      mbar_arrive_expect_tx(bar, C::STAGE);
+    mbar_arrive_expect_tx(bar, C::STAGE);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        tma_load_3d(dst + g * C::REG, &kmap, 64 * g, kvh, row, bar);
-        tma_load_3d(dst + (G + g) * C::REG, &vmap, 64 * g, kvh, row, bar);
-      }
+    for (int g = 0; g < C::NREG; ++g) {
+      tma_load_3d(dst + g * C::REG, &kmap, 64 * g, kvh, row, bar);
+      tma_load_3d(dst + (C::NREG + g) * C::REG, &vmap, 64 * g, kvh, row, bar);
     }
   };
 
   // ---------------- producer cursor (warp-uniform) ----------------------
   int64_t p_item = first - nwarps;
-  int p_sub = 0, p_half = SPP;  // p_half == SPP: take the next page
+  int p_sub = 0, p_half = HALVES;  // p_half == HALVES: take the next page
   bool p_more = false;
   uint32_t p_mask = 0;
   int p_phys = -1, p_page = -1;
@@ -188,7 +170,7 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
 
   auto produce = [&]() {
     if (p_done) return;
-    if (p_half == SPP) {
+    if (p_half == HALVES) {
       while (!p_done && p_mask == 0) {
         if (p_more) {
           ++p_sub;
@@ -264,30 +246,15 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
       rlo[hr] = p.window < e ? e - p.window : 0;
       rhi[hr] = rvalid[hr] ? e : 0;
     }
-    // Q as the A operand: a0/a2 row g8, a1/a3 row g8 + 8.  fp16: k index
-    // 2t4 (+1) of k-step kk is dim 16kk + 2t4 (+1), 2t4 + 8 (+1) is + 8.
-    // INT4: the k order follows the code words (see the K fragments below):
-    // k-step kk lies in scale group g = kk / 4; with w = 8 (2 t4 + (kk & 3) / 2)
-    // + 64 g and sel = 2 (kk & 1), k 2t4, 2t4+1 are dims w + sel, w + 4 + sel
-    // and k 2t4+8, 2t4+9 are dims w + sel + 1, w + 5 + sel.
+    // Q as the A operand: a0/a2 row g8 (dims +2t4, +2t4+8), a1/a3 row g8 + 8.
     uint32_t qa[KK][4];
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
-      const __half* qrow = p.q + rpair[hr] * D;
+      const __half* qrow = p.q + rpair[hr] * D + 2 * t4;
 #pragma unroll
       for (int kk = 0; kk < KK; ++kk) {
-        if constexpr (!INT4) {
-          qa[kk][hr] = rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t4)) : 0u;
-          qa[kk][2 + hr] =
-              rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * t4 + 8)) : 0u;
-        } else {
-          const int w = 64 * (kk / 4) + 8 * (2 * t4 + ((kk & 3) >> 1));
-          const int sel = 2 * (kk & 1);
-          const uint32_t h0 = rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + w + sel)) : 0u;
-          const uint32_t h4 = rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + w + 4 + sel)) : 0u;
-          qa[kk][hr] = __byte_perm(h0, h4, 0x5410);      // (dim w+sel, dim w+4+sel)
-          qa[kk][2 + hr] = __byte_perm(h0, h4, 0x7632);  // (dim w+sel+1, dim w+5+sel)
-        }
+        qa[kk][hr] = rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * kk)) : 0u;
+        qa[kk][2 + hr] = rvalid[hr] ? __ldg(reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 8)) : 0u;
       }
     }
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
@@ -307,96 +274,23 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
         const int page = c_lo + jpage;
 #pragma unroll 1
         for (int half = 0; half < HALVES; ++half) {
-          if (!INT4 || half == 0) {
-            if (!wait_stage(c_seq)) {
-              failed = true;
-              break;
-            }
+          if (!wait_stage(c_seq)) {
+            failed = true;
+            break;
           }
           const uint32_t stg = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
           const int tok0 = page * BS + half * 16;
+          // ---- S = Q K^T on the tensor pipe ----
           float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-          if constexpr (!INT4) {
-            // ---- S = Q K^T on the tensor pipe ----
 #pragma unroll
-            for (int kk = 0; kk < KK; ++kk) {
-              const int ch = 2 * kk + k_dhalf;
-              const uint32_t addr =
-                  stg + (ch >> 3) * C::REG + k_tok * 128 + (((ch & 7) ^ (k_tok & 7)) << 4);
-              uint32_t b00, b01, b10, b11;
-              ldsm_x4(addr, b00, b01, b10, b11);
-              int4mma::mma16816(s[0], qa[kk], b00, b01);
-              int4mma::mma16816(s[1], qa[kk], b10, b11);
-            }
-          } else {
-            // ---- S = Q K^T from the codes: B fragments straight from the
-            // code words, one accumulator set per scale group, the K scales
-            // applied per token afterwards.  Word (1024 + c) halves minus
-            // 1032 are the exact integers c - 8. ----
-            const __half2 k1032 = __float2half2_rn(1032.f);
-            float sg[G][2][4];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt) {
-                sg[g][nt][0] = sg[g][nt][1] = sg[g][nt][2] = sg[g][nt][3] = 0.f;
-                const int pos = half * 16 + nt * 8 + g8;  // token row of this lane's B column
-                const uint2 w2 = lds_v2(stg + pos * (D / 2) + 32 * g + 8 * t4);
-#pragma unroll
-                for (int wl = 0; wl < 2; ++wl) {
-                  const uint32_t w = wl ? w2.y : w2.x;
-                  uint32_t x[4];
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) {
-                    const uint32_t r = int4mma::and_or(w >> (4 * j), 0x000F000Fu, 0x64006400u);
-                    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&r), k1032);
-                    x[j] = *reinterpret_cast<const uint32_t*>(&h);
-                  }
-                  int4mma::mma16816(sg[g][nt], qa[4 * g + 2 * wl], x[0], x[1]);
-                  int4mma::mma16816(sg[g][nt], qa[4 * g + 2 * wl + 1], x[2], x[3]);
-                }
-              }
-            }
-            // K scales: token column tok of the fragment, group g.
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int pos = half * 16 + nt * 8 + 2 * t4 + e;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                  const float ks = lds_f16_as_f32(stg + C::K_SCALE + (pos * G + g) * 2);
-                  s[nt][e] = fmaf(ks, sg[g][nt][e], s[nt][e]);
-                  s[nt][2 + e] = fmaf(ks, sg[g][nt][2 + e], s[nt][2 + e]);
-                }
-              }
-            }
-            // ---- V codes of the tile -> exact fp16 values c - 8 in the
-            // warp's scratch tile ([token][dim] 128-byte rows, swizzled;
-            // inside each 8-dim chunk the dims sit in the order 0 4 1 5 2 6
-            // 3 7, which the output mapping undoes).  The V scales are folded
-            // into P per scale group instead. ----
-            __syncwarp();  // the previous tile's reads of the scratch are done
-#pragma unroll
-            for (int i = 0; i < (16 * D / 8) / 32; ++i) {
-              const int qd = lane + 32 * i;
-              const int tr = qd / (D / 8), c = qd % (D / 8);
-              const int pos = half * 16 + tr;
-              const int byte = (D == 128 && (pos & 2)) ? ((4 * c) ^ 32) : 4 * c;
-              const uint32_t w = lds_u32(stg + C::V_CODES + pos * (D / 2) + byte);
-              uint32_t x[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t r = int4mma::and_or(w >> (4 * j), 0x000F000Fu, 0x64006400u);
-                const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&r), k1032);
-                x[j] = *reinterpret_cast<const uint32_t*>(&h);
-              }
-              const uint32_t addr = scr + (c >> 3) * C::REG + tr * 128 + (((c & 7) ^ (tr & 7)) << 4);
-              asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(x[0]), "r"(x[1]), "r"(x[2]),
-                           "r"(x[3])
-                           : "memory");
-            }
-            __syncwarp();
+          for (int kk = 0; kk < KK; ++kk) {
+            const int ch = 2 * kk + k_dhalf;
+            const uint32_t addr =
+                stg + (ch >> 3) * C::REG + k_tok * 128 + (((ch & 7) ^ (k_tok & 7)) << 4);
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(addr, b00, b01, b10, b11);
+            int4mma::mma16816(s[0], qa[kk], b00, b01);
+            int4mma::mma16816(s[1], qa[kk], b10, b11);
           }
           // ---- scale, mask, online softmax (rows g8 and g8 + 8) ----
           const bool interior = tok0 >= rlo[0] && tok0 + 16 <= rhi[0] && tok0 >= rlo[1] && tok0 + 16 <= rhi[1];
@@ -422,7 +316,8 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
             mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
             const float mn = fmaxf(m[hr], mx[hr]);
             const float msub = mn == -INFINITY ? 0.f : mn;  // a row with nothing visible yet
-            corr[hr] = int4mma::ex2_approx(m[hr] - msub);
+            // A row that has seen nothing yet has zero accumulators: no rescale.
+            corr[hr] = m[hr] == -INFINITY ? 1.f : int4mma::ex2_approx(m[hr] - msub);
             m[hr] = mn;
             mx[hr] = msub;
           }
@@ -448,61 +343,25 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
             }
           }
           // P as the A operand: the S fragments of tokens 0-7 and 8-15.
-          if constexpr (!INT4) {
-            uint32_t pa[4];
-            pa[0] = int4mma::pack_half2(s[0][0], s[0][1]);
-            pa[1] = int4mma::pack_half2(s[0][2], s[0][3]);
-            pa[2] = int4mma::pack_half2(s[1][0], s[1][1]);
-            pa[3] = int4mma::pack_half2(s[1][2], s[1][3]);
-            // ---- O += P V (V transposed out of shared memory) ----
+          uint32_t pa[4];
+          pa[0] = int4mma::pack_half2(s[0][0], s[0][1]);
+          pa[1] = int4mma::pack_half2(s[0][2], s[0][3]);
+          pa[2] = int4mma::pack_half2(s[1][0], s[1][1]);
+          pa[3] = int4mma::pack_half2(s[1][2], s[1][3]);
+          // ---- O += P V (V transposed out of shared memory) ----
 #pragma unroll
-            for (int nn = 0; nn < D / 16; ++nn) {
-              const int ch = 2 * nn + v_dhalf;
-              const uint32_t addr =
-                  stg + (G + (ch >> 3)) * C::REG + v_tok * 128 + (((ch & 7) ^ (v_tok & 7)) << 4);
-              uint32_t v0, v1, v2, v3;
-              ldsm_x4_t(addr, v0, v1, v2, v3);
-              int4mma::mma16816(o[2 * nn], pa, v0, v1);
-              int4mma::mma16816(o[2 * nn + 1], pa, v2, v3);
-            }
-          } else {
-            // P'_g = P * (V scale of the token, group g): one A operand per group.
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-              float vs[2][2];
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int pos = half * 16 + nt * 8 + 2 * t4 + e;
-                  const int r = pos & 15;
-                  const int slot = ((pos >> 4) * G + g) * 16 + 2 * (r & 3) + ((r >> 2) & 1) + 8 * (r >> 3);
-                  vs[nt][e] = lds_f16_as_f32(stg + C::V_SCALE + slot * 2);
-                }
-              }
-              uint32_t pa[4];
-              pa[0] = int4mma::pack_half2(s[0][0] * vs[0][0], s[0][1] * vs[0][1]);
-              pa[1] = int4mma::pack_half2(s[0][2] * vs[0][0], s[0][3] * vs[0][1]);
-              pa[2] = int4mma::pack_half2(s[1][0] * vs[1][0], s[1][1] * vs[1][1]);
-              pa[3] = int4mma::pack_half2(s[1][2] * vs[1][0], s[1][3] * vs[1][1]);
-#pragma unroll
-              for (int nl = 0; nl < 4; ++nl) {
-                const int nn = 4 * g + nl;
-                const int ch = 2 * nn + v_dhalf;
-                const uint32_t addr =
-                    scr + (ch >> 3) * C::REG + v_tok * 128 + (((ch & 7) ^ (v_tok & 7)) << 4);
-                uint32_t v0, v1, v2, v3;
-                ldsm_x4_t(addr, v0, v1, v2, v3);
-                int4mma::mma16816(o[2 * nn], pa, v0, v1);
-                int4mma::mma16816(o[2 * nn + 1], pa, v2, v3);
-              }
-            }
+          for (int nn = 0; nn < D / 16; ++nn) {
+            const int ch = 2 * nn + v_dhalf;
+            const uint32_t addr = stg + (C::NREG + (ch >> 3)) * C::REG + v_tok * 128 +
+                                  (((ch & 7) ^ (v_tok & 7)) << 4);
+            uint32_t v0, v1, v2, v3;
+            ldsm_x4_t(addr, v0, v1, v2, v3);
+            int4mma::mma16816(o[2 * nn], pa, v0, v1);
+            int4mma::mma16816(o[2 * nn + 1], pa, v2, v3);
           }
-          if (!INT4 || half == HALVES - 1) {
-            ++c_seq;
-            __syncwarp();
-            produce();
-          }
+          ++c_seq;
+          __syncwarp();
+          produce();
         }
         if (failed) break;
       }
@@ -523,20 +382,11 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
       for (int hr = 0; hr < 2; ++hr) {
         if (!rvalid[hr]) continue;
         const float inv = l[hr] > 0.f ? 1.f / l[hr] : 0.f;
-        if constexpr (!INT4) {
-          __half* orow = p.out + rpair[hr] * D + 2 * t4;
+        __half* orow = p.out + rpair[hr] * D + 2 * t4;
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            *reinterpret_cast<__half2*>(orow + 8 * nt) =
-                __floats2half2_rn(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
-        } else {  // columns 2t4, 2t4 + 1 of an n-tile are dims t4, t4 + 4
-          __half* orow = p.out + rpair[hr] * D + t4;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            orow[8 * nt] = __float2half_rn(o[nt][2 * hr] * inv);
-            orow[8 * nt + 4] = __float2half_rn(o[nt][2 * hr + 1] * inv);
-          }
-        }
+        for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<__half2*>(orow + 8 * nt) =
+              __floats2half2_rn(o[nt][2 * hr] * inv, o[nt][2 * hr + 1] * inv);
       }
       continue;
     }
@@ -544,19 +394,10 @@ paged_decode_mq_kernel(const __grid_constant__ Params p, const __grid_constant__
     for (int hr = 0; hr < 2; ++hr) {
       if (!rvalid[hr]) continue;
       const int64_t slot = rpair[hr] * p.n_chunks + chunk;
-      if constexpr (!INT4) {
-        float* dst = p.po + slot * D + 2 * t4;
+      float* dst = p.po + slot * D + 2 * t4;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          *reinterpret_cast<float2*>(dst + 8 * nt) = make_float2(o[nt][2 * hr], o[nt][2 * hr + 1]);
-      } else {
-        float* dst = p.po + slot * D + t4;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          dst[8 * nt] = o[nt][2 * hr];
-          dst[8 * nt + 4] = o[nt][2 * hr + 1];
-        }
-      }
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float2*>(dst + 8 * nt) = make_float2(o[nt][2 * hr], o[nt][2 * hr + 1]);
       if (t4 == 0) p.ml[slot] = make_float2(m[hr], l[hr]);
     }
     __threadfence();

@@ -25,6 +25,7 @@ def lib() -> C.CDLL:
         _lib = C.CDLL(_LIB_PATH)
         _lib.memopt_last_error.restype = C.c_char_p
         _lib.memopt_paged_attention_workspace_size.restype = SZ
+        _lib.memopt_paged_attention_workspace_size_ex.restype = SZ
         _lib.memopt_paged_attention_ticket_bytes.restype = SZ
     return _lib
 
@@ -49,6 +50,30 @@ def paged_attention_int4(q, pages, block_size, bt, ctx, out, msl, win, ws, ws_by
         P(q.data_ptr()), P(pages.data_ptr()), P(bt.data_ptr()), P(ctx.data_ptr()), I(B), I(QL), I(H), I(D),
         I(bt.shape[1]), I64(pages.shape[0]), I(block_size), I(msl), I(win), P(out.data_ptr()),
         P(ws.data_ptr() if ws is not None else 0), SZ(ws_bytes), P(stream)), "memopt_paged_attention_int4")
+
+
+def paged_attention_f16_ex(q, kpool, vpool, bt, ctx, out, msl, win, causal, ws, ws_bytes, stream):
+    """Pools of kpool.shape[2] heads (dividing the query's H)."""
+    B, QL, H, D = q.shape
+    check(lib().memopt_paged_attention_f16_ex(
+        P(q.data_ptr()), P(kpool.data_ptr()), P(vpool.data_ptr()), P(bt.data_ptr()), P(ctx.data_ptr()),
+        I(B), I(QL), I(H), I(kpool.shape[2]), I(D), I(bt.shape[1]), I64(kpool.shape[0]), I(kpool.shape[1]),
+        I(msl), I(win), I(int(causal)), P(out.data_ptr()), P(ws.data_ptr() if ws is not None else 0),
+        SZ(ws_bytes), P(stream)), "memopt_paged_attention_f16_ex")
+
+
+def paged_attention_int4_ex(q, pages, block_size, bt, ctx, out, msl, win, causal, ws, ws_bytes, stream):
+    """INT4 pages [NB, KVH, page_bytes] with KVH dividing the query's H."""
+    B, QL, H, D = q.shape
+    check(lib().memopt_paged_attention_int4_ex(
+        P(q.data_ptr()), P(pages.data_ptr()), P(bt.data_ptr()), P(ctx.data_ptr()), I(B), I(QL), I(H),
+        I(pages.shape[1]), I(D), I(bt.shape[1]), I64(pages.shape[0]), I(block_size), I(msl), I(win),
+        I(int(causal)), P(out.data_ptr()), P(ws.data_ptr() if ws is not None else 0), SZ(ws_bytes), P(stream)),
+        "memopt_paged_attention_int4_ex")
+
+
+def workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win) -> int:
+    return int(lib().memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win))
 
 
 def workspace_size(B, QL, H, D, MB, BS, msl, win) -> int:
