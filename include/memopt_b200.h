@@ -179,6 +179,17 @@ int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, 
                               int32_t* freed_count, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/* The same operator on an INT4 pool: kv_pages [pool_num_blocks][num_heads]   */
+/* [page bytes] as written by write_cache (head_dim 64 or 128, block_size a   */
+/* multiple of 16, <= 64 heads); each kept token's codes and scales move with */
+/* it (the position-dependent V row and V scale layout re-laid out).          */
+int memopt_evict_topk_compact_int4(const float* scores, int num_seqs, int num_heads, int max_len,
+                                   int32_t* block_tables, int max_blocks_per_seq, int32_t* context_lens,
+                                   uint8_t* kv_pages, int pool_num_blocks, int block_size, int head_dim,
+                                   float retain_ratio, int num_sink_tokens, int32_t* kept_idx, int32_t* kept_count,
+                                   int32_t* freed_pages, int32_t* freed_count, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Head-sharded form of the same operator (the one cross-GPU exchange of the  */
 /* data plane): with the heads of every sequence split over G ranks, rank r   */
 /* writes the fp32 sum of its own heads' scores (heads in order) with         */

@@ -32,6 +32,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "int4.cuh"
 #include "memopt_b200.h"
 
 namespace memopt {
@@ -364,6 +365,104 @@ __global__ void __launch_bounds__(32) move_rows_inplace_kernel(
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// The same move on INT4 pages ([num_blocks][KVH][page bytes], layout of
+// int4.cuh): a token row is, in each head's page, a K code row, a V code row
+// (16-byte chunks exchanged in pairs on rows whose position has bit 1 set, at
+// D = 128), the K scales and the V scales (slots permuted per 16-token tile),
+// so the position-dependent parts are re-laid out for the destination.  One
+// warp per row, lane h moving heads h and h + 32 (KVH <= 64) through
+// registers; the read flag is published after the warp's loads completed.
+template <int D>
+__global__ void __launch_bounds__(32) move_rows_int4_kernel(
+    const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ src_ord,
+    const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
+    const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
+    int nseg, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags) {
+  constexpr int G = D / 64;
+  constexpr int CB = D / 2;     // code row bytes
+  constexpr int NCH = CB / 16;  // 16-byte chunks per code row
+  const int lane = threadIdx.x;
+  int ticket = 0;
+  if (lane == 0) ticket = atomicAdd(&ctrl[0], 1);
+  ticket = __shfl_sync(0xffffffffu, ticket, 0);
+  const int b = ticket / nseg, row = ticket % nseg;  // one row per segment
+  if (row >= kept_count[b]) return;
+  const int64_t rb = static_cast<int64_t>(b) * max_len;
+  int* my_flag = flags + static_cast<int64_t>(b) * kMaxSegs + row;
+  if (src_ord[rb + row] == row) {  // already in place
+    if (lane == 0) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+    return;
+  }
+  const int t = kept_idx[rb + row];
+  const int sp = old_bt[static_cast<int64_t>(b) * MB + t / BS], spos = t % BS;
+  const int dp = new_bt[static_cast<int64_t>(b) * MB + row / BS], dpos = row % BS;
+  const int sswap = (D == 128 && (spos & 2)) ? 2 : 0, dswap = (D == 128 && (dpos & 2)) ? 2 : 0;
+  uint4 kc[2][NCH], vc[2][NCH];
+  uint16_t ks[2][G], vs[2][G];
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const int h = lane + 32 * hi;
+    if (h >= KVH) continue;
+    const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
+    const uint4* kr = reinterpret_cast<const uint4*>(pg + spos * CB);
+    const uint4* vr = reinterpret_cast<const uint4*>(pg + BS * CB + spos * CB);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      kc[hi][c] = kr[c];
+      vc[hi][c] = vr[c ^ sswap];  // logical chunk c
+    }
+    const uint16_t* ksp = reinterpret_cast<const uint16_t*>(pg + BS * D) + spos * G;
+    const uint16_t* vsp = reinterpret_cast<const uint16_t*>(pg + BS * D + BS * G * 2);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      ks[hi][g] = ksp[g];
+      vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
+    }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+    // Wait until the row that lives at this row's destination has been read.
+    const int d = seg_dep[static_cast<int64_t>(b) * kMaxSegs + row];
+    for (int m = d; m < row && m <= d + 1; ++m) {
+      const int* f = flags + static_cast<int64_t>(b) * kMaxSegs + m;
+      uint32_t polls = 0;
+      int v = 0;
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v) break;
+        if (++polls > kMaxPolls) {
+          atomicExch(&ctrl[1], 1);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const int h = lane + 32 * hi;
+    if (h >= KVH) continue;
+    uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
+    uint4* kr = reinterpret_cast<uint4*>(pg + dpos * CB);
+    uint4* vr = reinterpret_cast<uint4*>(pg + BS * CB + dpos * CB);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      kr[c] = kc[hi][c];
+      vr[c ^ dswap] = vc[hi][c];
+    }
+    uint16_t* ksp = reinterpret_cast<uint16_t*>(pg + BS * D) + dpos * G;
+    uint16_t* vsp = reinterpret_cast<uint16_t*>(pg + BS * D + BS * G * 2);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      ksp[g] = ks[hi][g];
+      vsp[int4_vscale_index(dpos, g, G)] = vs[hi][g];
+    }
+  }
+}
+
 }  // namespace
 
 // Workspace: old block tables, token sums, source ordinals, segment
@@ -391,7 +490,9 @@ extern "C" __attribute__((visibility("default"))) size_t memopt_evict_topk_works
   return topk_ws_layout(num_seqs, max_len, &a, &b, &c, &d, &e);
 }
 
-static int topk_compact(const char* who, const float* src, int64_t b_stride, int64_t i_stride, int n_terms,
+// int4: key_pool holds the INT4 pages [pool_num_blocks][num_heads][page
+// bytes] and value_pool is unused.
+static int topk_compact(const char* who, bool int4, const float* src, int64_t b_stride, int64_t i_stride, int n_terms,
                         int num_seqs, int num_heads, int max_len, int32_t* block_tables, int max_blocks_per_seq,
                         int32_t* context_lens, void* key_pool, void* value_pool, int pool_num_blocks,
                         int block_size, int head_dim, float retain_ratio, int num_sink_tokens, int32_t* kept_idx,
@@ -405,9 +506,13 @@ static int topk_compact(const char* who, const float* src, int64_t b_stride, int
   if (max_len > kMaxLen) return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": max_len exceeds 32768");
   if (max_blocks_per_seq > 2 * kSelThreads)
     return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": more than 2048 blocks per sequence");
-  if ((num_heads * head_dim) % 8 != 0)
+  if (!int4 && (num_heads * head_dim) % 8 != 0)
     return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim must be a multiple of 8");
+  if (int4 && !((head_dim == 64 || head_dim == 128) && block_size % 16 == 0 && num_heads <= 64))
+    return fail(MEMOPT_ERR_UNSUPPORTED,
+                std::string(who) + ": INT4 pages need head_dim 64 or 128, block_size % 16 == 0, <= 64 heads");
   if (num_seqs == 0 || max_len == 0) return MEMOPT_OK;
+  if (int4) value_pool = key_pool;
   if (!src || !block_tables || !context_lens || !key_pool || !value_pool || !kept_idx || !kept_count ||
       !freed_pages || !freed_count || !workspace)
     return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": null pointer");
@@ -419,7 +524,7 @@ static int topk_compact(const char* who, const float* src, int64_t b_stride, int
   cudaStream_t s = as_stream(stream);
   const uint32_t row_bytes = static_cast<uint32_t>(num_heads) * head_dim * 2;
   const size_t stage_bytes = static_cast<size_t>(2 * kSegRows) * row_bytes;
-  if (stage_bytes > static_cast<size_t>(kMoveSmemLimit))
+  if (!int4 && stage_bytes > static_cast<size_t>(kMoveSmemLimit))
     return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim above " +
                                              std::to_string(kMoveSmemLimit / (4 * kSegRows)));
   cudaError_t ea = cudaFuncSetAttribute(move_rows_inplace_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -447,6 +552,20 @@ static int topk_compact(const char* who, const float* src, int64_t b_stride, int
                                                       kept_count, freed_pages, freed_count, ord, dep);
   MEMOPT_LAUNCH_CHECK("topk_select_kernel launch");
   const int nseg = (max_len + kSegRows - 1) / kSegRows;
+  if (int4) {
+    const int64_t pb = static_cast<int64_t>(block_size) * head_dim + static_cast<int64_t>(block_size) * (head_dim / 64) * 4;
+    uint8_t* pages = static_cast<uint8_t*>(key_pool);
+    if (head_dim == 128)
+      move_rows_int4_kernel<128><<<num_seqs * nseg, 32, 0, s>>>(kept_idx, ord, kept_count, dep, old_bt, block_tables,
+                                                                max_blocks_per_seq, max_len, block_size, nseg, pages,
+                                                                num_heads, pb, ctrl, flags);
+    else
+      move_rows_int4_kernel<64><<<num_seqs * nseg, 32, 0, s>>>(kept_idx, ord, kept_count, dep, old_bt, block_tables,
+                                                               max_blocks_per_seq, max_len, block_size, nseg, pages,
+                                                               num_heads, pb, ctrl, flags);
+    MEMOPT_LAUNCH_CHECK("move_rows_int4_kernel launch");
+    return MEMOPT_OK;
+  }
   move_rows_inplace_kernel<<<num_seqs * nseg, 32, stage_bytes, s>>>(
       kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
       static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags);
@@ -460,7 +579,7 @@ extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact(
     int32_t* context_lens, void* key_pool, void* value_pool, int pool_num_blocks, int block_size, int head_dim,
     float retain_ratio, int num_sink_tokens, int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages,
     int32_t* freed_count, void* workspace, size_t workspace_bytes, void* stream) {
-  return topk_compact("evict_topk_compact", scores, static_cast<int64_t>(num_heads) * max_len, max_len, num_heads,
+  return topk_compact("evict_topk_compact", false, scores, static_cast<int64_t>(num_heads) * max_len, max_len, num_heads,
                       num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens, key_pool,
                       value_pool, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens, kept_idx,
                       kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
@@ -485,10 +604,21 @@ extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact_
     int block_size, int num_heads, int head_dim, float retain_ratio, int num_sink_tokens, int32_t* kept_idx,
     int32_t* kept_count, int32_t* freed_pages, int32_t* freed_count, void* workspace, size_t workspace_bytes,
     void* stream) {
-  return topk_compact("evict_topk_compact_parts", partial_sums, max_len, static_cast<int64_t>(num_seqs) * max_len,
+  return topk_compact("evict_topk_compact_parts", false, partial_sums, max_len, static_cast<int64_t>(num_seqs) * max_len,
                       num_parts, num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens,
                       key_pool, value_pool, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens,
                       kept_idx, kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
+}
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact_int4(
+    const float* scores, int num_seqs, int num_heads, int max_len, int32_t* block_tables, int max_blocks_per_seq,
+    int32_t* context_lens, uint8_t* kv_pages, int pool_num_blocks, int block_size, int head_dim, float retain_ratio,
+    int num_sink_tokens, int32_t* kept_idx, int32_t* kept_count, int32_t* freed_pages, int32_t* freed_count,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  return topk_compact("evict_topk_compact_int4", true, scores, static_cast<int64_t>(num_heads) * max_len, max_len,
+                      num_heads, num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens, kv_pages,
+                      nullptr, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens, kept_idx,
+                      kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
 }
 
 }  // namespace memopt

@@ -294,7 +294,6 @@ pybind11::tuple evict_topk_compact(torch::Tensor attention_scores, torch::Tensor
                                    torch::Tensor context_lens, float retain_ratio, int num_sink_tokens) {
   TORCH_CHECK(P().live && memopt_pool_is_initialized(), "evict_topk_compact: pool not initialized");
   auto& p = P();
-  TORCH_CHECK(!p.int4, "evict_topk_compact: needs the fp16 pool");
   TORCH_CHECK(attention_scores.dim() == 3 && attention_scores.scalar_type() == torch::kFloat32,
               "evict_topk_compact: attention_scores must be float32 [num_seqs, num_heads, max_len]");
   TORCH_CHECK(block_tables.dim() == 2 && block_tables.scalar_type() == torch::kInt32 && block_tables.is_contiguous(),
@@ -319,12 +318,21 @@ pybind11::tuple evict_topk_compact(torch::Tensor attention_scores, torch::Tensor
   const at::cuda::CUDAGuard g(attention_scores.device());
   const size_t wsb = memopt_evict_topk_workspace_size(S, L, H, p.d);
   auto ws = torch::empty({static_cast<int64_t>(wsb)}, o.dtype(torch::kUInt8));
-  check(memopt_evict_topk_compact(attention_scores.data_ptr<float>(), S, H, L, block_tables.data_ptr<int32_t>(), MB,
-                                  context_lens.data_ptr<int32_t>(), p.k.data_ptr(), p.v.data_ptr(), p.nb, p.bs, p.d,
-                                  retain_ratio, num_sink_tokens, kept.data_ptr<int32_t>(), cnt.data_ptr<int32_t>(),
-                                  freed.data_ptr<int32_t>(), fcnt.data_ptr<int32_t>(), ws.data_ptr(), wsb,
-                                  cur_stream()),
-        "evict_topk_compact");
+  if (p.int4) {
+    check(memopt_evict_topk_compact_int4(attention_scores.data_ptr<float>(), S, H, L, block_tables.data_ptr<int32_t>(),
+                                         MB, context_lens.data_ptr<int32_t>(), p.kvp.data_ptr<uint8_t>(), p.nb, p.bs,
+                                         p.d, retain_ratio, num_sink_tokens, kept.data_ptr<int32_t>(),
+                                         cnt.data_ptr<int32_t>(), freed.data_ptr<int32_t>(), fcnt.data_ptr<int32_t>(),
+                                         ws.data_ptr(), wsb, cur_stream()),
+          "evict_topk_compact");
+  } else {
+    check(memopt_evict_topk_compact(attention_scores.data_ptr<float>(), S, H, L, block_tables.data_ptr<int32_t>(), MB,
+                                    context_lens.data_ptr<int32_t>(), p.k.data_ptr(), p.v.data_ptr(), p.nb, p.bs, p.d,
+                                    retain_ratio, num_sink_tokens, kept.data_ptr<int32_t>(), cnt.data_ptr<int32_t>(),
+                                    freed.data_ptr<int32_t>(), fcnt.data_ptr<int32_t>(), ws.data_ptr(), wsb,
+                                    cur_stream()),
+          "evict_topk_compact");
+  }
   return pybind11::make_tuple(kept, cnt, freed, fcnt);
 }
 

@@ -184,13 +184,24 @@ class PagedKVCache:
         kc, vc = self._C.get_pool_tensors()
         return self._C.dynamic_sparse_attention(q16, kc, vc, bt, ctx, msl, win)
 
+    def _keys(self, pages: torch.Tensor, n: int) -> torch.Tensor:
+        """fp32 keys [n, H, D] of a sequence's first n tokens: the fp16 pool's
+        rows, or the INT4 pool's codes dequantised as the reference does
+        (fp16((c - 8) * scale), quantization.cu:254-268)."""
+        H, D = self.num_heads, self.head_dim
+        if self.kv_format == "fp16":
+            kc, _ = self._C.get_pool_tensors()
+            return kc[pages].reshape(-1, H, D)[:n].float()
+        kcodes, kscale, _, _ = self._C.get_int4_pool_tensors()
+        c = kcodes[pages].transpose(1, 2).reshape(-1, H, D // 2)[:n]  # [n, H, D/2]: byte i = dims 2i, 2i+1
+        codes = torch.stack([c & 15, c >> 4], dim=-1).reshape(n, H, D).float() - 8.0
+        sc = kscale[pages].transpose(1, 2).reshape(-1, H, D // 64)[:n].float().repeat_interleave(64, dim=-1)
+        return (codes * sc).half().float()
+
     def token_scores(self, q: torch.Tensor, sids: Sequence[int]) -> torch.Tensor:
         """Per-token attention weights [B, H, L] of the last query row of ``q``
-        over the cached context (fp16 pool), the eviction signal of Ada-KV.
-        Padding past a sequence's length is 0."""
-        if self.kv_format != "fp16":
-            raise RuntimeError("token_scores: needs the fp16 pool")
-        kc, _ = self._C.get_pool_tensors()
+        over the cached context (fp16 or INT4 pool), the eviction signal of
+        Ada-KV.  Padding past a sequence's length is 0."""
         lens = [self.table.length(s) for s in sids]
         L = max(lens, default=0)
         H, D, bs = self.num_heads, self.head_dim, self.block_size
@@ -201,7 +212,7 @@ class PagedKVCache:
             if n == 0:
                 continue
             pages = torch.tensor(self.table.pages(s), dtype=torch.long, device=self.device)
-            keys = kc[pages].reshape(-1, H, D)[:n].float()  # [n, H, D]
+            keys = self._keys(pages, n)  # [n, H, D]
             logits = torch.einsum("hd,nhd->hn", q[i, -1].float(), keys) * scale
             out[i, :, :n] = torch.softmax(logits, dim=-1)
         return out
@@ -227,8 +238,8 @@ class PagedKVCache:
         ``group`` (a :class:`memopt.sharding.RankGroup`): this cache holds one
         head shard of every sequence and ``scores`` are its heads; the ranks
         exchange partial token scores and take one shared decision."""
-        if self.kv_format != "fp16":
-            raise RuntimeError("evict_exact: works on the fp16 pool")
+        if group is not None and group.world_size > 1 and self.kv_format != "fp16":
+            raise RuntimeError("evict_exact: the head-sharded form works on the fp16 pool")
         bt = self.block_tables(sids).contiguous()
         ctx = self.context_lens(sids).contiguous()
         sc = scores.float().contiguous()
@@ -284,7 +295,7 @@ class PagedKVCache:
     def apply_policy(self, scheduler, q: Optional[torch.Tensor] = None, sids: Optional[Sequence[int]] = None,
                      num_sink_tokens: int = 4) -> Optional[tuple]:
         """Maps a scheduler snapshot onto the cache when it differs from the one
-        last applied: ``retain_ratio < 1`` evicts (fp16 pool, scores from
+        last applied: ``retain_ratio < 1`` evicts (scores from
         ``q``'s last row), then ``use_int4`` converts the pool to INT4.  A
         return to (1.0, fp16) only affects new caches (quantised tokens cannot
         be restored).  Returns the eviction result or None."""
@@ -293,7 +304,7 @@ class PagedKVCache:
             return None
         self._applied = (retain, use_int4)
         result = None
-        if retain < 1.0 and q is not None and sids and self.kv_format == "fp16":
+        if retain < 1.0 and q is not None and sids and (self.kv_format == "fp16" or self.eviction == "exact"):
             scores = self.token_scores(q, sids)
             if self.eviction == "exact":
                 result = self.evict_exact(sids, scores, retain, num_sink_tokens)

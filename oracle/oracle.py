@@ -198,8 +198,33 @@ def evict_topk_compact_parts(parts, block_tables, context_lens, kpool, vpool, re
     """The head-sharded form: parts [G, S, L] are the ranks' partial token
     scores (evict_topk_head_sum of each rank's heads) in rank order; the token
     score is their fp32 sum in rank order.  kpool/vpool hold this rank's heads."""
-    G, S, L = parts.shape
     NB, BS = kpool.shape[0], kpool.shape[1]
+    get = lambda pg, pos: (kpool[pg, pos].copy(), vpool[pg, pos].copy())
+
+    def put(pg, pos, row):
+        kpool[pg, pos], vpool[pg, pos] = row
+
+    return _topk_compact_rows(parts, block_tables, context_lens, NB, BS, get, put, retain_ratio, num_sink_tokens)
+
+
+def evict_topk_compact_int4(scores, block_tables, context_lens, kc, ks, vc, vs, retain_ratio, num_sink_tokens=4):
+    """The same operator on an INT4 pool, in the logical views of int4_views
+    (codes [NB, H, BS, D/2], fp16 scales [NB, H, BS, D/64]; modified in
+    place): a kept token's codes and scales move with it, every head."""
+    NB, BS = kc.shape[0], kc.shape[2]
+    get = lambda pg, pos: (kc[pg, :, pos].copy(), ks[pg, :, pos].copy(), vc[pg, :, pos].copy(), vs[pg, :, pos].copy())
+
+    def put(pg, pos, row):
+        kc[pg, :, pos], ks[pg, :, pos], vc[pg, :, pos], vs[pg, :, pos] = row
+
+    return _topk_compact_rows(evict_topk_head_sum(scores)[None], block_tables, context_lens, NB, BS, get, put,
+                              retain_ratio, num_sink_tokens)
+
+
+def _topk_compact_rows(parts, block_tables, context_lens, NB, BS, get, put, retain_ratio, num_sink_tokens):
+    """Decision and row moves shared by both pool formats: get(page, pos) reads
+    a token row of every head, put(page, pos, row) writes one."""
+    G, S, L = parts.shape
     MB = block_tables.shape[1]
     kept_idx = np.full((S, L), -1, np.int32)
     kept_count = np.zeros(S, np.int32)
@@ -229,8 +254,7 @@ def evict_topk_compact_parts(parts, block_tables, context_lens, kpool, vpool, re
         kept_idx[b, :keep] = kept
         kept_count[b] = keep
         old = row.copy()
-        rows_k = [kpool[old[t // BS], t % BS].copy() for t in kept]
-        rows_v = [vpool[old[t // BS], t % BS].copy() for t in kept]
+        rows = [get(old[t // BS], t % BS) for t in kept]
         need = (keep + BS - 1) // BS
         new_row = np.full(MB, -1, np.int32)
         new_row[:need] = valid_pages[:need]
@@ -239,7 +263,6 @@ def evict_topk_compact_parts(parts, block_tables, context_lens, kpool, vpool, re
         freed_count[b] = len(fl)
         block_tables[b] = new_row
         for i in range(keep):
-            kpool[new_row[i // BS], i % BS] = rows_k[i]
-            vpool[new_row[i // BS], i % BS] = rows_v[i]
+            put(new_row[i // BS], i % BS, rows[i])
         context_lens[b] = keep
     return kept_idx, kept_count, freed, freed_count

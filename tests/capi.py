@@ -140,6 +140,23 @@ def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
     return kept, cnt, freed, fcnt
 
 
+def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain_ratio, sinks):
+    S, H, L = scores.shape
+    MB = bt.shape[1]
+    dev = scores.device
+    kept = torch.empty(S, L, dtype=torch.int32, device=dev)
+    cnt = torch.empty(S, dtype=torch.int32, device=dev)
+    freed = torch.empty(S, MB, dtype=torch.int32, device=dev)
+    fcnt = torch.empty(S, dtype=torch.int32, device=dev)
+    lib().memopt_evict_topk_workspace_size.restype = SZ
+    wsb = int(lib().memopt_evict_topk_workspace_size(I(S), I(L), I(H), I(head_dim)))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    ok(lib().memopt_evict_topk_compact_int4(ptr(scores), I(S), I(H), I(L), ptr(bt), I(MB), ptr(ctx), ptr(pages),
+                                            I(pages.shape[0]), I(block_size), I(head_dim), F(retain_ratio), I(sinks),
+                                            ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt), ptr(ws), SZ(wsb), stream()))
+    return kept, cnt, freed, fcnt
+
+
 def evict_topk_head_sum(scores):
     S, H, L = scores.shape
     out = torch.empty(S, L, dtype=torch.float32, device=scores.device)

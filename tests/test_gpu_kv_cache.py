@@ -110,3 +110,34 @@ def test_exact_eviction_frees_pages_and_keeps_top_tokens():
         torch.testing.assert_close(out[0, 0].float(), ref, atol=2e-3, rtol=1e-2)
     # 200 tokens = 13 pages each -> 100 tokens = 7 pages: 12 pages back in the pool
     assert memopt.memopt_C.free_blocks_count() == free0 + 12
+
+
+def test_exact_eviction_on_the_int4_pool():
+    torch.manual_seed(5)
+    H, D, BS = 2, 128, 16
+    cache = PagedKVCache(40, H, D, BS, kv_format="int4", eviction="exact")
+    sids = [cache.add_sequence(), cache.add_sequence()]
+    k = torch.randn(2, 200, H, D, device=DEV, dtype=torch.float16)
+    v = torch.randn(2, 200, H, D, device=DEV, dtype=torch.float16)
+    cache.append(sids, k, v)
+    q = torch.randn(2, 1, H, D, device=DEV, dtype=torch.float16)
+    before = cache.attend(q, sids)
+    free0 = memopt.memopt_C.free_blocks_count()
+    scores = cache.token_scores(q, sids)  # from the dequantised INT4 keys
+    assert scores.shape == (2, H, 200)
+    torch.testing.assert_close(scores.sum(-1), torch.ones(2, H, device=DEV), atol=1e-4, rtol=0)
+    kept = cache.evict_exact(sids, scores, 0.5, num_sink_tokens=4)
+    assert memopt.memopt_C.free_blocks_count() == free0 + 12
+    after = cache.attend(q, sids)
+    # The compacted cache must attend exactly like a cache that was only ever
+    # given the kept tokens (INT4 codes and scales depend on the token alone).
+    ref_cache_kept = [torch.tensor(kk, device=DEV) for kk in kept]
+    for i, s in enumerate(sids):
+        assert cache.table.length(s) == 100 and kept[i][:4] == [0, 1, 2, 3]
+    fresh = PagedKVCache(40, H, D, BS, kv_format="int4")  # the same process-wide pool: new pages
+    fs = [fresh.add_sequence(), fresh.add_sequence()]
+    fresh.append(fs, torch.stack([k[i, ref_cache_kept[i]] for i in range(2)]),
+                 torch.stack([v[i, ref_cache_kept[i]] for i in range(2)]))
+    torch.testing.assert_close(after, fresh.attend(q, fs), atol=0, rtol=0)
+    assert not torch.equal(before, after)
+

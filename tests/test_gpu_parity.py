@@ -221,6 +221,41 @@ def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
             assert np.array_equal(np16(gv[pg, pos]).view(np.uint16), vp[pg, pos].view(np.uint16))
 
 
+@pytest.mark.parametrize("S,H,L,BS,D,r,sinks,dist,holes", [
+    (2, 4, 1000, 16, 128, 0.5, 4, "lognormal", True),
+    (2, 2, 777, 32, 64, 0.3, 2, "ties", False),
+    (1, 32, 4096, 16, 128, 0.75, 4, "lognormal", False),   # 32 heads: one per lane
+    (1, 40, 600, 16, 128, 0.6, 0, "specials", True),       # 40 heads: lanes take two
+    (1, 2, 20000, 16, 64, 0.05, 0, "normal", False),       # long forward moves
+])
+def test_evict_topk_compact_int4_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
+    """INT4 pool: every kept token's codes and scales (all heads) land at its
+    new position, with the position-dependent V layout re-applied."""
+    sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + 3 * S, dist, holes=holes)
+    rng = np.random.default_rng(L + H)
+    ctx = np.array([L - int(rng.integers(0, min(L, 40))) for _ in range(S)], np.int32)
+    ctx[0] = L
+    NB = kp.shape[0]
+    T = NB * BS
+    pages = torch.zeros(NB, H, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(torch.from_numpy(kp.reshape(T, H, D)).to(DEV), torch.from_numpy(vp.reshape(T, H, D)).to(DEV),
+                          torch.from_numpy(np.arange(T, dtype=np.int32)).to(DEV), pages, BS)
+    views = [np.ascontiguousarray(a) for a in O.int4_views(np16(pages), BS, D)]
+    gbt, gctx = torch.from_numpy(bt).to(DEV), torch.from_numpy(ctx).to(DEV)
+    kept, cnt, freed, fcnt = capi.evict_topk_compact_int4(torch.from_numpy(sc).to(DEV), gbt, gctx, pages, BS, D, r, sinks)
+    rbt, rctx = bt.copy(), ctx.copy()
+    rk, rc, rf, rfc = O.evict_topk_compact_int4(sc, rbt, rctx, *views, r, sinks)
+    assert np.array_equal(np16(cnt), rc) and np.array_equal(np16(kept), rk)
+    assert np.array_equal(np16(fcnt), rfc) and np.array_equal(np16(freed), rf)
+    assert np.array_equal(np16(gbt), rbt) and np.array_equal(np16(gctx), rctx)
+    got = O.int4_views(np16(pages), BS, D)
+    for b in range(S):
+        for i in range(int(rc[b])):
+            pg, pos = rbt[b, i // BS], i % BS
+            for a, ref in zip(got, views):
+                assert np.array_equal(a[pg, :, pos].view(np.uint8), ref[pg, :, pos].view(np.uint8))
+
+
 @pytest.mark.parametrize("S,H,G,L,BS,D,r,sinks,dist,holes", [
     (2, 4, 2, 512, 16, 64, 0.75, 4, "lognormal", False),
     (3, 4, 4, 1000, 16, 128, 0.5, 0, "normal", True),
