@@ -566,6 +566,33 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
     ms_topk = max_over_ranks(statistics.median(topk_ms))
     kept_rows = int(kcnt.sum().item())
     topk_bytes = eb * H * ectx * 4 + 2 * 2 * kept_rows * H * D * 2  # scores + K/V rows read and written once
+    # The same eviction on an INT4 pool of the same sequences (seeded random
+    # codes and scales): each kept token moves 2 x D/2 code bytes and
+    # 2 x D/64 fp16 scales per head.
+    q4_ms = []
+    memopt_C.init_pool(nb, BS, H, D, kv_format="int4")
+    pages4 = memopt_C.get_int4_pages()
+    pages4.random_(0, 256, generator=g)
+    pages4[:, :, BS * D:].view(torch.float16).uniform_(0.05, 0.55, generator=g)
+    for it in range(4):
+        bt_c = bt.clone()
+        ctx_c = torch.full((eb,), ectx, dtype=torch.int32, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        _, kcnt4, _, _ = memopt_C.evict_topk_compact(scores, bt_c, ctx_c, 0.75, 4)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if it > 0:
+            q4_ms.append(e0.elapsed_time(e1))
+    ms_topk4 = max_over_ranks(statistics.median(q4_ms))
+    topk4_bytes = eb * H * ectx * 4 + 2 * int(kcnt4.sum().item()) * H * (D + 4 * (D // 64))
+    del pages4
+    memopt_C.init_pool(nb, BS, H, D)
+    kp, vp = memopt_C.get_pool_tensors()
+    kp.normal_(generator=g)
+    vp.normal_(generator=g)
     q = torch.randn(eb, 1, H, D, dtype=torch.float16, device=dev, generator=g)
     ctx = torch.full((eb,), ectx, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
@@ -590,6 +617,12 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
                                    "ms_per_call": round(ms_topk, 4), "kept_rows": kept_rows,
                                    "note": "median of 3 calls after an untimed one; kept rows move in place (each "
                                            "read and written once)"},
+            "evict_topk_compact_int4": {"workload": "the same eviction on an INT4 pool of the same 8 x 32768 tokens "
+                                                    "(32 heads x 128, seeded random codes and scales)",
+                                        "value": round(topk4_bytes * ws_n / (ms_topk4 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                        "ms_per_call": round(ms_topk4, 4),
+                                        "note": "median of 3 calls after an untimed one; each kept token's codes "
+                                                "and scales read and written once"},
             "window_decode": {"workload": "BASELINE configs[3]: decode batch 8, ctx 32768, window 4096",
                               "value": round(dbytes * ws_n / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                               "ms_per_step": round(ms, 5),

@@ -276,25 +276,35 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
   }
 }
 
-// In-place move of the kept rows, kSegRows rows per CTA (one thread issues
-// bulk copies).  Segments are handed out in order by a ticket counter, so
-// every lower segment of the same sequence is already resident or finished
-// when a segment waits on it.  A segment bulk-loads its moving rows (K and V)
+// In-place move of the kept rows, kSegRows rows per warp and kMoveWarps16
+// warps per CTA (lane 0 of each warp issues its bulk copies).  CTAs take
+// their consecutive segments in order from a ticket counter, so every lower
+// segment of the same sequence is held by a warp of the same CTA or of an
+// earlier ticket, resident or finished, when a segment waits on it.  A segment bulk-loads its moving rows (K and V)
 // into shared memory, publishes "read" in flags[ticket], waits until the
 // (at most two) segments whose rows read its destination slots have
 // published, then bulk-stores its rows.  Reads never wait, so every wait
 // ends; each is still bounded, recording 1 in ctrl[1] if it gives up.
 // Rows whose source is already their destination are not touched.
-__global__ void __launch_bounds__(32) move_rows_inplace_kernel(
+constexpr int kMoveWarps16 = 4;  // fp16 move: segments (warps) per CTA, one ticket per CTA
+
+__global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
     const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ src_ord,
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
-    int nseg, uint8_t* __restrict__ kpool, uint8_t* __restrict__ vpool, uint32_t row_bytes, int* ctrl,
-    int* flags) {
-  if (threadIdx.x != 0) return;
-  extern __shared__ __align__(128) uint8_t stage[];
-  __shared__ __align__(8) uint64_t bar;
-  const int ticket = atomicAdd(&ctrl[0], 1);
+    int nseg, int total_segs, uint8_t* __restrict__ kpool, uint8_t* __restrict__ vpool, uint32_t row_bytes,
+    int* ctrl, int* flags) {
+  __shared__ int cta_ticket;
+  if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
+  __syncthreads();
+  if ((threadIdx.x & 31) != 0) return;
+  const int w = threadIdx.x >> 5;
+  extern __shared__ __align__(128) uint8_t stage_all[];
+  __shared__ __align__(8) uint64_t bars[kMoveWarps16];
+  uint8_t* stage = stage_all + static_cast<size_t>(w) * 2 * kSegRows * row_bytes;
+  uint64_t& bar = bars[w];
+  const int ticket = cta_ticket * kMoveWarps16 + w;  // this warp's segment, in ticket order
+  if (ticket >= total_segs) return;
   const int b = ticket / nseg, k = ticket % nseg;
   const int cnt = kept_count[b];
   const int r0 = k * kSegRows;
@@ -370,21 +380,35 @@ __global__ void __launch_bounds__(32) move_rows_inplace_kernel(
 // (16-byte chunks exchanged in pairs on rows whose position has bit 1 set, at
 // D = 128), the K scales and the V scales (slots permuted per 16-token tile),
 // so the position-dependent parts are re-laid out for the destination.  One
-// warp per row, lane h moving heads h and h + 32 (KVH <= 64) through
-// registers; the read flag is published after the warp's loads completed.
+// warp per row, kMoveWarps consecutive rows per CTA taken with one ticket: a
+// row only waits for lower rows, held by warps of its own CTA or of a CTA that
+// took an earlier ticket, all resident or finished.  The code rows go through
+// shared memory by cp.async (four lanes per 64-byte row, so a warp
+// instruction reads whole rows of several heads), the scales through
+// registers; the read flag is published after the warp's copies landed.
+constexpr int kMoveWarps = 8;  // rows (warps) per CTA of the INT4 move, one ticket per CTA
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
 template <int D>
-__global__ void __launch_bounds__(32) move_rows_int4_kernel(
+__global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ src_ord,
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
-    int nseg, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags) {
+    int nseg, int total_rows, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags) {
   constexpr int G = D / 64;
-  constexpr int CB = D / 2;     // code row bytes
-  constexpr int NCH = CB / 16;  // 16-byte chunks per code row
-  const int lane = threadIdx.x;
-  int ticket = 0;
-  if (lane == 0) ticket = atomicAdd(&ctrl[0], 1);
-  ticket = __shfl_sync(0xffffffffu, ticket, 0);
+  constexpr int CB = D / 2;       // code row bytes
+  constexpr int LPR = CB / 16;    // lanes per code row (16 bytes each)
+  constexpr int HPI = 32 / LPR;   // heads per warp instruction
+  extern __shared__ __align__(16) uint8_t stage_all[];  // per warp: KVH x (K row, V row) code bytes
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  __shared__ int cta_ticket;
+  if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
+  __syncthreads();
+  const int ticket = cta_ticket * kMoveWarps + w;  // this warp's row, in ticket order
+  if (ticket >= total_rows) return;
   const int b = ticket / nseg, row = ticket % nseg;  // one row per segment
   if (row >= kept_count[b]) return;
   const int64_t rb = static_cast<int64_t>(b) * max_len;
@@ -397,20 +421,23 @@ __global__ void __launch_bounds__(32) move_rows_int4_kernel(
   const int sp = old_bt[static_cast<int64_t>(b) * MB + t / BS], spos = t % BS;
   const int dp = new_bt[static_cast<int64_t>(b) * MB + row / BS], dpos = row % BS;
   const int sswap = (D == 128 && (spos & 2)) ? 2 : 0, dswap = (D == 128 && (dpos & 2)) ? 2 : 0;
-  uint4 kc[2][NCH], vc[2][NCH];
+  uint8_t* stage = stage_all + static_cast<size_t>(w) * KVH * 2 * CB;
+  const uint32_t sst = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+  // Lane -> (head hs of each group of HPI heads, 16-byte chunk c of its rows):
+  // a warp instruction covers HPI whole code rows (coalesced 64-byte runs).
+  const int hs = lane / LPR, c = lane % LPR;
+  for (int h = hs; h < KVH; h += HPI) {
+    const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
+    cp_async16(sst + (2 * h) * CB + 16 * c, pg + spos * CB + 16 * c);
+    cp_async16(sst + (2 * h + 1) * CB + 16 * c, pg + BS * CB + spos * CB + 16 * (c ^ sswap));  // logical chunk c
+  }
+  // Scales (2 G halves per head) through registers: lane h, h + 32.
   uint16_t ks[2][G], vs[2][G];
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
     const int h = lane + 32 * hi;
     if (h >= KVH) continue;
     const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
-    const uint4* kr = reinterpret_cast<const uint4*>(pg + spos * CB);
-    const uint4* vr = reinterpret_cast<const uint4*>(pg + BS * CB + spos * CB);
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      kc[hi][c] = kr[c];
-      vc[hi][c] = vr[c ^ sswap];  // logical chunk c
-    }
     const uint16_t* ksp = reinterpret_cast<const uint16_t*>(pg + BS * D) + spos * G;
     const uint16_t* vsp = reinterpret_cast<const uint16_t*>(pg + BS * D + BS * G * 2);
 #pragma unroll
@@ -419,6 +446,7 @@ __global__ void __launch_bounds__(32) move_rows_int4_kernel(
       vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
   if (lane == 0) {
     __threadfence();
@@ -441,18 +469,18 @@ __global__ void __launch_bounds__(32) move_rows_int4_kernel(
     }
   }
   __syncwarp();
+  for (int h = hs; h < KVH; h += HPI) {
+    uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
+    const uint4 kv = *reinterpret_cast<const uint4*>(stage + (2 * h) * CB + 16 * c);
+    const uint4 vv = *reinterpret_cast<const uint4*>(stage + (2 * h + 1) * CB + 16 * c);
+    *reinterpret_cast<uint4*>(pg + dpos * CB + 16 * c) = kv;
+    *reinterpret_cast<uint4*>(pg + BS * CB + dpos * CB + 16 * (c ^ dswap)) = vv;
+  }
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
     const int h = lane + 32 * hi;
     if (h >= KVH) continue;
     uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
-    uint4* kr = reinterpret_cast<uint4*>(pg + dpos * CB);
-    uint4* vr = reinterpret_cast<uint4*>(pg + BS * CB + dpos * CB);
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      kr[c] = kc[hi][c];
-      vr[c ^ dswap] = vc[hi][c];
-    }
     uint16_t* ksp = reinterpret_cast<uint16_t*>(pg + BS * D) + dpos * G;
     uint16_t* vsp = reinterpret_cast<uint16_t*>(pg + BS * D + BS * G * 2);
 #pragma unroll
@@ -523,10 +551,10 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
   if (workspace_bytes < need) return fail(MEMOPT_ERR_WORKSPACE, std::string(who) + ": workspace too small");
   cudaStream_t s = as_stream(stream);
   const uint32_t row_bytes = static_cast<uint32_t>(num_heads) * head_dim * 2;
-  const size_t stage_bytes = static_cast<size_t>(2 * kSegRows) * row_bytes;
+  const size_t stage_bytes = static_cast<size_t>(2 * kSegRows) * row_bytes * kMoveWarps16;
   if (!int4 && stage_bytes > static_cast<size_t>(kMoveSmemLimit))
     return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim above " +
-                                             std::to_string(kMoveSmemLimit / (4 * kSegRows)));
+                                             std::to_string(kMoveSmemLimit / (4 * kSegRows * kMoveWarps16)));
   cudaError_t ea = cudaFuncSetAttribute(move_rows_inplace_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         kMoveSmemLimit);
   if (ea != cudaSuccess) return cuda_fail(ea, "evict_topk: shared-memory attribute");
@@ -555,19 +583,28 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
   if (int4) {
     const int64_t pb = static_cast<int64_t>(block_size) * head_dim + static_cast<int64_t>(block_size) * (head_dim / 64) * 4;
     uint8_t* pages = static_cast<uint8_t*>(key_pool);
+    const int rows_total = num_seqs * nseg;
+    const int grid4 = (rows_total + kMoveWarps - 1) / kMoveWarps;
+    const size_t smem4 = static_cast<size_t>(kMoveWarps) * num_heads * head_dim;  // 2 code rows of D/2 per head
+    cudaError_t ea4 = head_dim == 128 ? cudaFuncSetAttribute(move_rows_int4_kernel<128>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024)
+                                      : cudaFuncSetAttribute(move_rows_int4_kernel<64>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (ea4 != cudaSuccess) return cuda_fail(ea4, "evict_topk_int4: shared-memory attribute");
     if (head_dim == 128)
-      move_rows_int4_kernel<128><<<num_seqs * nseg, 32, 0, s>>>(kept_idx, ord, kept_count, dep, old_bt, block_tables,
-                                                                max_blocks_per_seq, max_len, block_size, nseg, pages,
-                                                                num_heads, pb, ctrl, flags);
+      move_rows_int4_kernel<128><<<grid4, 32 * kMoveWarps, smem4, s>>>(
+          kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
+          rows_total, pages, num_heads, pb, ctrl, flags);
     else
-      move_rows_int4_kernel<64><<<num_seqs * nseg, 32, 0, s>>>(kept_idx, ord, kept_count, dep, old_bt, block_tables,
-                                                               max_blocks_per_seq, max_len, block_size, nseg, pages,
-                                                               num_heads, pb, ctrl, flags);
+      move_rows_int4_kernel<64><<<grid4, 32 * kMoveWarps, smem4, s>>>(
+          kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
+          rows_total, pages, num_heads, pb, ctrl, flags);
     MEMOPT_LAUNCH_CHECK("move_rows_int4_kernel launch");
     return MEMOPT_OK;
   }
-  move_rows_inplace_kernel<<<num_seqs * nseg, 32, stage_bytes, s>>>(
-      kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
+  const int segs = num_seqs * nseg;
+  move_rows_inplace_kernel<<<(segs + kMoveWarps16 - 1) / kMoveWarps16, 32 * kMoveWarps16, stage_bytes, s>>>(
+      kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg, segs,
       static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags);
   MEMOPT_LAUNCH_CHECK("move_rows_inplace_kernel launch");
   return MEMOPT_OK;
