@@ -164,11 +164,12 @@ int memopt_evict_tokens(const float* scores, int num_seqs, int num_heads, int se
 /* scores fp32 [num_seqs, num_heads, max_len]; kept_idx int32 [num_seqs,      */
 /* max_len] (ascending original indices, -1 pad); kept_count int32            */
 /* [num_seqs]; freed_pages int32 [num_seqs, max_blocks_per_seq]; freed_count  */
-/* int32 [num_seqs].  max_len <= 32768, max_blocks_per_seq <= 2048; fp16      */
+/* int32 [num_seqs].  max_blocks_per_seq <= 16384 and <= max(2048, max_len)  */
+/* (sequences beyond 32768 tokens or 2048 pages use a streaming select); fp16 */
 /* pools in reference layout; a physical page appears at most once in the   */
 /* tables.  Rows move in place.  The workspace (16-byte aligned,               */
-/* memopt_evict_topk_workspace_size() bytes: about 16 B per token plus 8 B    */
-/* per 4 tokens, no K/V rows) holds tables, ordinals and move flags.          */
+/* memopt_evict_topk_workspace_size() bytes: about 20 B per token, no K/V    */
+/* rows) holds tables, ordinals and move flags.                                */
 /* ------------------------------------------------------------------------ */
 size_t memopt_evict_topk_workspace_size(int num_seqs, int max_len, int num_heads, int head_dim);
 int memopt_evict_topk_compact(const float* scores, int num_seqs, int num_heads, int max_len,

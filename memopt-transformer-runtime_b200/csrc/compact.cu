@@ -45,7 +45,7 @@ constexpr int kVPT = kMaxLen / kSelThreads;  // 32 tokens per thread
 // (retain 0.75) one row per CTA moved the rows in 1.17 ms, 2 in 1.19 ms,
 // 4 in 1.29 ms and 8 in 1.73 ms: small CTAs keep more copies in flight.
 constexpr int kSegRows = 1;
-constexpr int kMaxSegs = kMaxLen / kSegRows;
+constexpr int kMaxPagesBig = 16 * kSelThreads;   // streaming select: up to 16 table entries per thread
 constexpr int kMoveSmemLimit = 200 * 1024;       // 2 * kSegRows rows staged in shared memory
 
 // sums[b, t] = fp32 sum over i in order of src[b * b_stride + i * i_stride + t].
@@ -98,7 +98,7 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
                    int32_t* __restrict__ ctx_lens, int NB, int BS, float retain_ratio, int num_sinks,
                    int32_t* __restrict__ kept_idx, int32_t* __restrict__ kept_count,
                    int32_t* __restrict__ freed, int32_t* __restrict__ freed_count,
-                   int32_t* __restrict__ src_ord, int32_t* __restrict__ seg_dep) {
+                   int32_t* __restrict__ src_ord, int32_t* __restrict__ seg_dep, int seg_stride) {
   __shared__ int hist[256];
   __shared__ int warp_sums[32];
   __shared__ int page_rank[2 * kSelThreads];  // rank of each valid page among the row's valid pages
@@ -230,7 +230,7 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
     }
   }
   const int nseg = (total + kSegRows - 1) / kSegRows;
-  int32_t* dep = seg_dep + static_cast<int64_t>(b) * kMaxSegs;
+  int32_t* dep = seg_dep + static_cast<int64_t>(b) * seg_stride;
   for (int k = tid; k < nseg; k += kSelThreads) dep[k] = INT_MAX;
   __syncthreads();
 
@@ -276,6 +276,179 @@ topk_select_kernel(const float* __restrict__ sums, int max_len, int32_t* __restr
   }
 }
 
+// The same selection for long sequences (max_len > 32768 or more than 2048
+// table entries): keys are recomputed from the token sums (L2-resident) in
+// every pass instead of being held in registers, each thread owns a
+// contiguous chunk of tokens (so block scans give token order), and the page
+// ranks live in dynamic shared memory.  Same outputs as topk_select_kernel.
+__global__ void __launch_bounds__(kSelThreads, 1)
+topk_select_big_kernel(const float* __restrict__ sums, int max_len, int32_t* __restrict__ bt, int MB,
+                       int32_t* __restrict__ ctx_lens, int NB, int BS, float retain_ratio, int num_sinks,
+                       int32_t* __restrict__ kept_idx, int32_t* __restrict__ kept_count,
+                       int32_t* __restrict__ freed, int32_t* __restrict__ freed_count,
+                       int32_t* __restrict__ src_ord, int32_t* __restrict__ seg_dep, int seg_stride) {
+  extern __shared__ int page_rank[];  // [MB]: rank among the row's valid pages, -1 if invalid
+  __shared__ int hist[256];
+  __shared__ int warp_sums[32];
+  __shared__ uint32_t sh_prefix;
+  __shared__ int sh_remaining;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  int32_t* btrow = bt + static_cast<int64_t>(b) * MB;
+  const int L = min(max(ctx_lens[b], 0), max_len);
+  const float* srow = sums + static_cast<int64_t>(b) * max_len;
+
+  // Page ranks: thread tid owns table entries [tid * PPT, tid * PPT + PPT).
+  const int PPT = (MB + kSelThreads - 1) / kSelThreads;  // <= 16
+  int pg[16];
+  int pvalid = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int lb = tid * PPT + k;
+    pg[k] = (k < PPT && lb < MB) ? btrow[lb] : -1;
+    if (pg[k] >= 0 && pg[k] < NB) ++pvalid;
+  }
+  int nvp = 0;
+  const int vrank0 = block_excl_scan(pvalid, warp_sums, &nvp);
+  {
+    int v = vrank0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int lb = tid * PPT + k;
+      if (k < PPT && lb < MB) page_rank[lb] = (pg[k] >= 0 && pg[k] < NB) ? v++ : -1;
+    }
+  }
+  __syncthreads();
+
+  // Key of token t (< L): 0 = not a candidate (NaN keys are 0 too, as below).
+  const int CH = (L + kSelThreads - 1) / kSelThreads;
+  const int t_lo = min(tid * CH, L), t_hi = min(t_lo + CH, L);
+  auto valid_tok = [&](int t) { return page_rank[t / BS] >= 0; };  // t < L <= max_len, t / BS < MB checked below
+  auto key_of = [&](int t) -> uint32_t { return t < num_sinks ? 0xFFFFFFFFu : score_key(srow[t]); };
+  const bool tbl_ok = (L + BS - 1) / BS <= MB;  // tokens on entries past the table are never valid
+  auto in_table = [&](int t) { return tbl_ok || t / BS < MB; };
+
+  int nv_thread = 0;
+  for (int t = t_lo; t < t_hi; ++t) nv_thread += (in_table(t) && valid_tok(t)) ? 1 : 0;
+  int nvalid = 0;
+  block_excl_scan(nv_thread, warp_sums, &nvalid);
+  const int keep = nvalid == 0 ? 0 : max(1, min(nvalid, static_cast<int>(ceilf(retain_ratio * static_cast<float>(nvalid)))));
+
+  if (tid == 0) {
+    sh_prefix = 0u;
+    sh_remaining = keep;
+  }
+  uint32_t prefix_mask = 0u;
+  for (int pass = 0; pass < 4 && keep > 0; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = sh_prefix;
+    for (int t = t_lo; t < t_hi; ++t) {
+      if (!(in_table(t) && valid_tok(t))) continue;
+      const uint32_t k = key_of(t);
+      if ((k & prefix_mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const int rem = sh_remaining;
+      int c[8];
+      int part = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        c[k] = hist[255 - (tid * 8 + k)];
+        part += c[k];
+      }
+      int incl = part;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += n;
+      }
+      int above = incl - part;
+      int found_digit = -1, found_above = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (found_digit < 0 && above + c[k] >= rem) {
+          found_digit = 255 - (tid * 8 + k);
+          found_above = above;
+        }
+        above += c[k];
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, found_digit >= 0);
+      const int src = __ffs(m) - 1;
+      const int dig = __shfl_sync(0xffffffffu, found_digit, src);
+      const int abv = __shfl_sync(0xffffffffu, found_above, src);
+      if (tid == 0) {
+        sh_prefix = prefix | (static_cast<uint32_t>(dig) << shift);
+        sh_remaining = rem - abv;
+      }
+    }
+    prefix_mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  const uint32_t T = sh_prefix;
+  const int need_eq = sh_remaining;
+
+  int eq_thread = 0;
+  for (int t = t_lo; t < t_hi; ++t)
+    if (in_table(t) && valid_tok(t) && key_of(t) == T) ++eq_thread;
+  const int eq_before = block_excl_scan(eq_thread, warp_sums, nullptr);
+  auto kept_tok = [&](int t, int& eq_rank) -> bool {
+    if (keep == 0 || !(in_table(t) && valid_tok(t))) return false;
+    const uint32_t k = key_of(t);
+    if (k > T) return true;
+    if (k == T) return eq_rank++ < need_eq;
+    return false;
+  };
+  int kept_thread = 0;
+  {
+    int er = eq_before;
+    for (int t = t_lo; t < t_hi; ++t) kept_thread += kept_tok(t, er) ? 1 : 0;
+  }
+  int total = 0;
+  int pos = block_excl_scan(kept_thread, warp_sums, &total);
+
+  const int nseg = (total + kSegRows - 1) / kSegRows;
+  int32_t* dep = seg_dep + static_cast<int64_t>(b) * seg_stride;
+  for (int k = tid; k < nseg; k += kSelThreads) dep[k] = INT_MAX;
+  __syncthreads();
+  int32_t* kout = kept_idx + static_cast<int64_t>(b) * max_len;
+  int32_t* oout = src_ord + static_cast<int64_t>(b) * max_len;
+  {
+    int er = eq_before;
+    for (int t = t_lo; t < t_hi; ++t) {
+      if (!kept_tok(t, er)) continue;
+      const int so = page_rank[t / BS] * BS + t % BS;
+      kout[pos] = t;
+      oout[pos] = so;
+      if (so / kSegRows != pos / kSegRows) atomicMin(&dep[so / kSegRows], pos / kSegRows);
+      ++pos;
+    }
+  }
+  for (int t = total + tid; t < max_len; t += kSelThreads) kout[t] = -1;
+
+  const int need_pages = (total + BS - 1) / BS;
+  int32_t* frow = freed + static_cast<int64_t>(b) * MB;
+  __syncthreads();  // every table entry was read (pg[]) before any is rewritten
+  for (int lb = tid; lb < MB; lb += kSelThreads) btrow[lb] = -1;
+  for (int lb = tid; lb < MB; lb += kSelThreads) frow[lb] = -1;
+  __syncthreads();
+  int vrank = vrank0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (k < PPT && pg[k] >= 0 && pg[k] < NB) {
+      if (vrank < need_pages) btrow[vrank] = pg[k];
+      else frow[vrank - need_pages] = pg[k];
+      ++vrank;
+    }
+  }
+  if (tid == 0) {
+    kept_count[b] = total;
+    freed_count[b] = max(0, nvp - need_pages);
+    ctx_lens[b] = total;
+  }
+}
+
 // In-place move of the kept rows, kSegRows rows per warp and kMoveWarps16
 // warps per CTA (lane 0 of each warp issues its bulk copies).  CTAs take
 // their consecutive segments in order from a ticket counter, so every lower
@@ -293,7 +466,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
     int nseg, int total_segs, uint8_t* __restrict__ kpool, uint8_t* __restrict__ vpool, uint32_t row_bytes,
-    int* ctrl, int* flags) {
+    int* ctrl, int* flags, int seg_stride) {
   __shared__ int cta_ticket;
   if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
   __syncthreads();
@@ -344,11 +517,11 @@ __global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
       }
     }
   }
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flags + static_cast<int64_t>(b) * kMaxSegs + k), "r"(1) : "memory");
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flags + static_cast<int64_t>(b) * seg_stride + k), "r"(1) : "memory");
   if (!moving) return;
-  const int d = seg_dep[static_cast<int64_t>(b) * kMaxSegs + k];
+  const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + k];
   for (int m = d; m < k && m <= d + 1; ++m) {
-    const int* f = flags + static_cast<int64_t>(b) * kMaxSegs + m;
+    const int* f = flags + static_cast<int64_t>(b) * seg_stride + m;
     uint32_t polls = 0;
     int v = 0;
     while (true) {
@@ -397,7 +570,8 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     const int32_t* __restrict__ kept_idx, const int32_t* __restrict__ src_ord,
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
-    int nseg, int total_rows, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags) {
+    int nseg, int total_rows, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags,
+    int seg_stride) {
   constexpr int G = D / 64;
   constexpr int CB = D / 2;       // code row bytes
   constexpr int LPR = CB / 16;    // lanes per code row (16 bytes each)
@@ -412,7 +586,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   const int b = ticket / nseg, row = ticket % nseg;  // one row per segment
   if (row >= kept_count[b]) return;
   const int64_t rb = static_cast<int64_t>(b) * max_len;
-  int* my_flag = flags + static_cast<int64_t>(b) * kMaxSegs + row;
+  int* my_flag = flags + static_cast<int64_t>(b) * seg_stride + row;
   if (src_ord[rb + row] == row) {  // already in place
     if (lane == 0) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
     return;
@@ -452,9 +626,9 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     __threadfence();
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
     // Wait until the row that lives at this row's destination has been read.
-    const int d = seg_dep[static_cast<int64_t>(b) * kMaxSegs + row];
+    const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + row];
     for (int m = d; m < row && m <= d + 1; ++m) {
-      const int* f = flags + static_cast<int64_t>(b) * kMaxSegs + m;
+      const int* f = flags + static_cast<int64_t>(b) * seg_stride + m;
       uint32_t polls = 0;
       int v = 0;
       while (true) {
@@ -499,15 +673,16 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
 static size_t topk_ws_layout(int num_seqs, int max_len, size_t* off_sums, size_t* off_ord, size_t* off_dep,
                              size_t* off_flags, size_t* off_ctrl) {
   const size_t S = static_cast<size_t>(num_seqs);
-  size_t o = S * 2 * kSelThreads * 4;  // old block-table copy (max_blocks_per_seq <= 2048)
+  const size_t bt_cap = static_cast<size_t>(max_len > 2 * kSelThreads ? max_len : 2 * kSelThreads);
+  size_t o = S * bt_cap * 4;  // old block-table copy (max_blocks_per_seq <= max(2048, max_len))
   *off_sums = o;
   o += S * max_len * 4;
   *off_ord = o;
   o += S * max_len * 4;
   *off_dep = o;
-  o += S * kMaxSegs * 4;
+  o += S * max_len * 4;  // one dependency and one flag per kept row (kSegRows == 1)
   *off_flags = o;
-  o += S * kMaxSegs * 4;
+  o += S * max_len * 4;
   *off_ctrl = o;
   return o + 256;
 }
@@ -531,9 +706,10 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
   if (n_terms <= 0 || num_seqs < 0 || num_heads <= 0 || max_len < 0 || max_blocks_per_seq < 0 || pool_num_blocks < 0 ||
       block_size <= 0 || head_dim <= 0)
     return fail(MEMOPT_ERR_INVALID_ARG, std::string(who) + ": invalid geometry");
-  if (max_len > kMaxLen) return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": max_len exceeds 32768");
-  if (max_blocks_per_seq > 2 * kSelThreads)
-    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": more than 2048 blocks per sequence");
+  if (max_blocks_per_seq > kMaxPagesBig)
+    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": more than 16384 blocks per sequence");
+  if (max_blocks_per_seq > 2 * kSelThreads && max_blocks_per_seq > max_len)
+    return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": more than max(2048, max_len) blocks per sequence");
   if (!int4 && (num_heads * head_dim) % 8 != 0)
     return fail(MEMOPT_ERR_UNSUPPORTED, std::string(who) + ": num_heads * head_dim must be a multiple of 8");
   if (int4 && !((head_dim == 64 || head_dim == 128) && block_size % 16 == 0 && num_heads <= 64))
@@ -570,15 +746,27 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
   const size_t bt_bytes = static_cast<size_t>(num_seqs) * max_blocks_per_seq * 4;
   cudaError_t e = cudaMemcpyAsync(old_bt, block_tables, bt_bytes, cudaMemcpyDeviceToDevice, s);
   if (e != cudaSuccess) return cuda_fail(e, (std::string(who) + ": block-table copy").c_str());
-  e = cudaMemsetAsync(flags, 0, static_cast<size_t>(num_seqs) * kMaxSegs * 4 + 256, s);
+  e = cudaMemsetAsync(flags, 0, static_cast<size_t>(num_seqs) * max_len * 4 + 256, s);
   if (e != cudaSuccess) return cuda_fail(e, (std::string(who) + ": clearing flags").c_str());
   head_sum_kernel<<<dim3((max_len + 255) / 256, num_seqs), 256, 0, s>>>(src, b_stride, i_stride, n_terms, max_len, sums);
   MEMOPT_LAUNCH_CHECK("head_sum_kernel launch");
   const int sinks = num_sink_tokens < 0 ? 0 : num_sink_tokens;
-  topk_select_kernel<<<num_seqs, kSelThreads, 0, s>>>(sums, max_len, block_tables, max_blocks_per_seq, context_lens,
-                                                      pool_num_blocks, block_size, retain_ratio, sinks, kept_idx,
-                                                      kept_count, freed_pages, freed_count, ord, dep);
-  MEMOPT_LAUNCH_CHECK("topk_select_kernel launch");
+  if (max_len <= kMaxLen && max_blocks_per_seq <= 2 * kSelThreads) {
+    topk_select_kernel<<<num_seqs, kSelThreads, 0, s>>>(sums, max_len, block_tables, max_blocks_per_seq,
+                                                        context_lens, pool_num_blocks, block_size, retain_ratio, sinks,
+                                                        kept_idx, kept_count, freed_pages, freed_count, ord, dep,
+                                                        max_len);
+    MEMOPT_LAUNCH_CHECK("topk_select_kernel launch");
+  } else {
+    const size_t psm = static_cast<size_t>(max_blocks_per_seq) * 4;
+    cudaError_t eb = cudaFuncSetAttribute(topk_select_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kMaxPagesBig * 4);
+    if (eb != cudaSuccess) return cuda_fail(eb, "evict_topk: shared-memory attribute (select)");
+    topk_select_big_kernel<<<num_seqs, kSelThreads, psm, s>>>(
+        sums, max_len, block_tables, max_blocks_per_seq, context_lens, pool_num_blocks, block_size, retain_ratio, sinks,
+        kept_idx, kept_count, freed_pages, freed_count, ord, dep, max_len);
+    MEMOPT_LAUNCH_CHECK("topk_select_big_kernel launch");
+  }
   const int nseg = (max_len + kSegRows - 1) / kSegRows;
   if (int4) {
     const int64_t pb = static_cast<int64_t>(block_size) * head_dim + static_cast<int64_t>(block_size) * (head_dim / 64) * 4;
@@ -594,18 +782,18 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
     if (head_dim == 128)
       move_rows_int4_kernel<128><<<grid4, 32 * kMoveWarps, smem4, s>>>(
           kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
-          rows_total, pages, num_heads, pb, ctrl, flags);
+          rows_total, pages, num_heads, pb, ctrl, flags, max_len);
     else
       move_rows_int4_kernel<64><<<grid4, 32 * kMoveWarps, smem4, s>>>(
           kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
-          rows_total, pages, num_heads, pb, ctrl, flags);
+          rows_total, pages, num_heads, pb, ctrl, flags, max_len);
     MEMOPT_LAUNCH_CHECK("move_rows_int4_kernel launch");
     return MEMOPT_OK;
   }
   const int segs = num_seqs * nseg;
   move_rows_inplace_kernel<<<(segs + kMoveWarps16 - 1) / kMoveWarps16, 32 * kMoveWarps16, stage_bytes, s>>>(
       kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg, segs,
-      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags);
+      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags, max_len);
   MEMOPT_LAUNCH_CHECK("move_rows_inplace_kernel launch");
   return MEMOPT_OK;
 }

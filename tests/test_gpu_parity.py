@@ -197,6 +197,9 @@ def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     (2, 2, 16384, 16, 64, 0.6, 0, "ties", True),
     (2, 32, 4096, 16, 128, 0.75, 4, "lognormal", True),  # 8 KB rows, the bench's geometry
     (1, 4, 20000, 16, 64, 0.05, 0, "normal", False),     # long forward moves
+    (2, 2, 70000, 16, 64, 0.75, 4, "lognormal", True),   # streaming select: > 32768 tokens, > 2048 pages
+    (1, 2, 40000, 32, 64, 0.5, 3, "ties", False),        # > 32768 tokens, 1250 pages
+    (1, 2, 50000, 16, 64, 0.6, 0, "specials", True),
 ])
 def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + 7 * S, dist, holes=holes)
@@ -227,6 +230,7 @@ def test_evict_topk_compact_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     (1, 32, 4096, 16, 128, 0.75, 4, "lognormal", False),   # 32 heads: one per lane
     (1, 40, 600, 16, 128, 0.6, 0, "specials", True),       # 40 heads: lanes take two
     (1, 2, 20000, 16, 64, 0.05, 0, "normal", False),       # long forward moves
+    (1, 4, 66000, 16, 128, 0.75, 4, "lognormal", True),    # streaming select
 ])
 def test_evict_topk_compact_int4_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     """INT4 pool: every kept token's codes and scales (all heads) land at its
