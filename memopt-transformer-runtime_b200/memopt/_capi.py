@@ -72,6 +72,22 @@ def paged_attention_int4_ex(q, pages, block_size, bt, ctx, out, msl, win, causal
         "memopt_paged_attention_int4_ex")
 
 
+def evict_topk_workspace_size(S, L, H, D) -> int:
+    lib().memopt_evict_topk_workspace_size.restype = SZ
+    return int(lib().memopt_evict_topk_workspace_size(I(S), I(L), I(H), I(D)))
+
+
+def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain_ratio, sinks, kept, cnt, freed,
+                            fcnt, ws, ws_bytes, stream):
+    """Exact top-k eviction with compaction on INT4 pages [NB, H, page_bytes]."""
+    S, H, L = scores.shape
+    check(lib().memopt_evict_topk_compact_int4(
+        P(scores.data_ptr()), I(S), I(H), I(L), P(bt.data_ptr()), I(bt.shape[1]), P(ctx.data_ptr()),
+        P(pages.data_ptr()), I(pages.shape[0]), I(block_size), I(head_dim), C.c_float(retain_ratio), I(sinks),
+        P(kept.data_ptr()), P(cnt.data_ptr()), P(freed.data_ptr()), P(fcnt.data_ptr()), P(ws.data_ptr()),
+        SZ(ws_bytes), P(stream)), "memopt_evict_topk_compact_int4")
+
+
 def workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win) -> int:
     return int(lib().memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win))
 
