@@ -15,9 +15,6 @@
 #include "decode_mq.cuh"
 #include "decode_mq4.cuh"
 
-#ifndef MEMOPT_SPLIT_F16
-#define MEMOPT_SPLIT_F16 3
-#endif
 
 namespace memopt {
 
@@ -107,7 +104,7 @@ struct Split {
 // sub-windows), so calls with many query rows need no partials at all.
 // Measured on B200: fp16 decode is fastest near 1.5 items per slot, the INT4
 // kernel (16 warps per SM, cheaper items) near 4.
-constexpr int kSplitF16 = MEMOPT_SPLIT_F16;
+constexpr int kSplitF16 = 3;
 constexpr int kSplitInt4 = 8;
 Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window, int twice_target) {
   Split s;
