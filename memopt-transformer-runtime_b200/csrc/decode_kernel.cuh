@@ -443,9 +443,11 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         // B = q_int halves (qb); lane mt4 < G gets the group-mt4 sums.
 #pragma unroll
         for (int ti = 0; ti < 2; ++ti) {
+          // Without a second page the tile is still computed on the stage's
+          // stale bytes and masked below: a branch here would keep the two
+          // tiles' conversion and mma chains from interleaving.
           slo[ti] = -INFINITY;
           shi[ti] = -INFINITY;
-          if (ti == 1 && !has2) break;
           const uint32_t kr = tb[ti] + tt[ti] * 16 * (D / 2) + o_k;
           uint32_t w0[NKB], w1[NKB];
           if constexpr (D == 128) {
@@ -489,6 +491,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           const bool interior = sub_interior || (ttok[ti] >= win_start && ttok[ti] + 16 <= ctx);
           slo[ti] = (interior || (tl >= win_start && tl < ctx)) ? a_lo : -INFINITY;
           shi[ti] = (interior || (tl + 8 >= win_start && tl + 8 < ctx)) ? a_hi : -INFINITY;
+          if (ti == 1 && !has2) slo[ti] = shi[ti] = -INFINITY;  // no second page: stale stage bytes
         }
         // Step max over the lanes that own scores (mt4 == 0), in one warp
         // reduction on an order-preserving integer image of the floats
@@ -529,7 +532,7 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
           // (j, high) = dims D/8 mg + 4j + {1, 3}.
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
-            if (ti == 1 && !has2) break;
+
             const uint32_t pk = pack_half2(slo[ti], shi[ti]);   // (p_mg, p_mg+8)
             const uint32_t u0 = __shfl_sync(0xffffffffu, pk, 4 * mt4);        // (p_t, p_t+8)
             const uint32_t u1 = __shfl_sync(0xffffffffu, pk, 4 * mt4 + 16);   // (p_t+4, p_t+12)
@@ -540,8 +543,11 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
             const uint32_t vs8c = lds_u32(vsa + 16);
             const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
             const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
+            // No second page: p = 0 but the stale scale may be NaN, so zero B itself
+            // (the V code halves are finite by construction).
+            const bool live = ti == 0 || has2;
+            const uint32_t b0 = live ? *reinterpret_cast<const uint32_t*>(&b0h) : 0u;
+            const uint32_t b1 = live ? *reinterpret_cast<const uint32_t*>(&b1h) : 0u;
             const uint32_t vr = tb[ti] + tt[ti] * 16 * (D / 2) + o_v;
             uint32_t T0[2], T4[2], Y0[2], Y4[2];
             if constexpr (D == 128) {
