@@ -291,105 +291,143 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
     load_item(item, 0, mask, phys_lane, kvh_i, c_lo, more);
     for (;;) {
       while (mask != 0) {
-        const int jpage = __ffs(mask) - 1;
+        // One softmax step covers two 16-token tiles: both halves of a
+        // 32-token page, or two 16-token pages of the sub-window.  Without a
+        // second page the second tile is computed on the stage's stale bytes
+        // and masked (scores -inf, P.V operand zero): a branch would keep the
+        // two tiles' chains from interleaving.
+        const int ja = __ffs(mask) - 1;
         mask &= mask - 1;
-        const int page = c_lo + jpage;
-        if (!wait_stage(c_seq)) {
+        int jb = -1;
+        if (HALVES == 1 && mask != 0) {
+          jb = __ffs(mask) - 1;
+          mask &= mask - 1;
+        }
+        const int nst = (HALVES == 1 && jb >= 0) ? 2 : 1;  // ring stages this step
+        if (!wait_stage(c_seq) || (nst == 2 && !wait_stage(c_seq + 1))) {
           failed = true;
           break;
         }
-        const uint32_t stg = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
-#pragma unroll 1
-        for (int half = 0; half < HALVES; ++half) {
-          const int tok0 = page * BS + half * 16;
-          // ---- scores: exact integer products ----
-          int sacc[G][2][4];
+        const bool has_b = HALVES == 2 || jb >= 0;
+        uint32_t tstg[2];
+        int thalf[2], ttok[2];
+        tstg[0] = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
+        thalf[0] = 0;
+        ttok[0] = (c_lo + ja) * BS;
+        if (HALVES == 2) {
+          tstg[1] = tstg[0];
+          thalf[1] = 1;
+          ttok[1] = ttok[0] + 16;
+        } else {
+          tstg[1] = st0 + static_cast<uint32_t>((c_seq + 1) % NS) * C::STAGE;
+          thalf[1] = 0;
+          ttok[1] = (c_lo + (jb >= 0 ? jb : ja)) * BS;
+        }
+        // ---- scores: exact integer products, both tiles ----
+        int sacc[2][G][2][4];
+#pragma unroll
+        for (int ti = 0; ti < 2; ++ti) {
 #pragma unroll
           for (int h = 0; h < G; ++h) {
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
-              sacc[h][nt][0] = sacc[h][nt][1] = sacc[h][nt][2] = sacc[h][nt][3] = 0;
-              const uint2 w2 = lds_v2(stg + (half * 16 + nt * 8) * (D / 2) + o_k + 32 * h);
+              sacc[ti][h][nt][0] = sacc[ti][h][nt][1] = sacc[ti][h][nt][2] = sacc[ti][h][nt][3] = 0;
+              const uint2 w2 = lds_v2(tstg[ti] + (thalf[ti] * 16 + nt * 8) * (D / 2) + o_k + 32 * h);
 #pragma unroll
               for (int sb = 0; sb < 2; ++sb) {
                 const uint32_t w = sb ? w2.y : w2.x;
-                mma_s8(sacc[h][nt], qa[2 * h + sb], s8x16_even(w, kS8), s8x16_odd(w, kS8));
+                mma_s8(sacc[ti][h][nt], qa[2 * h + sb], s8x16_even(w, kS8), s8x16_odd(w, kS8));
               }
             }
           }
-          // Tokens of this lane's scores: tile token t4 + 4 e + 8 nt.
-          const bool interior = tok0 >= rlo && tok0 + 16 <= rhi;
-          float s[2][2];
+        }
+        float s[2][2][2];
+#pragma unroll
+        for (int ti = 0; ti < 2; ++ti) {
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const int pos = half * 16 + nt * 8 + t4 + 4 * e;
-              float v = 0.f;
+              const int pos = thalf[ti] * 16 + nt * 8 + t4 + 4 * e;
+              float v;
               if constexpr (G == 2) {
-                const uint32_t k2 = lds_u32(stg + C::K_SCALE + pos * 4);
+                const uint32_t k2 = lds_u32(tstg[ti] + C::K_SCALE + pos * 4);
                 const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&k2));
-                v = fmaf(kf.x, static_cast<float>(sacc[0][nt][e] * 256 + sacc[0][nt][e + 2]),
-                         kf.y * static_cast<float>(sacc[1][nt][e] * 256 + sacc[1][nt][e + 2]));
+                v = fmaf(kf.x, static_cast<float>(sacc[ti][0][nt][e] * 256 + sacc[ti][0][nt][e + 2]),
+                         kf.y * static_cast<float>(sacc[ti][1][nt][e] * 256 + sacc[ti][1][nt][e + 2]));
               } else {
-                v = lds_f16_as_f32(stg + C::K_SCALE + pos * 2) *
-                    static_cast<float>(sacc[0][nt][e] * 256 + sacc[0][nt][e + 2]);
+                v = lds_f16_as_f32(tstg[ti] + C::K_SCALE + pos * 2) *
+                    static_cast<float>(sacc[ti][0][nt][e] * 256 + sacc[ti][0][nt][e + 2]);
               }
               v *= sfac;
-              const int tok = tok0 + nt * 8 + t4 + 4 * e;
-              s[nt][e] = (interior || (tok >= rlo && tok < rhi)) ? v : -INFINITY;
+              const int tok = ttok[ti] + nt * 8 + t4 + 4 * e;
+              const bool vis = (ti == 0 || has_b) && tok >= rlo && tok < rhi;
+              s[ti][nt][e] = vis ? v : -INFINITY;
             }
           }
-          // ---- online softmax for row g8 (one quad per row) ----
-          float mx = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float mn = fmaxf(m, mx);
-          const float msub = mn == -INFINITY ? 0.f : mn;
-          // A row that has seen nothing yet has zero accumulators: no rescale.
-          const float corr = m == -INFINITY ? 1.f : ex2_approx(m - msub);
-          m = mn;
+        }
+        // ---- online softmax for row g8 (one quad per row) ----
+        float mx = fmaxf(fmaxf(fmaxf(s[0][0][0], s[0][0][1]), fmaxf(s[0][1][0], s[0][1][1])),
+                         fmaxf(fmaxf(s[1][0][0], s[1][0][1]), fmaxf(s[1][1][0], s[1][1][1])));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m, mx);
+        const float msub = mn == -INFINITY ? 0.f : mn;
+        // A row that has seen nothing yet has zero accumulators: no rescale.
+        const float corr = m == -INFINITY ? 1.f : ex2_approx(m - msub);
+        m = mn;
+        float psum = 0.f;
+#pragma unroll
+        for (int ti = 0; ti < 2; ++ti) {
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            s[nt][0] = ex2_approx(s[nt][0] - msub);
-            s[nt][1] = ex2_approx(s[nt][1] - msub);
-          }
-          l = fmaf(l, corr, (s[0][0] + s[0][1]) + (s[1][0] + s[1][1]));
-          // The O^T columns of this lane are query rows 2 t4 and 2 t4 + 1.
-          const float c0 = __shfl_sync(0xffffffffu, corr, 8 * t4);
-          const float c1 = __shfl_sync(0xffffffffu, corr, 8 * t4 + 4);
-          if (__any_sync(0xffffffffu, c0 != 1.f || c1 != 1.f)) {
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-#pragma unroll
-              for (int bp = 0; bp < 2; ++bp) {
-#pragma unroll
-                for (int hl = 0; hl < 2; ++hl) {
-                  acc[h][bp][hl][0] *= c0;
-                  acc[h][bp][hl][1] *= c1;
-                  acc[h][bp][hl][2] *= c0;
-                  acc[h][bp][hl][3] *= c1;
-                }
-              }
-              wsum[h][0] *= c0;
-              wsum[h][1] *= c1;
-              wsum[h][2] *= c0;
-              wsum[h][3] *= c1;
+            for (int e = 0; e < 2; ++e) {
+              s[ti][nt][e] = ex2_approx(s[ti][nt][e] - msub);
+              psum += s[ti][nt][e];
             }
           }
-          // ---- P.V transposed: A = V codes (dims x tokens), B = p * V scale ----
-          const uint32_t p04 = pack_half2(s[0][0], s[0][1]);  // tokens (t4, t4 + 4)
-          const uint32_t p8c = pack_half2(s[1][0], s[1][1]);  // tokens (t4 + 8, t4 + 12)
-          const uint32_t vr = stg + half * 16 * (D / 2) + o_v;
+        }
+        l = fmaf(l, corr, psum);
+        // The O^T columns of this lane are query rows 2 t4 and 2 t4 + 1.
+        const float c0 = __shfl_sync(0xffffffffu, corr, 8 * t4);
+        const float c1 = __shfl_sync(0xffffffffu, corr, 8 * t4 + 4);
+        if (__any_sync(0xffffffffu, c0 != 1.f || c1 != 1.f)) {
 #pragma unroll
           for (int h = 0; h < G; ++h) {
-            const uint32_t vsa = stg + o_vs + (half * G + h) * 32;
+#pragma unroll
+            for (int bp = 0; bp < 2; ++bp) {
+#pragma unroll
+              for (int hl = 0; hl < 2; ++hl) {
+                acc[h][bp][hl][0] *= c0;
+                acc[h][bp][hl][1] *= c1;
+                acc[h][bp][hl][2] *= c0;
+                acc[h][bp][hl][3] *= c1;
+              }
+            }
+            wsum[h][0] *= c0;
+            wsum[h][1] *= c1;
+            wsum[h][2] *= c0;
+            wsum[h][3] *= c1;
+          }
+        }
+        // ---- P.V transposed: A = V codes (dims x tokens), B = p * V scale ----
+#pragma unroll
+        for (int ti = 0; ti < 2; ++ti) {
+          const bool live = ti == 0 || has_b;
+          const uint32_t p04 = pack_half2(s[ti][0][0], s[ti][0][1]);  // tokens (t4, t4 + 4)
+          const uint32_t p8c = pack_half2(s[ti][1][0], s[ti][1][1]);  // tokens (t4 + 8, t4 + 12)
+          const uint32_t vr = tstg[ti] + thalf[ti] * 16 * (D / 2) + o_v;
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const uint32_t vsa = tstg[ti] + o_vs + (thalf[ti] * G + h) * 32;
             const uint32_t vs04 = lds_u32(vsa);
             const uint32_t vs8c = lds_u32(vsa + 16);
             const __half2 b0h = __hmul2(*reinterpret_cast<const __half2*>(&p04), *reinterpret_cast<const __half2*>(&vs04));
             const __half2 b1h = __hmul2(*reinterpret_cast<const __half2*>(&p8c), *reinterpret_cast<const __half2*>(&vs8c));
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&b0h);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&b1h);
+            // A stale scale may be NaN: zero the operand of a missing tile.
+            const uint32_t b0 = live ? *reinterpret_cast<const uint32_t*>(&b0h) : 0u;
+            const uint32_t b1 = live ? *reinterpret_cast<const uint32_t*>(&b1h) : 0u;
             // Group h's 4 bytes of rows t4, t4+4, t4+8, t4+12 (the half swap
             // moves the second group's bytes by -32 on swapped rows).
             const uint32_t ho = (D == 128 && h == 1) ? ((t4 & 2) ? 0u - 32u : 32u) : 0u;
@@ -412,11 +450,13 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
             const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
             mma16816(wsum[h], ones, b0, b1);
           }
-          if (++since_flush == kFlushSteps) flush_offsets();
         }
+        if (++since_flush == kFlushSteps) flush_offsets();
         __syncwarp();
-        ++c_seq;
-        produce();
+        for (int k = 0; k < nst; ++k) {
+          ++c_seq;
+          produce();
+        }
       }
       if (failed || !more) break;
       ++sub;
