@@ -503,13 +503,16 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
         mk ^= (mk >> 31) & 0x7fffffff;
         mp = __int_as_float(mk);
         const float m_new = fmaxf(m, mp);
-        if (m_new != -INFINITY) {
-          const float alpha = ex2_approx(m - m_new);
+        {
+          // Nothing visible yet: subtract 0 (every p is 0) and keep the
+          // (zero) accumulators unscaled, so no branch skips the step.
+          const float msub = m_new == -INFINITY ? 0.f : m_new;
+          const float alpha = m == -INFINITY ? 1.f : ex2_approx(m - msub);
           m = m_new;
 #pragma unroll
           for (int ti = 0; ti < 2; ++ti) {
-            slo[ti] = ex2_approx(slo[ti] - m_new);
-            shi[ti] = ex2_approx(shi[ti] - m_new);
+            slo[ti] = ex2_approx(slo[ti] - msub);
+            shi[ti] = ex2_approx(shi[ti] - msub);
           }
           const float psum = (slo[0] + shi[0]) + (slo[1] + shi[1]);
           l = l * alpha + (mt4 == 0 ? psum : 0.f);
