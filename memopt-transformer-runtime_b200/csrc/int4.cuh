@@ -72,11 +72,31 @@ __device__ __forceinline__ uint32_t int4_code_fast(float x, float scale, float r
 
 // Eight consecutive codes packed into one little-endian word: nibble j holds
 // element j, so byte k = q[2k] | q[2k+1] << 4 as in the reference.
+// The near-boundary test of int4_code_fast is made once for the eight
+// elements: the exact quotient is a division (a call, not a predicated
+// instruction), so a per-element test costs a branch per element even though
+// it is almost never taken.  When any of the eight is near a boundary the
+// whole word is recomputed with int4_code; the result is the same either way.
 __device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
   const float rinv = rcp_approx(scale);
   uint32_t w = 0;
+  bool near = false;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) w |= int4_code_fast(f[j], scale, rinv) << (4 * j);
+  for (int j = 0; j < 8; ++j) {
+    const float q = f[j] * rinv;
+    const float t = fabsf(q) + 0.5f;
+    const float k = floorf(t);
+    const float fr = t - k;
+    near |= fr < 1.6e-5f || fr > 1.f - 1.6e-5f;
+    const int ik = static_cast<int>(k);
+    const int iq = (q < 0.f ? -ik : ik) + 8;
+    w |= static_cast<uint32_t>(min(max(iq, 0), 15)) << (4 * j);
+  }
+  if (near) {
+    w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
+  }
   return w;
 }
 
