@@ -200,7 +200,30 @@ paged_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CU
       p_mask &= p_mask - 1;
       phys2 = __shfl_sync(0xffffffffu, p_phys, j2);
     }
-    if (lane == 0) issue(p_seq, phys, phys2, p_h);
+    if constexpr (INT4) {
+      // Warp-collective issue: one elected lane arms the stage's mbarrier and
+      // starts the copies, with no divergent branch around it.
+      const int s = static_cast<int>(p_seq % NS);
+      const uint32_t bar = bar0 + 8 * s;
+      const uint32_t dst = st0 + s * C::STAGE;
+      const uint32_t bytes = (C::PPS == 2 && phys2 >= 0) ? 2 * C::PAGE_RAW : C::PAGE_RAW;
+      const uint8_t* src1 = p.pages + (static_cast<int64_t>(phys) * p.KVH + p_h) * C::PAGE_RAW;
+      const uint8_t* src2 = p.pages + (static_cast<int64_t>(phys2 >= 0 ? phys2 : phys) * p.KVH + p_h) * C::PAGE_RAW;
+      const uint32_t two = (C::PPS == 2 && phys2 >= 0) ? 1u : 0u;
+      asm volatile(
+          "{\n\t.reg .pred pe, p2;\n\t"
+          "elect.sync _|pe, 0xffffffff;\n\t"
+          "setp.ne.and.u32 p2, %5, 0, pe;\n\t"
+          "@pe fence.proxy.async.shared::cta;\n\t"
+          "@pe mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t"
+          "@pe cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3], %6, [%0];\n\t"
+          "@p2 cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%7], [%4], %6, [%0];\n\t"
+          "}" ::"r"(bar), "r"(bytes), "r"(dst), "l"(src1), "l"(src2), "r"(two), "r"(static_cast<uint32_t>(C::PAGE_RAW)),
+          "r"(dst + static_cast<uint32_t>(C::PAGE_RAW))
+          : "memory");
+    } else {
+      if (lane == 0) issue(p_seq, phys, phys2, p_h);
+    }
     ++p_seq;
   };
 
