@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   constexpr int CB = D / 2;       // code row bytes
   constexpr int LPR = CB / 16;    // lanes per code row (16 bytes each)
   constexpr int HPI = 32 / LPR;   // heads per warp instruction
-  extern __shared__ __align__(16) uint8_t stage_all[];  // per warp: KVH x (K row, V row) code bytes
+  extern __shared__ __align__(128) uint8_t stage_rows[];  // per warp: KVH x (K row, V row) code bytes
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   __shared__ int cta_ticket;
   if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   const int sp = old_bt[static_cast<int64_t>(b) * MB + t / BS], spos = t % BS;
   const int dp = new_bt[static_cast<int64_t>(b) * MB + row / BS], dpos = row % BS;
   const int sswap = (D == 128 && (spos & 2)) ? 2 : 0, dswap = (D == 128 && (dpos & 2)) ? 2 : 0;
-  uint8_t* stage = stage_all + static_cast<size_t>(w) * KVH * 2 * CB;
+  uint8_t* stage = stage_rows + static_cast<size_t>(w) * KVH * 2 * CB;
   const uint32_t sst = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
   // Lane -> (head hs of each group of HPI heads, 16-byte chunk c of its rows):
   // a warp instruction covers HPI whole code rows (coalesced 64-byte runs).

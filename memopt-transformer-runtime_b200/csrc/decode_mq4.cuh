@@ -107,14 +107,6 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
     mask = __ballot_sync(0xffffffffu, ok);
   };
 
-  auto issue = [&](uint32_t seq, int phys, int kvh) {
-    const int s = static_cast<int>(seq % NS);
-    const uint32_t bar = bar0 + 8 * s;
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar, C::PAGE_RAW);
-    bulk_g2s(st0 + s * C::STAGE, p.pages + (static_cast<int64_t>(phys) * p.KVH + kvh) * C::PAGE_RAW,
-             C::PAGE_RAW, bar);
-  };
 
   // ---------------- producer cursor (warp-uniform) ----------------------
   int64_t p_item = first - nwarps;
@@ -145,7 +137,21 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
     const int j = __ffs(p_mask) - 1;
     p_mask &= p_mask - 1;
     const int phys = __shfl_sync(0xffffffffu, p_phys, j);
-    if (lane == 0) issue(p_seq, phys, p_kvh);
+    {
+      // Warp-collective issue: one elected lane arms the stage and starts the
+      // copy, with no divergent branch around it.
+      const int st = static_cast<int>(p_seq % NS);
+      const uint32_t bar = bar0 + 8 * st;
+      const uint8_t* src = p.pages + (static_cast<int64_t>(phys) * p.KVH + p_kvh) * C::PAGE_RAW;
+      asm volatile(
+          "{\n\t.reg .pred pe;\n\t"
+          "elect.sync _|pe, 0xffffffff;\n\t"
+          "@pe fence.proxy.async.shared::cta;\n\t"
+          "@pe mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t"
+          "@pe cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3], %1, [%0];\n\t"
+          "}" ::"r"(bar), "r"(static_cast<uint32_t>(C::PAGE_RAW)), "r"(st0 + st * C::STAGE), "l"(src)
+          : "memory");
+    }
     ++p_seq;
   };
 
