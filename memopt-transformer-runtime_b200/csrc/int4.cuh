@@ -100,6 +100,66 @@ __device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
   return w;
 }
 
+// Max over the 8-lane group with NaN propagation: NaN if any element of the
+// group is NaN (fmaxf in group8_absmax would skip it).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// The lane's 8 codes of a group of 64 (8 lanes per group, all present) and
+// the group's scale, bit-identical to int4_scale_from_absmax(group8_absmax)
+// and int4_code.  Groups holding a NaN or an infinity take that exact path.
+// Otherwise |x / scale| <= 7 (+ rounding), so each code is
+// sign(q) floor(|q| + 1/2) + 8 in [1, 15] with q = x * rcp(scale) (the
+// int4_code_fast argument), built without float->int conversion or clamps:
+// copysign(k, q) + (8 + 2^23) puts the code in the low mantissa bits, and
+// byte permutes pack the nibbles.  If any of the lane's 8 quotients is near a
+// rounding boundary (| frac - 1/2 | >= 1/2 - 1.6e-5) its word is recomputed
+// with the exact division.
+__device__ __forceinline__ uint32_t int4_quant8(const float f[8], float& scale_out) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmax_nan(m, fabsf(f[i]));
+  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  if (!(m < INFINITY)) {  // NaN or inf in the group (uniform over its 8 lanes): the reference path
+    const float scale = int4_scale_from_absmax(group8_absmax(f));
+    scale_out = scale;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
+    return w;
+  }
+  const float scale = int4_scale_from_absmax(m);
+  scale_out = scale;
+  const float rinv = rcp_approx(scale);
+  uint32_t u[8];
+  float dmax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float q = f[j] * rinv;
+    const float t = fabsf(q) + 0.5f;
+    const float k = floorf(t);
+    dmax = fmaxf(dmax, fabsf((t - k) - 0.5f));
+    u[j] = __float_as_uint(copysignf(k, q) + 8388616.0f);  // 2^23 + 8 + code - 8
+  }
+  // nibble j = low 4 bits of u[j]
+  const uint32_t b01 = (u[0] & 0xFu) | ((u[1] & 0xFu) << 4);
+  const uint32_t b23 = (u[2] & 0xFu) | ((u[3] & 0xFu) << 4);
+  const uint32_t b45 = (u[4] & 0xFu) | ((u[5] & 0xFu) << 4);
+  const uint32_t b67 = (u[6] & 0xFu) | ((u[7] & 0xFu) << 4);
+  uint32_t w = __byte_perm(__byte_perm(b01, b23, 0x0040), __byte_perm(b45, b67, 0x0040), 0x5410);
+  if (dmax >= 0.5f - 1.6e-5f) {
+    w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
+  }
+  return w;
+}
+
 // INT4 page layout helpers (one page per (block, head)):
 //   [K codes BS*D/2 | V codes BS*D/2 | K scales BS*(D/64) fp16 | V scales]
 // K row pos holds byte i = q[2i] | q[2i+1] << 4 at byte i.  The V row holds

@@ -31,9 +31,10 @@ quantize_int4_kernel(const uint4* __restrict__ in, uint32_t* __restrict__ codes,
 #pragma unroll
       for (int j = 0; j < 8; ++j) f[j] = 0.f;
     }
-    const float scale = int4_scale_from_absmax(group8_absmax(f));
+    float scale;
+    const uint32_t w = int4_quant8(f, scale);
     if (live) {
-      codes[c] = int4_pack8(f, scale);
+      codes[c] = w;
       if ((c & 7) == 0) scales[c >> 3] = scale;
     }
   }

@@ -130,8 +130,9 @@ write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict_
         float fk[8], fv[8];
         unpack_half8(kv[u], fk);
         unpack_half8(vv[u], fv);
-        const float sk = int4_scale_from_absmax(group8_absmax(fk));
-        const float sv = int4_scale_from_absmax(group8_absmax(fv));
+        float sk, sv;
+        const uint32_t wk = int4_quant8(fk, sk);
+        const uint32_t wv = int4_quant8(fv, sv);
         if (c < chunks) {
           const int g = c >> 3;  // group within the token row
           const int h = g / gpr;
@@ -139,9 +140,8 @@ write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict_
           uint8_t* page = pages + (blk * num_heads + h) * page_bytes;
           const int byte = gi * 32 + (c & 7) * 4;  // logical byte of the row
           const int64_t row = static_cast<int64_t>(pos) * (head_dim / 2);
-          *reinterpret_cast<uint32_t*>(page + row + byte) = int4_pack8(fk, sk);
-          *reinterpret_cast<uint32_t*>(page + codes_bytes + row + int4_vrow_swizzle(pos, byte, head_dim)) =
-              int4_pack8(fv, sv);
+          *reinterpret_cast<uint32_t*>(page + row + byte) = wk;
+          *reinterpret_cast<uint32_t*>(page + codes_bytes + row + int4_vrow_swizzle(pos, byte, head_dim)) = wv;
           if ((c & 7) == 0) {
             __half* ks = reinterpret_cast<__half*>(page + 2 * codes_bytes);
             __half* vs = reinterpret_cast<__half*>(page + 2 * codes_bytes + scale_bytes);
