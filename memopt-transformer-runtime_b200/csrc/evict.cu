@@ -139,9 +139,10 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
       // or below its smallest counts every comparable score: no scan needed.
       int c = mid > tmax ? 0 : ncmp;
       if (mid > tmin && mid <= tmax) {
-        c = 0;
+        int cp[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // eight independent chains instead of one of VPT adds
 #pragma unroll
-        for (int i = 0; i < VPT; ++i) c += (v[i] >= mid) ? 1 : 0;
+        for (int i = 0; i < VPT; ++i) cp[i & 7] += (v[i] >= mid) ? 1 : 0;
+        c = ((cp[0] + cp[1]) + (cp[2] + cp[3])) + ((cp[4] + cp[5]) + (cp[6] + cp[7]));
       }
       c = warp_sum_i(c);
       const int buf = it & 1;
