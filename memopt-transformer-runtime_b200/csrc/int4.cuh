@@ -133,7 +133,17 @@ __device__ __forceinline__ uint32_t int4_quant8(const float f[8], float& scale_o
     for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
     return w;
   }
-  const float scale = int4_scale_from_absmax(m);
+  // absmax / 7 without the division routine: q0 = m * fp32(1/7) corrected by one
+  // fma step is the correctly rounded quotient for every finite fp16 value m
+  // (checked exhaustively over all 31743 positive finite fp16 values against
+  // the IEEE fp32 quotient; m is the max of fp16 inputs, and NaN/inf groups
+  // took the path above).
+  float scale = 1.0f;
+  if (m > 0.f) {
+    const float r7 = 0.142857149f;  // fp32(1/7)
+    const float q0 = __fmul_rn(m, r7);
+    scale = __fmaf_rn(__fmaf_rn(-q0, 7.0f, m), r7, q0);
+  }
   scale_out = scale;
   const float rinv = rcp_approx(scale);
   uint32_t u[8];
