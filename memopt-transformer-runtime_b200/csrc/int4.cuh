@@ -45,59 +45,10 @@ __device__ __forceinline__ uint32_t int4_code(float x, float scale) {
   return static_cast<uint32_t>(min(max(iq, 0), 15));
 }
 
-// The same code without an IEEE division per element.  With scale =
-// absmax / 7, |x / scale| is at most 7 plus rounding, and roundf(x / scale)
-// = sign(q) floor(|q| + 1/2) can differ from the value computed from
-// q' = x * rcp(scale) (a few ulp of 8 away, < 3e-6) only when |q'| + 1/2 is
-// within 1.6e-5 of an integer; those elements take the exact quotient.  The
-// result is bit-identical to int4_code, NaN and inf included (NaN -> 8; the
-// saturated conversion of an infinite quotient wraps and clamps to 0 in
-// both).
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-__device__ __forceinline__ uint32_t int4_code_fast(float x, float scale, float rinv) {
-  const float q = x * rinv;
-  const float t = fabsf(q) + 0.5f;
-  float k = floorf(t);
-  const float fr = t - k;
-  // (also catches |q| + 1/2 rounding up to an integer, where floor would be off)
-  if (fr < 1.6e-5f || fr > 1.f - 1.6e-5f) k = fabsf(roundf(x / scale));
-  const int ik = static_cast<int>(k);
-  const int iq = (q < 0.f ? -ik : ik) + 8;
-  return static_cast<uint32_t>(min(max(iq, 0), 15));
-}
-
-// Eight consecutive codes packed into one little-endian word: nibble j holds
-// element j, so byte k = q[2k] | q[2k+1] << 4 as in the reference.
-// The near-boundary test of int4_code_fast is made once for the eight
-// elements: the exact quotient is a division (a call, not a predicated
-// instruction), so a per-element test costs a branch per element even though
-// it is almost never taken.  When any of the eight is near a boundary the
-// whole word is recomputed with int4_code; the result is the same either way.
-__device__ __forceinline__ uint32_t int4_pack8(const float f[8], float scale) {
-  const float rinv = rcp_approx(scale);
-  uint32_t w = 0;
-  bool near = false;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float q = f[j] * rinv;
-    const float t = fabsf(q) + 0.5f;
-    const float k = floorf(t);
-    const float fr = t - k;
-    near |= fr < 1.6e-5f || fr > 1.f - 1.6e-5f;
-    const int ik = static_cast<int>(k);
-    const int iq = (q < 0.f ? -ik : ik) + 8;
-    w |= static_cast<uint32_t>(min(max(iq, 0), 15)) << (4 * j);
-  }
-  if (near) {
-    w = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
-  }
-  return w;
 }
 
 // Max over the 8-lane group with NaN propagation: NaN if any element of the
@@ -111,9 +62,11 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 // The lane's 8 codes of a group of 64 (8 lanes per group, all present) and
 // the group's scale, bit-identical to int4_scale_from_absmax(group8_absmax)
 // and int4_code.  Groups holding a NaN or an infinity take that exact path.
-// Otherwise |x / scale| <= 7 (+ rounding), so each code is
-// sign(q) floor(|q| + 1/2) + 8 in [1, 15] with q = x * rcp(scale) (the
-// int4_code_fast argument), built without float->int conversion or clamps:
+// Otherwise |x / scale| <= 7 (+ rounding), and roundf(x / scale) =
+// sign(q) floor(|q| + 1/2) can differ from the value computed from
+// q = x * rcp(scale) (a few ulp of 8 away, < 3e-6) only when |q| + 1/2 is
+// within 1.6e-5 of an integer; so each code is sign(q) floor(|q| + 1/2) + 8
+// in [1, 15], built without float->int conversion or clamps:
 // copysign(k, q) + (8 + 2^23) puts the code in the low mantissa bits, and
 // byte permutes pack the nibbles.  If any of the lane's 8 quotients is near a
 // rounding boundary (| frac - 1/2 | >= 1/2 - 1.6e-5) its word is recomputed
