@@ -106,6 +106,11 @@ struct Split {
 // kernel (16 warps per SM, cheaper items) near 4.
 constexpr int kSplitF16 = 3;
 constexpr int kSplitInt4 = 8;
+// The INT4 multi-query kernel (costlier items: q hi/lo preparation, up to 8
+// rows merged) measured best near 1.5 items per slot as well: at 32 query
+// heads over 8 KV heads, batch 32 / 128, ctx 4096, 64 / 172 us against 84 /
+// 177 us at the one-row INT4 target.
+constexpr int kSplitMq4 = 3;
 Split choose_split(int64_t pairs, int max_blocks_per_seq, int block_size, int window, int twice_target) {
   Split s;
   const int64_t wpages =
@@ -157,7 +162,7 @@ int64_t mq_groups(int batch, int q_len, int H, int KVH, int tile_rows) {
 // token), so its chunks cover window + q_len - 1 tokens.
 Split mq_split(bool int4, int batch, int q_len, int H, int KVH, int MB, int BS, int window) {
   return choose_split(mq_groups(batch, q_len, H, KVH, mq_tile_rows(int4)), MB, BS, window + q_len - 1,
-                      int4 ? kSplitInt4 : kSplitF16);
+                      int4 ? kSplitMq4 : kSplitF16);
 }
 
 template <int D, int BS>
