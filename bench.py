@@ -58,51 +58,104 @@ def peaks() -> tuple[float, str]:
 
 
 class Clocks:
-    """nvidia-smi sampler running during the timed region."""
+    """SM clock and clock-event reasons sampled during the timed region.
+
+    NVML is polled from a thread every millisecond (a decode step lasts a
+    fraction of a millisecond, so nvidia-smi's 100 ms loop sees nothing);
+    nvidia-smi is the fallback when NVML cannot be opened.  Read-only."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.sm, self.mx, self.reasons = [], 0.0, set()
+        self._stop = None
+        self._thread = None
+        self.source = "none"
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:  # noqa: BLE001
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self, nv, h):
+        import time as _t
+
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        while True:
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                self.mx = max(self.mx, float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.reasons.update(n for n, b in bits.items() if r & b)
+            except Exception:  # noqa: BLE001
+                pass
+            if self._stop.wait(0.001):
+                return
 
     def __enter__(self):
+        import threading
+
+        try:
+            nv, h = self._nvml_handle()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self._thread.start()
+            self.source = "nvml"
+            return self
+        except Exception:  # noqa: BLE001
+            self._thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi"
         except Exception:  # noqa: BLE001
             self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        out = ""
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                out, _ = self.proc.communicate(timeout=5)
             except Exception:  # noqa: BLE001
                 self.proc.kill()
-
-    def summary(self) -> dict:
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (self.out or "").splitlines():
+        for line in (out or "").splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                self.sm.append(float(f[1]))
+                self.mx = max(self.mx, float(f[2]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(self.NAMES, f[5:9]):
                 if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                    self.reasons.add(n)
+
+    def summary(self) -> dict:
+        sm = self.sm
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.mx or None,
+                "reasons": sorted(self.reasons), "samples": len(sm), "source": self.source}
 
 
 def dist_env():
@@ -120,6 +173,25 @@ def make_fp16_workload(torch, seed: int, dev):
     bt = torch.randperm(NB, generator=gc)[: B * MB].reshape(B, MB).to(torch.int32).to(dev)
     q = torch.randn(B, 1, H, D, device=dev, dtype=torch.float16, generator=g)
     ctx = torch.full((B,), CTX, dtype=torch.int32, device=dev)
+    return kp, vp, bt, q, ctx
+
+
+PREFILL_B, PREFILL_QL = 4, 8192  # BASELINE configs[4] prefill
+
+
+def make_prefill_workload(torch, dev, rank: int = 0, batch: int = PREFILL_B):
+    """configs[4] prefill inputs: `batch` sequences x 8192 query tokens over
+    their own 8192 cached tokens (seeded N(0,1) fp16, permuted tables)."""
+    pql = PREFILL_QL
+    mb = pql // BS
+    nb = batch * mb
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    kp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    vp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(5 + rank))[: batch * mb].reshape(batch, mb)
+    bt = bt.to(torch.int32).to(dev)
+    q = torch.randn(batch, pql, H, D, device=dev, dtype=torch.float16, generator=g)
+    ctx = torch.full((batch,), pql, dtype=torch.int32, device=dev)
     return kp, vp, bt, q, ctx
 
 
@@ -207,7 +279,46 @@ def run_reference(args) -> None:
                                    "oracle/memopt_oracle.c with OpenMP on all host cores"},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    line["reference_gpu_kernel"] = reference_gpu_kernel(args)
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_kernel(args) -> dict:
+    """The reference's own CUDA dynamic_sparse_attention (attention.cu:371-521,
+    compiled unmodified from its sources into oracle/_ref by
+    oracle/build_ref.py) on the configs[1] workload, for comparison with this
+    build's kernel.  The reference op synchronises the device after its
+    launch (its debug-sync macro), so each call is timed alone with CUDA
+    events on the default stream it launches on.  configs[1] is within its
+    limits (8192 pages x 65536 elements < 2^31)."""
+    try:
+        import torch
+
+        if not torch.cuda.is_available():
+            return {"unavailable": "no CUDA device"}
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        from build_ref import load
+
+        ref = load()
+        if ref is None:
+            return {"unavailable": "oracle/_ref/memopt_ref_C.so was not built (no reference checkout at build time)"}
+        dev = torch.device("cuda", 0)
+        kp, vp, bt, q, ctx = make_fp16_workload(torch, 1234, dev)
+        stream = torch.cuda.default_stream(dev)
+        with torch.cuda.stream(stream):
+            ref.dynamic_sparse_attention(q, kp, vp, bt, ctx, CTX, CTX)
+            torch.cuda.synchronize()
+            ms = time_each(torch, lambda: ref.dynamic_sparse_attention(q, kp, vp, bt, ctx, CTX, CTX),
+                           max(3, min(args.steps, 10)), stream)
+        sbytes = step_bytes(B, CTX)
+        peak, kind = peaks()
+        return {"workload": "BASELINE configs[1] (the same seeded inputs as this build's headline)",
+                "value": round(sbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+                "frac_of_hbm_peak": round(sbytes / ms / 1e6 / peak, 4), "peak_kind": kind,
+                "decode_tokens_per_s": round(B / (ms * 1e-3), 1),
+                "kernel": "reference sparse_flash_attention_kernel<16,128> (one CTA per (sequence, head, query))"}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
 
 
 def config_dict(n: int) -> dict:
@@ -302,6 +413,7 @@ def run_ours(args) -> None:
         extra.update(evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         extra.update(long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         extra.update(multi_query_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
+        extra.update(ops_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
         if ws_n > 1:
             extra.update(evict_head_sharded_extra(torch, memopt_C, dev, stream, group, ws_n))
 
@@ -343,7 +455,29 @@ def run_ours(args) -> None:
         "extra": extra,
     }
     print(json.dumps(line), flush=True)
+    print_leg_summary(extra, ws_n)
     group.destroy()
+
+
+# Order of the one-line summaries printed after the JSON line: the north-star
+# legs come last, so that a reader of the last lines of the output sees them.
+LEG_ORDER = ["evict_tokens", "evict_tokens_l2_flushed", "evict_cache", "evict_topk_compact", "evict_topk_compact_int4",
+             "evict_topk_head_sharded", "window_decode", "quantize_int4", "dequantize_int4", "write_cache_f16",
+             "multi_row_decode_f16", "gqa_decode_f16", "gqa_decode_int4", "long_context_decode_retain_0.75",
+             "long_context_decode", "prefill", "int4_write_cache", "int4_decode"]
+
+
+def print_leg_summary(extra: dict, n: int) -> None:
+    """One short text line per secondary leg (not JSON: the JSON line above is
+    the bench result): value, unit, fraction of the measured peak, time."""
+    names = [k for k in LEG_ORDER if k in extra] + [k for k in extra if k not in LEG_ORDER]
+    for k in names:
+        v = extra[k]
+        frac = next((v[f] for f in ("frac_of_hbm_peak", "frac_of_hbm_peak_per_gpu", "frac_of_tensor_peak")
+                     if f in v), None)
+        ms = next((v[f] for f in ("ms_per_step", "ms_per_call", "ms_per_launch") if f in v), None)
+        fs = f" frac {frac:.3f}" if frac is not None else ""
+        print(f"leg {k} N={n}: {v['value']} {v['unit']}{fs} {ms} ms", flush=True)
 
 
 def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
@@ -424,11 +558,102 @@ def run_only(args) -> None:
         res = prefill_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "mq":
         res = multi_query_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
+    elif args.only == "ops":
+        res = ops_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     elif args.only == "long":
         res = long_decode_extra(torch, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     else:
         res = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, lambda: None, lambda x: x, 1, 0)
     print(json.dumps(res), flush=True)
+
+
+def time_each(torch, fn, n: int, stream, flush=None) -> float:
+    """Median device time (ms) of n calls timed one by one with CUDA events on
+    `stream`; `flush` (untimed) runs before each call."""
+    evs = []
+    for _ in range(n):
+        if flush is not None:
+            flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+
+def l2_flusher(torch, dev):
+    """A write of 256 MB (twice the 126 MB L2) that evicts earlier data."""
+    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    return lambda: buf.zero_()
+
+
+def ops_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
+    """The data-plane operators besides decode, each on inputs larger than L2,
+    median of >= 20 calls timed one by one:
+    * quantize / dequantize (quantization.cu:104-270) of a 1.07 GB fp16 cache
+      [16, 32, 8192, 128]: bytes = fp16 elements x 2 + codes (1/2 B per
+      element) + fp32 scales (4 B per 64 elements);
+    * fp16 write_cache (kv_cache.cu:228-348) of 131072 tokens x 32 heads x 128
+      at configs[1] into an 8192-page pool: K and V read and written once plus
+      the int32 slots;
+    * evict_cache (kv_cache.cu:379-559) over a configs[3]-sized pool (16384
+      pages x 16 x 32 heads x 128), retain 0.75: per (block, head) 12 rows
+      kept, 4 zeroed; bytes = fp32 scores read + zeroed rows written."""
+    peak, _ = peaks()
+    res = {}
+    n = max(20, min(args.steps, 50))
+    g = torch.Generator(device=dev).manual_seed(71 + rank)
+    # quantize / dequantize
+    x = torch.randn(16, 32, 8192, 128, dtype=torch.float16, device=dev, generator=g)
+    ne = x.numel()
+    packed = torch.empty(16, 32, 8192, 64, dtype=torch.uint8, device=dev)
+    scales = torch.empty(ne // 64, dtype=torch.float32, device=dev)
+    qbytes = ne * 2 + ne // 2 + (ne // 64) * 4
+    ms_q = max_over_ranks(time_each(torch, lambda: _capi.quantize_int4(x, packed, scales, sp), n, stream))
+    y = torch.empty_like(x)
+    ms_d = max_over_ranks(time_each(torch, lambda: _capi.dequantize_int4(packed, scales, y, sp), n, stream))
+    res["quantize_int4"] = {"workload": "fp16 cache [16, 32, 8192, 128] (1.07 GB), group 64",
+                            "value": round(qbytes * ws_n / (ms_q * 1e-3) / 1e9, 2), "unit": "GB/s",
+                            "ms_per_call": round(ms_q, 5), "frac_of_hbm_peak": round(qbytes / ms_q / 1e6 / peak, 4),
+                            "algorithmic_bytes_per_call": qbytes}
+    res["dequantize_int4"] = {"workload": "packed codes + fp32 scales of the same cache -> fp16",
+                              "value": round(qbytes * ws_n / (ms_d * 1e-3) / 1e9, 2), "unit": "GB/s",
+                              "ms_per_call": round(ms_d, 5), "frac_of_hbm_peak": round(qbytes / ms_d / 1e6 / peak, 4),
+                              "algorithmic_bytes_per_call": qbytes}
+    del x, y, packed, scales
+    # fp16 write_cache, 131072 tokens
+    T = B * CTX
+    keys = torch.randn(T, H, D, dtype=torch.float16, device=dev, generator=g)
+    vals = torch.randn(T, H, D, dtype=torch.float16, device=dev, generator=g)
+    kp = torch.empty(NB, BS, H, D, dtype=torch.float16, device=dev)
+    vp = torch.empty_like(kp)
+    slots = (torch.randperm(NB, generator=torch.Generator().manual_seed(9 + rank)).to(torch.int32)
+             .repeat_interleave(BS) * BS + torch.arange(BS, dtype=torch.int32).repeat(NB)).to(dev)
+    wbytes = 2 * (2 * T * H * D * 2) + T * 4
+    ms_w = max_over_ranks(time_each(torch, lambda: _capi.write_cache_f16(keys, vals, slots, kp, vp, sp), n, stream))
+    res["write_cache_f16"] = {"workload": "configs[1]: 131072 tokens x 32 heads x 128 fp16 into 8192 permuted pages",
+                              "value": round(wbytes * ws_n / (ms_w * 1e-3) / 1e9, 2), "unit": "GB/s",
+                              "ms_per_call": round(ms_w, 5), "frac_of_hbm_peak": round(wbytes / ms_w / 1e6 / peak, 4),
+                              "tokens_per_s": round(T * ws_n / (ms_w * 1e-3), 1), "algorithmic_bytes_per_call": wbytes}
+    del keys, vals, kp, vp, slots
+    # evict_cache over a configs[3]-sized pool
+    enb = 16384
+    kp = torch.randn(enb, BS, H, D, dtype=torch.float16, device=dev, generator=g)
+    vp = torch.randn_like(kp)
+    sc = torch.empty(enb, BS, H, device=dev).log_normal_(0.0, 1.0, generator=g)
+    keep = max(1, int(0.75 * BS))
+    ebytes = sc.numel() * 4 + 2 * enb * H * (BS - keep) * D * 2
+    ms_e = max_over_ranks(time_each(torch, lambda: _capi.evict_cache(sc, kp, vp, 0.75, sp), n, stream))
+    res["evict_cache"] = {"workload": "configs[3] pool: 16384 pages x 16 x 32 heads x 128, lognormal scores, "
+                                      "retain 0.75 (12 of 16 rows kept per block and head)",
+                          "value": round(ebytes * ws_n / (ms_e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                          "ms_per_call": round(ms_e, 5), "frac_of_hbm_peak": round(ebytes / ms_e / 1e6 / peak, 4),
+                          "algorithmic_bytes_per_call": ebytes}
+    del kp, vp, sc
+    torch.cuda.empty_cache()
+    return res
 
 
 def long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
@@ -527,16 +752,8 @@ def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, 
     """BASELINE configs[4] prefill: 4 sequences x 8192 query tokens over their
     own 8192 cached tokens, 32 heads x 128, fp16, non-causal (reference
     semantics), on the tcgen05 path.  FLOPs = 4 * B * H * QL * ctx * D."""
-    pb, pql = 4, 8192
-    mb = pql // BS
-    nb = pb * mb
-    g = torch.Generator(device=dev).manual_seed(11 + rank)
-    kp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
-    vp = torch.randn(nb, BS, H, D, device=dev, dtype=torch.float16, generator=g)
-    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(5 + rank))[: pb * mb].reshape(pb, mb)
-    bt = bt.to(torch.int32).to(dev)
-    q = torch.randn(pb, pql, H, D, device=dev, dtype=torch.float16, generator=g)
-    ctx = torch.full((pb,), pql, dtype=torch.int32, device=dev)
+    pb, pql = PREFILL_B, PREFILL_QL
+    kp, vp, bt, q, ctx = make_prefill_workload(torch, dev, rank)
     out = torch.empty_like(q)
 
     def step():
@@ -584,6 +801,8 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
 
     ev_steps = max(3, min(args.steps, 50))
     ms_ev = max_over_ranks(time_loop(torch, evict, ev_steps, args.warmup, barrier, stream))
+    # the same calls with the L2 flushed before each (scores streamed from HBM)
+    ms_ev_cold = max_over_ranks(time_each(torch, evict, max(20, ev_steps), stream, l2_flusher(torch, dev)))
     idx, cnt = memopt_C.evict_tokens(scores, bt, ibf, 0.75, 4, return_retained=True)
     kept = float(cnt.float().mean().item()) / ectx
     ev_bytes = 2 * eb * H * ectx * 4  # scores read + kept-index list written (no row is evicted with sinks)
@@ -652,6 +871,11 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
                              "ms_per_call": round(ms_ev, 5), "kept_fraction": round(kept, 4),
                              "note": "reference semantics: with sinks the 32-step bisection keeps every token",
                              "l2": "the 33.5 MB of scores fit in L2 and stay resident between calls"},
+            "evict_tokens_l2_flushed": {"workload": "the same evict_tokens calls with a 256 MB write between them "
+                                                    "(scores read from HBM)",
+                                        "value": round(ev_bytes * ws_n / (ms_ev_cold * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                        "ms_per_call": round(ms_ev_cold, 5),
+                                        "frac_of_hbm_peak": round(ev_bytes / ms_ev_cold / 1e6 / peaks()[0], 4)},
             "evict_topk_compact": {"workload": "BASELINE configs[3] scores, exact top-k shared across heads "
                                                "(retain 0.75, 4 sinks), kept K/V rows compacted, pages released",
                                    "value": round(topk_bytes * ws_n / (ms_topk * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -778,7 +1002,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-int4", action="store_true", help="skip the INT4 secondary line")
-    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict", "long", "mq"], help="time one kernel family alone (profiling)")
+    ap.add_argument("--only", choices=["fp16", "int4", "prefill", "evict", "long", "mq", "ops"], help="time one kernel family alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

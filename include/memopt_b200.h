@@ -42,6 +42,7 @@ extern "C" {
 #define MEMOPT_ERR_CUDA             (-4)
 #define MEMOPT_ERR_OUT_OF_RANGE     (-5)
 #define MEMOPT_ERR_WORKSPACE        (-6)
+#define MEMOPT_ERR_TIMEOUT          (-7)
 
 /* Version of this ABI (bumped on any signature change). */
 int memopt_abi_version(void);
@@ -191,6 +192,20 @@ int memopt_evict_topk_compact_int4(const float* scores, int num_seqs, int num_he
                                    int32_t* freed_pages, int32_t* freed_count, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* Outcome of the last evict_topk_compact* call that used `workspace` on
+ * `stream` (no reference counterpart).  Synchronises the stream.  Every row
+ * move waits, with a bound, for the rows at its destination to be read; a
+ * wait that runs out skips that row's store (the destination keeps its old
+ * contents, so no kept row is overwritten before it is read) and is reported
+ * here as MEMOPT_ERR_TIMEOUT: the pool, block tables and lengths are then
+ * only partly compacted. */
+int memopt_evict_topk_status(const void* workspace, int num_seqs, int max_len, void* stream);
+/* Test hook (process-wide): bound of the row movers' flag waits in polls
+ * (0 = the default, over a second) and, when withhold_read_flags != 0, movers
+ * that never publish their "read" flags, so that every wait on one runs out.
+ * Only for testing the failure path above. */
+int memopt_evict_topk_set_test_hooks(uint32_t flag_poll_limit, int withhold_read_flags);
+
 /* Head-sharded form of the same operator (the one cross-GPU exchange of the  */
 /* data plane): with the heads of every sequence split over G ranks, rank r   */
 /* writes the fp32 sum of its own heads' scores (heads in order) with         */
@@ -254,16 +269,6 @@ int memopt_paged_attention_f16(const void* query, const void* key_pool,
                                void* out, void* workspace, size_t workspace_bytes,
                                void* stream);
 
-/* No counterpart in the reference.  Same as memopt_paged_attention_f16, but
- * for callers that cannot allocate device memory at call time (hosts with
- * their own allocator-free runtime, or steps where allocator calls are not
- * allowed): the split-K scratch is a fixed 4 MiB array inside this library's
- * device image (held on every GPU that loads the library until exit), so the
- * call allocates nothing.  Calls needing more scratch than
- * memopt_paged_attention_noalloc_max_bytes() return MEMOPT_ERR_WORKSPACE.
- * The first call on a device looks up the array's address (make it before
- * any stream capture).  All calls share the array: calls that overlap on the
- * GPU race.  The ticket region is cleared at the start of every call. */
 /* Extended attention (no reference counterpart for the options):          */
 /* num_kv_heads divides num_heads; the pools (fp16 [NB, BS, num_kv_heads, D]  */
 /* or INT4 pages [NB, num_kv_heads, page_bytes]) hold num_kv_heads heads and  */
@@ -287,6 +292,20 @@ int memopt_paged_attention_int4_ex(const void* query, const uint8_t* kv_pages,
                                    void* out, void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* No counterpart in the reference.  Same as memopt_paged_attention_f16, but
+ * for callers that cannot allocate device memory at call time (hosts with
+ * their own allocator-free runtime, or steps where allocator calls are not
+ * allowed): the split-K scratch is a fixed 4 MiB array inside this library's
+ * device image, so the call allocates nothing.  Calls needing more scratch
+ * than memopt_paged_attention_noalloc_max_bytes() return
+ * MEMOPT_ERR_WORKSPACE; calls with invalid arguments are rejected before the
+ * scratch is touched.  The first call on a device looks up the array's
+ * address; CUDA loads the module that holds the array lazily, so that first
+ * call is also when the 4 MiB are committed on that device and it can fail
+ * with an out-of-memory error (MEMOPT_ERR_CUDA): make it at start-up, before
+ * any stream capture.  From then on the array stays on that GPU until the
+ * process exits.  All calls share the array: calls that overlap on the GPU
+ * race.  The ticket region is cleared at the start of every call. */
 size_t memopt_paged_attention_noalloc_max_bytes(void);
 int memopt_paged_attention_f16_noalloc(const void* query, const void* key_pool,
                                        const void* value_pool,

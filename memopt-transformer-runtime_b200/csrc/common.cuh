@@ -20,6 +20,10 @@ void set_last_error(const std::string& msg);
 int fail(int status, const std::string& msg);
 int cuda_fail(cudaError_t err, const char* what);
 int sm_count();  // SMs of the current device (cached per device)
+// Argument checks of memopt_paged_attention_f16_ex that need no workspace
+// (sizes, head grouping, supported geometry, alignment, row count).
+int validate_attention_f16(const void* query, const void* key_pool, const void* value_pool, int batch, int q_len,
+                           int H, int KVH, int D, int MB, int64_t NB, int BS, const void* out);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -29,6 +29,7 @@
 // move in place.  A row only moves forward (destination ordinal <= source
 // ordinal), so the one hazard is overwriting a slot before the row that
 // lives there has been read; the move kernel orders exactly those pairs.
+#include <atomic>
 #include <climits>
 
 #include "common.cuh"
@@ -45,6 +46,11 @@ constexpr int kVPT = kMaxLen / kSelThreads;  // 32 tokens per thread
 // (retain 0.75) one row per CTA moved the rows in 1.17 ms, 2 in 1.19 ms,
 // 4 in 1.29 ms and 8 in 1.73 ms: small CTAs keep more copies in flight.
 constexpr int kSegRows = 1;
+
+// Flag-wait bound of the row movers and the test hook that withholds their
+// "read" flags (memopt_evict_topk_set_test_hooks); defaults: kMaxPolls, off.
+std::atomic<uint32_t> g_flag_polls{kMaxPolls};
+std::atomic<int> g_withhold_flags{0};
 constexpr int kMaxPagesBig = 16 * kSelThreads;   // streaming select: up to 16 table entries per thread
 constexpr int kMoveSmemLimit = 200 * 1024;       // 2 * kSegRows rows staged in shared memory
 
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
     int nseg, int total_segs, uint8_t* __restrict__ kpool, uint8_t* __restrict__ vpool, uint32_t row_bytes,
-    int* ctrl, int* flags, int seg_stride) {
+    int* ctrl, int* flags, int seg_stride, uint32_t flag_polls, int withhold_flags) {
   __shared__ int cta_ticket;
   if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
   __syncthreads();
@@ -509,15 +515,21 @@ __global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
       bulk_g2s(sstage + (2 * i) * row_bytes, kpool + src[i], row_bytes, sbar);
       bulk_g2s(sstage + (2 * i + 1) * row_bytes, vpool + src[i], row_bytes, sbar);
     }
-    uint32_t polls = 0;
-    while (!mbar_try_wait(sbar, 0)) {
-      if (++polls > kMaxPolls) {
-        atomicExch(&ctrl[1], 1);
-        break;
+    bool landed = false;
+    for (uint32_t polls = 0; polls <= kMaxPolls && !landed; ++polls) landed = mbar_try_wait(sbar, 0);
+    if (!landed) {
+      // The rows never arrived: this segment neither publishes "read" nor
+      // stores (its sources stay where they are), records the failure, and
+      // gives its copies in flight one more bounded wait before the CTA's
+      // shared memory goes away.
+      atomicExch(&ctrl[1], 1);
+      for (uint32_t polls = 0; polls <= kMaxPolls && !mbar_try_wait(sbar, 0); ++polls) {
       }
+      return;
     }
   }
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flags + static_cast<int64_t>(b) * seg_stride + k), "r"(1) : "memory");
+  if (!withhold_flags)
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flags + static_cast<int64_t>(b) * seg_stride + k), "r"(1) : "memory");
   if (!moving) return;
   const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + k];
   for (int m = d; m < k && m <= d + 1; ++m) {
@@ -527,9 +539,11 @@ __global__ void __launch_bounds__(32 * kMoveWarps16) move_rows_inplace_kernel(
     while (true) {
       asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
       if (v) break;
-      if (++polls > kMaxPolls) {
+      if (++polls > flag_polls) {
+        // A row at this segment's destination may still be unread: skip the
+        // stores (the destination keeps its old contents) and record it.
         atomicExch(&ctrl[1], 1);
-        break;
+        return;
       }
       __nanosleep(64);
     }
@@ -571,7 +585,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     const int32_t* __restrict__ kept_count, const int32_t* __restrict__ seg_dep,
     const int32_t* __restrict__ old_bt, const int32_t* __restrict__ new_bt, int MB, int max_len, int BS,
     int nseg, int total_rows, uint8_t* __restrict__ pages, int KVH, int64_t page_bytes, int* ctrl, int* flags,
-    int seg_stride) {
+    int seg_stride, uint32_t flag_polls, int withhold_flags) {
   constexpr int G = D / 64;
   constexpr int CB = D / 2;       // code row bytes
   constexpr int LPR = CB / 16;    // lanes per code row (16 bytes each)
@@ -588,7 +602,7 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   const int64_t rb = static_cast<int64_t>(b) * max_len;
   int* my_flag = flags + static_cast<int64_t>(b) * seg_stride + row;
   if (src_ord[rb + row] == row) {  // already in place
-    if (lane == 0) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+    if (lane == 0 && !withhold_flags) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
     return;
   }
   const int t = kept_idx[rb + row];
@@ -622,27 +636,31 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
+  int gave_up = 0;
   if (lane == 0) {
     __threadfence();
-    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+    if (!withhold_flags) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
     // Wait until the row that lives at this row's destination has been read.
     const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + row];
-    for (int m = d; m < row && m <= d + 1; ++m) {
+    for (int m = d; m < row && m <= d + 1 && !gave_up; ++m) {
       const int* f = flags + static_cast<int64_t>(b) * seg_stride + m;
       uint32_t polls = 0;
       int v = 0;
       while (true) {
         asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
         if (v) break;
-        if (++polls > kMaxPolls) {
+        if (++polls > flag_polls) {
           atomicExch(&ctrl[1], 1);
+          gave_up = 1;
           break;
         }
         __nanosleep(64);
       }
     }
   }
-  __syncwarp();
+  // After a give-up the row is not stored: its destination may still hold an
+  // unread kept row.
+  if (__shfl_sync(0xffffffffu, gave_up, 0)) return;
   for (int h = hs; h < KVH; h += HPI) {
     uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
     const uint4 kv = *reinterpret_cast<const uint4*>(stage + (2 * h) * CB + 16 * c);
@@ -768,6 +786,8 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
     MEMOPT_LAUNCH_CHECK("topk_select_big_kernel launch");
   }
   const int nseg = (max_len + kSegRows - 1) / kSegRows;
+  const uint32_t polls = g_flag_polls.load(std::memory_order_relaxed);
+  const int withhold = g_withhold_flags.load(std::memory_order_relaxed);
   if (int4) {
     const int64_t pb = static_cast<int64_t>(block_size) * head_dim + static_cast<int64_t>(block_size) * (head_dim / 64) * 4;
     uint8_t* pages = static_cast<uint8_t*>(key_pool);
@@ -782,18 +802,19 @@ static int topk_compact(const char* who, bool int4, const float* src, int64_t b_
     if (head_dim == 128)
       move_rows_int4_kernel<128><<<grid4, 32 * kMoveWarps, smem4, s>>>(
           kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
-          rows_total, pages, num_heads, pb, ctrl, flags, max_len);
+          rows_total, pages, num_heads, pb, ctrl, flags, max_len, polls, withhold);
     else
       move_rows_int4_kernel<64><<<grid4, 32 * kMoveWarps, smem4, s>>>(
           kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg,
-          rows_total, pages, num_heads, pb, ctrl, flags, max_len);
+          rows_total, pages, num_heads, pb, ctrl, flags, max_len, polls, withhold);
     MEMOPT_LAUNCH_CHECK("move_rows_int4_kernel launch");
     return MEMOPT_OK;
   }
   const int segs = num_seqs * nseg;
   move_rows_inplace_kernel<<<(segs + kMoveWarps16 - 1) / kMoveWarps16, 32 * kMoveWarps16, stage_bytes, s>>>(
       kept_idx, ord, kept_count, dep, old_bt, block_tables, max_blocks_per_seq, max_len, block_size, nseg, segs,
-      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags, max_len);
+      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), row_bytes, ctrl, flags, max_len, polls,
+      withhold);
   MEMOPT_LAUNCH_CHECK("move_rows_inplace_kernel launch");
   return MEMOPT_OK;
 }
@@ -844,6 +865,33 @@ extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_compact_
                       num_heads, num_seqs, num_heads, max_len, block_tables, max_blocks_per_seq, context_lens, kv_pages,
                       nullptr, pool_num_blocks, block_size, head_dim, retain_ratio, num_sink_tokens, kept_idx,
                       kept_count, freed_pages, freed_count, workspace, workspace_bytes, stream);
+}
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_set_test_hooks(uint32_t flag_poll_limit,
+                                                                                      int withhold_read_flags) {
+  g_flag_polls.store(flag_poll_limit == 0 ? kMaxPolls : flag_poll_limit, std::memory_order_relaxed);
+  g_withhold_flags.store(withhold_read_flags ? 1 : 0, std::memory_order_relaxed);
+  return MEMOPT_OK;
+}
+
+extern "C" __attribute__((visibility("default"))) int memopt_evict_topk_status(const void* workspace, int num_seqs,
+                                                                              int max_len, void* stream) {
+  if (num_seqs < 0 || max_len < 0) return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_status: invalid geometry");
+  if (num_seqs == 0 || max_len == 0) return MEMOPT_OK;
+  if (!workspace) return fail(MEMOPT_ERR_INVALID_ARG, "evict_topk_status: null workspace");
+  size_t o_sums, o_ord, o_dep, o_flags, o_ctrl;
+  topk_ws_layout(num_seqs, max_len, &o_sums, &o_ord, &o_dep, &o_flags, &o_ctrl);
+  int ctrl1 = 0;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemcpyAsync(&ctrl1, static_cast<const uint8_t*>(workspace) + o_ctrl + 4, 4,
+                                  cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "evict_topk_status: reading the status word");
+  if (ctrl1 != 0)
+    return fail(MEMOPT_ERR_TIMEOUT,
+                "evict_topk: a row move gave up waiting; rows whose wait ran out were not stored, so the pool, "
+                "block tables and lengths are only partly compacted (no kept row was overwritten before it was read)");
+  return MEMOPT_OK;
 }
 
 }  // namespace memopt

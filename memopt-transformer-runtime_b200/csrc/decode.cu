@@ -367,6 +367,23 @@ int zero_output(void* out, int batch, int q_len, int H, int D, void* stream) {
 }
 
 }  // namespace
+
+int validate_attention_f16(const void* query, const void* key_pool, const void* value_pool, int batch, int q_len,
+                           int H, int KVH, int D, int MB, int64_t NB, int BS, const void* out) {
+  if (batch < 0 || q_len < 0 || H < 0 || D < 0 || MB < 0 || NB < 0)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: negative size");
+  if (KVH <= 0 || (H > 0 && H % KVH != 0))
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: num_kv_heads must divide num_heads");
+  if (!((BS == 16 || BS == 32) && (D == 64 || D == 128))) return unsupported(BS, D);
+  if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: query/out must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(key_pool) | reinterpret_cast<uintptr_t>(value_pool)) & 15u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention: pools must be 16-byte aligned");
+  if (NB * BS > 0x7fffffffLL)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "dynamic_sparse_attention: pool has more than 2^31 token rows");
+  return MEMOPT_OK;
+}
+
 }  // namespace memopt
 
 using namespace memopt;

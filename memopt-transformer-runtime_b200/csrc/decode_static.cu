@@ -14,8 +14,12 @@
 //   * a call whose split-K scratch would exceed it is rejected with
 //     MEMOPT_ERR_WORKSPACE before any work is queued;
 //   * the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (once per device, with that device current); make
-//     that first call before any stream capture;
+//     cudaGetSymbolAddress (once per device, with that device current).  CUDA
+//     loads modules lazily, so that first call is also when the array's
+//     4 MiB are committed on the device, and it can fail with out-of-memory;
+//     make that first call at start-up, before any stream capture;
+//   * arguments are validated before the scratch is touched: a rejected call
+//     queues no work;
 //   * every call shares the one array: calls that overlap on the GPU (e.g. on
 //     two streams without ordering between them) race.  The ticket region,
 //     which must start at zero, is cleared at the start of every call.
@@ -69,6 +73,11 @@ extern "C" int memopt_paged_attention_f16_noalloc(const void* query, const void*
                                                   int num_heads, int head_dim, int max_blocks_per_seq,
                                                   int64_t num_blocks, int block_size, int max_seq_len,
                                                   int window_size, void* out, void* stream) {
+  // Arguments are checked before the shared scratch is touched, so a call
+  // that is rejected queues nothing.
+  const int vst = validate_attention_f16(query, key_pool, value_pool, batch, q_len, num_heads, num_heads, head_dim,
+                                         max_blocks_per_seq, num_blocks, block_size, out);
+  if (vst != MEMOPT_OK) return vst;
   const size_t need = memopt_paged_attention_workspace_size(batch, q_len, num_heads, head_dim,
                                                             max_blocks_per_seq, block_size, max_seq_len,
                                                             window_size);

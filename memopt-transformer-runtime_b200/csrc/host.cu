@@ -72,6 +72,7 @@ const char* memopt_status_string(int status) {
     case MEMOPT_ERR_CUDA: return "CUDA error";
     case MEMOPT_ERR_OUT_OF_RANGE: return "out of range";
     case MEMOPT_ERR_WORKSPACE: return "workspace too small";
+    case MEMOPT_ERR_TIMEOUT: return "a bounded device wait ran out";
     default: return "unknown status";
   }
 }

@@ -59,6 +59,24 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return d;
 }
 
+// absmax / 7 for a finite absmax m >= 0 without the division routine:
+// q0 = m * fp32(1/7) followed by one residual correction step
+// q = fma(fma(-q0, 7, m), fp32(1/7), q0) (Markstein's correction for
+// division by a constant: P. Markstein, "IA-64 and Elementary Functions",
+// Prentice Hall 2000, ch. 8) is the correctly rounded quotient for every
+// finite fp16 value m (checked exhaustively over all 31743 positive finite
+// fp16 values against the IEEE fp32 quotient; m is the max of |fp16| inputs).
+// 1.0 for an all-zero group, as in the reference.
+__device__ __forceinline__ float int4_scale_div7(float m) {
+  float scale = 1.0f;
+  if (m > 0.f) {
+    const float r7 = 0.142857149f;  // fp32(1/7)
+    const float q0 = __fmul_rn(m, r7);
+    scale = __fmaf_rn(__fmaf_rn(-q0, 7.0f, m), r7, q0);
+  }
+  return scale;
+}
+
 // The lane's 8 codes of a group of 64 (8 lanes per group, all present) and
 // the group's scale, bit-identical to int4_scale_from_absmax(group8_absmax)
 // and int4_code.  Groups holding a NaN or an infinity take that exact path.
@@ -86,17 +104,7 @@ __device__ __forceinline__ uint32_t int4_quant8(const float f[8], float& scale_o
     for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
     return w;
   }
-  // absmax / 7 without the division routine: q0 = m * fp32(1/7) corrected by one
-  // fma step is the correctly rounded quotient for every finite fp16 value m
-  // (checked exhaustively over all 31743 positive finite fp16 values against
-  // the IEEE fp32 quotient; m is the max of fp16 inputs, and NaN/inf groups
-  // took the path above).
-  float scale = 1.0f;
-  if (m > 0.f) {
-    const float r7 = 0.142857149f;  // fp32(1/7)
-    const float q0 = __fmul_rn(m, r7);
-    scale = __fmaf_rn(__fmaf_rn(-q0, 7.0f, m), r7, q0);
-  }
+  const float scale = int4_scale_div7(m);
   scale_out = scale;
   const float rinv = rcp_approx(scale);
   uint32_t u[8];
@@ -121,6 +129,78 @@ __device__ __forceinline__ uint32_t int4_quant8(const float f[8], float& scale_o
     for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
   }
   return w;
+}
+
+// The lane's 16 codes of a group of 64 shared by 4 consecutive lanes (16
+// elements each, given as two 16-byte vectors a, b in element order) and the
+// group's scale, bit-identical to int4_scale_from_absmax(absmax) and
+// int4_code.  Returned as two code words (byte i = code 2i | code 2i+1 << 4).
+// The group max is taken on the fp16 pairs (exact; NaN propagates), a group
+// holding a NaN or an infinity takes the reference path.  Otherwise, with
+// q = x * rcp(scale) (within 2e-6 of x / scale, |q| <= 7 + rounding),
+// q + (2^23 + 8) rounded to nearest puts 8 + rint(q) in the low byte of its
+// bit pattern; rint (ties to even) and the reference's roundf (ties away)
+// of x / scale can only differ when q is within 1.6e-5 of a half-integer,
+// which |q - rint(q)| shows, and then the lane recomputes its codes with the
+// exact division.  Bytes are gathered with byte permutes and the two nibbles
+// of each output byte joined by one shift-add.
+__device__ __forceinline__ uint2 int4_quant16(const uint4& a, const uint4& b, float& scale_out) {
+  const __half2* ha = reinterpret_cast<const __half2*>(&a);
+  const __half2* hb = reinterpret_cast<const __half2*>(&b);
+  __half2 m2 = __habs2(ha[0]);
+#pragma unroll
+  for (int i = 1; i < 4; ++i) m2 = __hmax2_nan(m2, __habs2(ha[i]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m2 = __hmax2_nan(m2, __habs2(hb[i]));
+  float m = fmax_nan(__low2float(m2), __high2float(m2));
+  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  float f[16];
+  unpack_half8(a, f);
+  unpack_half8(b, f + 8);
+  uint32_t w0 = 0, w1 = 0;
+  if (!(m < INFINITY)) {  // NaN or inf in the group (uniform over its 4 lanes)
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) am = fmaxf(am, fabsf(f[j]));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    const float scale = int4_scale_from_absmax(am);
+    scale_out = scale;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w0 |= int4_code(f[j], scale) << (4 * j);
+      w1 |= int4_code(f[8 + j], scale) << (4 * j);
+    }
+    return make_uint2(w0, w1);
+  }
+  const float scale = int4_scale_div7(m);
+  scale_out = scale;
+  const float rinv = rcp_approx(scale);
+  constexpr float kMagic = 8388616.0f;  // 2^23 + 8
+  uint32_t u[16];
+  float dmax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float q = __fmul_rn(f[j], rinv);
+    const float t = __fadd_rn(q, kMagic);
+    u[j] = __float_as_uint(t);
+    dmax = fmaxf(dmax, fabsf(__fsub_rn(q, __fsub_rn(t, kMagic))));
+  }
+  if (dmax >= 0.5f - 1.6e-5f) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w0 |= int4_code(f[j], scale) << (4 * j);
+      w1 |= int4_code(f[8 + j], scale) << (4 * j);
+    }
+    return make_uint2(w0, w1);
+  }
+  // low byte of u[j] = code j
+  const uint32_t e0 = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
+  const uint32_t o0 = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
+  const uint32_t e1 = __byte_perm(__byte_perm(u[8], u[10], 0x0040), __byte_perm(u[12], u[14], 0x0040), 0x5410);
+  const uint32_t o1 = __byte_perm(__byte_perm(u[9], u[11], 0x0040), __byte_perm(u[13], u[15], 0x0040), 0x5410);
+  return make_uint2((o0 << 4) + e0, (o1 << 4) + e1);
 }
 
 // INT4 page layout helpers (one page per (block, head)):

@@ -16,6 +16,7 @@
 #include <c10/cuda/CUDAStream.h>
 
 #include <cstdlib>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -333,6 +334,8 @@ pybind11::tuple evict_topk_compact(torch::Tensor attention_scores, torch::Tensor
                                     cur_stream()),
           "evict_topk_compact");
   }
+  // Synchronises: a row move whose bounded wait ran out is an error here.
+  check(memopt_evict_topk_status(ws.data_ptr(), S, L, cur_stream()), "evict_topk_compact");
   return pybind11::make_tuple(kept, cnt, freed, fcnt);
 }
 
@@ -396,6 +399,7 @@ pybind11::tuple evict_topk_compact_parts(torch::Tensor partial_sums, torch::Tens
                                         cnt.data_ptr<int32_t>(), freed.data_ptr<int32_t>(),
                                         fcnt.data_ptr<int32_t>(), ws.data_ptr(), wsb, cur_stream()),
         "evict_topk_compact_parts");
+  check(memopt_evict_topk_status(ws.data_ptr(), S, L, cur_stream()), "evict_topk_compact_parts");
   return pybind11::make_tuple(kept, cnt, freed, fcnt);
 }
 
@@ -419,18 +423,49 @@ void attn_checks(const torch::Tensor& query, const torch::Tensor& block_tables, 
   TORCH_CHECK(query.size(3) <= 128, "head_dim ", query.size(3), " must be <= ATTN_BLOCK_DIM (128)");
 }
 
-// Split-K scratch from the caching allocator; only the ticket prefix is zeroed.
+// Split-K scratch, cached per (device, stream) so that a decode step does no
+// allocation and no clearing: the kernels leave the ticket prefix of the
+// workspace zero when they finish, so it is cleared only when the buffer is
+// new or when a call needs more ticket bytes than the previous call on that
+// stream left zero (the previous call's partials follow its own tickets).
+// Calls on one stream are ordered, so they can share the buffer; a failed
+// call drops the entry (its tickets may not have been reset).
+struct WsEntry {
+  torch::Tensor buf;
+  size_t zero_tickets = 0;  // bytes at the start known to be zero
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, WsEntry> g_ws;
+
 torch::Tensor attn_workspace(const torch::Tensor& query, int KVH, int MB, int BS, int max_seq_len,
                              int window_size, size_t* bytes) {
   const int B = static_cast<int>(query.size(0)), QL = static_cast<int>(query.size(1));
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
   *bytes = memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, max_seq_len, window_size);
   if (*bytes == 0) return torch::Tensor();
-  auto ws = torch::empty({static_cast<int64_t>(*bytes)},
-                         torch::TensorOptions().dtype(torch::kUInt8).device(query.device()));
   const size_t tb = memopt_paged_attention_ticket_bytes(B, QL, H);
-  C10_CUDA_CHECK(cudaMemsetAsync(ws.data_ptr(), 0, tb, at::cuda::getCurrentCUDAStream().stream()));
-  return ws;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  WsEntry& e = g_ws[{static_cast<int>(query.get_device()), st}];
+  if (!e.buf.defined() || static_cast<size_t>(e.buf.numel()) < *bytes) {
+    e.buf = torch::empty({static_cast<int64_t>(*bytes)},
+                         torch::TensorOptions().dtype(torch::kUInt8).device(query.device()));
+    e.zero_tickets = 0;
+  }
+  if (tb > e.zero_tickets) C10_CUDA_CHECK(cudaMemsetAsync(e.buf.data_ptr(), 0, tb, st));
+  e.zero_tickets = tb;
+  return e.buf;
+}
+
+void drop_workspace(const torch::Tensor& query) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  g_ws.erase({static_cast<int>(query.get_device()), at::cuda::getCurrentCUDAStream().stream()});
+}
+
+// Attention status check that forgets the stream's cached workspace first.
+void check_attn(int st, const char* what, const torch::Tensor& query) {
+  if (st != MEMOPT_OK) drop_workspace(query);
+  check(st, what);
 }
 
 }  // namespace
@@ -467,11 +502,11 @@ torch::Tensor dynamic_sparse_attention(torch::Tensor query, torch::Tensor key_ca
   auto q = aligned_contig(query);
   size_t wsb = 0;
   auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb);
-  check(memopt_paged_attention_f16_ex(q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+  check_attn(memopt_paged_attention_f16_ex(q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
                                       block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(), B, QL, H,
                                       KVH, D, MB, key_cache.size(0), BS, max_seq_len, window_size, causal ? 1 : 0,
                                       out.data_ptr(), wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
-        "dynamic_sparse_attention");
+             "dynamic_sparse_attention", q);
   return out;
 }
 
@@ -498,11 +533,11 @@ torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor k
   auto q = aligned_contig(query);
   size_t wsb = 0;
   auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb);
-  check(memopt_paged_attention_int4_ex(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
+  check_attn(memopt_paged_attention_int4_ex(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
                                        context_lens.data_ptr<int32_t>(), B, QL, H, KVH, D, MB, kv_pages.size(0), BS,
                                        max_seq_len, window_size, causal ? 1 : 0, out.data_ptr(),
                                        wsb ? ws.data_ptr() : nullptr, wsb, cur_stream()),
-        "dynamic_sparse_attention_int4");
+             "dynamic_sparse_attention_int4", q);
   return out;
 }
 
@@ -560,6 +595,10 @@ torch::Tensor dequantize_kv_cache_int4(torch::Tensor q_cache, torch::Tensor scal
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   namespace py = pybind11;
+  m.def("release_workspaces", [] {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    g_ws.clear();
+  }, "Drop the split-K workspaces cached per (device, stream) by dynamic_sparse_attention");
   m.def("get_hello", &get_hello, "Initial handshake function for MemOpt C++ extension");
   m.def("init_pool", &init_pool, "Allocate the paged KV cache pool tensors on GPU and seed the free-list",
         py::arg("num_blocks"), py::arg("block_size"), py::arg("num_heads"), py::arg("head_dim"),

@@ -103,3 +103,34 @@ def evict_tokens(scores, bt, ibf, kpool, vpool, retain_ratio, num_sinks, idx, cn
         I(ibf.shape[0]), P(kpool.data_ptr()), P(vpool.data_ptr()), I(kpool.shape[0]), I(kpool.shape[1]),
         I(kpool.shape[3]), F(retain_ratio), I(num_sinks), P(idx.data_ptr() if idx is not None else 0),
         P(cnt.data_ptr() if cnt is not None else 0), P(stream)), "memopt_evict_tokens")
+
+
+def quantize_int4(x, packed, scales, stream):
+    check(lib().memopt_quantize_int4(P(x.data_ptr()), I64(x.numel()), I(64), P(packed.data_ptr()),
+                                     P(scales.data_ptr()), P(stream)), "memopt_quantize_int4")
+
+
+def dequantize_int4(packed, scales, out, stream):
+    check(lib().memopt_dequantize_int4(P(packed.data_ptr()), P(scales.data_ptr()), I64(out.numel()), I(64),
+                                       P(out.data_ptr()), P(stream)), "memopt_dequantize_int4")
+
+
+def write_cache_f16(keys, values, slots, kpool, vpool, stream):
+    T, H, D = keys.shape
+    check(lib().memopt_write_cache_f16(P(keys.data_ptr()), P(values.data_ptr()), P(slots.data_ptr()), I64(T), I(H),
+                                       I(D), P(kpool.data_ptr()), P(vpool.data_ptr()), I64(kpool.shape[0]),
+                                       I(kpool.shape[1]), P(0), P(stream)), "memopt_write_cache_f16")
+
+
+def write_cache_int4(keys, values, slots, pages, block_size, stream):
+    T, H, D = keys.shape
+    check(lib().memopt_write_cache_int4(P(keys.data_ptr()), P(values.data_ptr()), P(slots.data_ptr()), I64(T), I(H),
+                                        I(D), P(pages.data_ptr()), I64(pages.shape[0]), I(block_size), P(0),
+                                        P(stream)), "memopt_write_cache_int4")
+
+
+def evict_cache(scores, kpool, vpool, retain_ratio, stream):
+    NB, BS, H = scores.shape
+    check(lib().memopt_evict_cache(P(scores.data_ptr()), I(NB), I(BS), I(H), I(kpool.shape[3]),
+                                   P(kpool.data_ptr()), P(vpool.data_ptr()), F(retain_ratio), P(stream)),
+          "memopt_evict_cache")

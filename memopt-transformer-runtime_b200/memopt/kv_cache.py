@@ -120,11 +120,15 @@ class PagedKVCache:
 
     def __init__(self, num_blocks: int, num_heads: int, head_dim: int, block_size: int = 16,
                  kv_format: str = "fp16", device: Optional[torch.device] = None,
-                 eviction: str = "reference") -> None:
-        """``eviction``: "reference" runs ``evict_tokens`` (the reference's
-        semantics: per-head threshold, rows zeroed, no page released);
-        "exact" runs ``evict_topk_compact`` (one exact top-k per sequence
-        shared by all heads, kept rows compacted, emptied pages freed)."""
+                 eviction: str = "exact") -> None:
+        """``eviction``: "exact" (the default) runs ``evict_topk_compact``
+        (one exact top-k per sequence shared by all heads, sinks always
+        kept, kept rows compacted, emptied pages freed), so a scheduler
+        decision of ``retain_ratio < 1`` returns pages to the pool;
+        "reference" runs ``evict_tokens`` (the reference's semantics:
+        per-head threshold, rows zeroed, no page released; with sink tokens
+        its sink boost makes the bisection keep every token, so it frees
+        nothing)."""
         if eviction not in ("reference", "exact"):
             raise ValueError("eviction must be 'reference' or 'exact'")
         self.eviction = eviction

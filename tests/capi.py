@@ -122,7 +122,17 @@ def int4_page_bytes(block_size, head_dim):
     return int(lib().memopt_int4_page_bytes(I(block_size), I(head_dim)))
 
 
-def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
+def _topk_status(ws, S, L, status):
+    """memopt_evict_topk_status after a compaction: asserted OK, or appended
+    to ``status`` (a list) when the caller checks it itself."""
+    st = lib().memopt_evict_topk_status(ptr(ws), I(S), I(L), stream())
+    if status is None:
+        ok(st)
+    else:
+        status.append(st)
+
+
+def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks, status=None):
     S, H, L = scores.shape
     MB = bt.shape[1]
     dev = scores.device
@@ -137,10 +147,11 @@ def evict_topk_compact(scores, bt, ctx, kpool, vpool, retain_ratio, sinks):
                                        ptr(vpool), I(kpool.shape[0]), I(kpool.shape[1]), I(kpool.shape[3]),
                                        F(retain_ratio), I(sinks), ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt),
                                        ptr(ws), SZ(wsb), stream()))
+    _topk_status(ws, S, L, status)
     return kept, cnt, freed, fcnt
 
 
-def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain_ratio, sinks):
+def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain_ratio, sinks, status=None):
     S, H, L = scores.shape
     MB = bt.shape[1]
     dev = scores.device
@@ -154,6 +165,7 @@ def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain
     ok(lib().memopt_evict_topk_compact_int4(ptr(scores), I(S), I(H), I(L), ptr(bt), I(MB), ptr(ctx), ptr(pages),
                                             I(pages.shape[0]), I(block_size), I(head_dim), F(retain_ratio), I(sinks),
                                             ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt), ptr(ws), SZ(wsb), stream()))
+    _topk_status(ws, S, L, status)
     return kept, cnt, freed, fcnt
 
 
@@ -164,7 +176,7 @@ def evict_topk_head_sum(scores):
     return out
 
 
-def evict_topk_compact_parts(parts, bt, ctx, kpool, vpool, retain_ratio, sinks):
+def evict_topk_compact_parts(parts, bt, ctx, kpool, vpool, retain_ratio, sinks, status=None):
     G, S, L = parts.shape
     MB = bt.shape[1]
     dev = parts.device
@@ -180,6 +192,7 @@ def evict_topk_compact_parts(parts, bt, ctx, kpool, vpool, retain_ratio, sinks):
                                              ptr(vpool), I(kpool.shape[0]), I(kpool.shape[1]), I(H), I(D),
                                              F(retain_ratio), I(sinks), ptr(kept), ptr(cnt), ptr(freed), ptr(fcnt),
                                              ptr(ws), SZ(wsb), stream()))
+    _topk_status(ws, S, L, status)
     return kept, cnt, freed, fcnt
 
 
@@ -204,3 +217,7 @@ def attention_int4_ex(q, pages, block_size, bt, ctx, msl, win, causal=False):
                                             I(pages.shape[1]), I(D), I(MB), I64(pages.shape[0]), I(block_size),
                                             I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))
     return out
+
+
+def evict_topk_set_test_hooks(flag_poll_limit: int, withhold_read_flags: bool) -> None:
+    ok(lib().memopt_evict_topk_set_test_hooks(C.c_uint32(flag_poll_limit), I(int(withhold_read_flags))))

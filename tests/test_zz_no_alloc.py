@@ -77,3 +77,18 @@ def test_noalloc_rejects_oversized_calls():
     st = _noalloc(q, kp, kp, bt, cl, MB * BS, MB * BS, out)
     assert st == -6  # MEMOPT_ERR_WORKSPACE
     assert b"static scratch" in lib.memopt_last_error()
+
+
+def test_noalloc_rejects_bad_arguments_before_touching_the_scratch():
+    """A call with invalid arguments fails before any work is queued (so it
+    cannot clear the tickets of another call that is using the scratch)."""
+    q, kp, vp, bt, cl, msl = _case(2, 8, 128, 16, [300, 200], 9)
+    out = torch.empty_like(q)
+    lib = capi.lib()
+    bad = kp.view(-1)[1:]  # a pool pointer 2 bytes off alignment
+    st = lib.memopt_paged_attention_f16_noalloc(
+        capi.ptr(q), capi.ptr(bad), capi.ptr(vp), capi.ptr(bt), capi.ptr(cl), C.c_int(2), C.c_int(1), C.c_int(8),
+        C.c_int(128), C.c_int(bt.shape[1]), C.c_int64(kp.shape[0]), C.c_int(16), C.c_int(msl), C.c_int(msl),
+        capi.ptr(out), capi.stream())
+    assert st == -1  # MEMOPT_ERR_INVALID_ARG
+    assert b"16-byte aligned" in lib.memopt_last_error()
