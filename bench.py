@@ -195,6 +195,24 @@ def make_prefill_workload(torch, dev, rank: int = 0, batch: int = PREFILL_B):
     return kp, vp, bt, q, ctx
 
 
+def time_e2e(torch, loop, steps: int, warmup: int, barrier, stream, copy_stream):
+    """time_loop for the pipelined end-to-end step: the copy stream starts
+    after the start event, and the end event follows the last step's
+    device->host copy."""
+    loop(warmup)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    copy_stream.wait_stream(stream)
+    loop(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / steps
+
+
 def time_loop(torch, fn, steps: int, warmup: int, barrier, stream):
     for _ in range(warmup):
         fn()
@@ -388,19 +406,46 @@ def run_ours(args) -> None:
     dbt = torch.empty_like(hbt, device=dev)
     dctx = torch.empty_like(hctx, device=dev)
 
+    # Serving-style pipeline: the step's host->device copies run on a copy
+    # stream into one of two device buffer sets while the previous step's
+    # attention runs, and its output goes back on a second copy stream; the
+    # compute stream waits for the step's inputs.  Every copy of every step
+    # is inside the timed region.
+    dq, dk, dv, ds, dbt, dctx = [[x, torch.empty_like(x)] for x in (dq, dk, dv, ds, dbt, dctx)]
+    houts = [hout, torch.empty_like(hout).pin_memory()]
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    freed = [torch.cuda.Event(), torch.cuda.Event()]  # buffer set i no longer read by compute
+    for e in freed:
+        e.record(stream)
+    it = [0]
+
     def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        ds.copy_(hslots, non_blocking=True)
-        dbt.copy_(hbt, non_blocking=True)
-        dctx.copy_(hctx, non_blocking=True)
-        memopt_C.write_cache(dk, dv, dbt, ds)
-        o = memopt_C.dynamic_sparse_attention(dq, pk, pv, dbt, dctx, CTX, CTX)
-        hout.copy_(o, non_blocking=True)
+        i = it[0] & 1
+        it[0] += 1
+        with torch.cuda.stream(h2d_s):
+            h2d_s.wait_event(freed[i])
+            for d_, h_ in ((dq, hq), (dk, hk), (dv, hv), (ds, hslots), (dbt, hbt), (dctx, hctx)):
+                d_[i].copy_(h_, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(h2d_s)
+        stream.wait_event(ready)
+        memopt_C.write_cache(dk[i], dv[i], dbt[i], ds[i])
+        o = memopt_C.dynamic_sparse_attention(dq[i], pk, pv, dbt[i], dctx[i], CTX, CTX)
+        done = torch.cuda.Event()
+        done.record(stream)
+        freed[i].record(stream)
+        with torch.cuda.stream(d2h_s):
+            d2h_s.wait_event(done)
+            houts[i].copy_(o, non_blocking=True)
+            o.record_stream(d2h_s)
+
+    def e2e_loop(n):
+        for _ in range(n):
+            e2e_step()
+        stream.wait_stream(d2h_s)  # the last outputs are on the host before the end event
 
     e2e_steps = max(1, min(args.steps, 500))
-    ms_e2e = max_over_ranks(time_loop(torch, e2e_step, e2e_steps, args.warmup, barrier, stream))
+    ms_e2e = max_over_ranks(time_e2e(torch, e2e_loop, e2e_steps, args.warmup, barrier, stream, h2d_s))
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hslots, hbt, hctx))
     d2h = hout.numel() * hout.element_size()
     e2e = job_rate(sbytes, ms_e2e, ws_n) / 1e9
@@ -449,7 +494,8 @@ def run_ours(args) -> None:
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(ms_e2e, 5), "steps": e2e_steps,
-                "path": "memopt_C.write_cache + memopt_C.dynamic_sparse_attention, pinned host buffers"},
+                "path": "memopt_C.write_cache + memopt_C.dynamic_sparse_attention, pinned host buffers; each step's "
+                        "copies overlap the previous step's attention (two buffer sets, two copy streams)"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
         "extra": extra,

@@ -77,6 +77,40 @@ int memopt_pool_free_block(int block_idx);
 int memopt_pool_free_blocks_count(void);
 
 /* ------------------------------------------------------------------------ */
+/* Pages spread over several GPUs (no reference counterpart: the reference's  */
+/* pool lives on one device, kv_cache.cu:97 and README "Future Work").  A     */
+/* page is (owner device, block).  Host-side, process-wide; every rank of an  */
+/* SPMD job makes the same calls and so holds the same state.                 */
+/* ------------------------------------------------------------------------ */
+
+/* One FIFO free-list per device with blocks 0..blocks_per_device[d]-1. */
+int memopt_mdpool_init(int num_devices, const int* blocks_per_device);
+void memopt_mdpool_reset(void);
+/* Oldest free block of preferred_device, else of the device with the most
+ * free blocks (lowest index on ties); writes the owner to *device_out.
+ * Returns the block, -1 when every device is exhausted, or an error code. */
+int memopt_mdpool_allocate(int preferred_device, int* device_out);
+/* Returns a block to its device's free-list (INVALID_ARG if already free). */
+int memopt_mdpool_free(int device, int block);
+int memopt_mdpool_free_count(int device);
+/* Gather plan of n pages (page_dev/page_blk; blk < 0 = no page) for
+ * home_device: local_blk[i] is the block to read on the home device: its own
+ * block for pages it owns, else a staging block staging_base + k.  Each
+ * distinct remote page gets one copy k (copy_src_dev/blk -> copy_dst_blk),
+ * grouped by owner in device order, so the pages of one owner land in
+ * consecutive staging blocks.  Copy arrays hold up to n entries.
+ * MEMOPT_ERR_WORKSPACE when more than staging_capacity pages are remote. */
+int memopt_mdpool_plan(const int32_t* page_dev, const int32_t* page_blk, int n, int home_device,
+                       int staging_base, int staging_capacity, int32_t* local_blk, int32_t* copy_src_dev,
+                       int32_t* copy_src_blk, int32_t* copy_dst_blk, int* n_copies);
+/* Device page copy on the current device: dst[dst_ids[i]] = src[src_ids[i]]
+ * for num_pages pages of page_bytes (a multiple of 16) each; NULL ids mean
+ * 0..num_pages-1 (a packed buffer); negative ids are skipped.  Packs pages
+ * for a transfer between GPUs and unpacks them. */
+int memopt_copy_pages(const void* src_pool, const int32_t* src_ids, void* dst_pool, const int32_t* dst_ids,
+                      int num_pages, int64_t page_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* write_cache (kv_cache.cu:228-348).                                         */
 /* keys/values: fp16 [num_tokens, num_heads, head_dim], contiguous.           */
 /* slot_mapping: int32 [num_tokens], slot = block * block_size + position.    */

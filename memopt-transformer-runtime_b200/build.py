@@ -20,7 +20,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 LIB = os.path.join(PKG, "libmemopt_b200.so")
 EXT = os.path.join(PKG, "memopt_C.so")
-CU_SOURCES = ["host.cu", "quant.cu", "write_cache.cu", "evict.cu", "decode.cu", "decode_static.cu", "prefill.cu", "compact.cu"]
+CU_SOURCES = ["host.cu", "quant.cu", "write_cache.cu", "evict.cu", "decode.cu", "decode_static.cu", "prefill.cu", "compact.cu", "mdpool.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",

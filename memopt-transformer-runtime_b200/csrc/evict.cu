@@ -244,6 +244,74 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   }
 }
 
+// One warp per physical block: its lanes first find, per head, the rows to
+// zero (the keep-th largest score by repeated arg-max, as below) as a row
+// bit mask in shared memory, then zero the marked rows of all heads with
+// 16-byte stores that cover each token row ([head][dim], contiguous) in
+// order, so every store instruction writes 512 contiguous bytes.  Needs
+// head_dim % 8 == 0 and 16-byte aligned pools.
+constexpr int kEvictCacheWarps = 8;
+
+template <int BS>
+__global__ void __launch_bounds__(kEvictCacheWarps * 32)
+evict_cache_rows_kernel(const float* __restrict__ scores, int num_blocks, int num_heads, int head_dim,
+                        uint4* __restrict__ kpool, uint4* __restrict__ vpool, float retain_ratio) {
+  extern __shared__ uint32_t row_masks_all[];  // kEvictCacheWarps x num_heads
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  uint32_t* masks = row_masks_all + w * num_heads;
+  const int cph = head_dim / 8;        // 16-byte chunks per head row
+  const int cpr = num_heads * cph;     // per token row
+  int keep = max(1, static_cast<int>(retain_ratio * static_cast<float>(BS)));
+  keep = min(keep, BS);
+  for (int64_t blk = static_cast<int64_t>(blockIdx.x) * kEvictCacheWarps + w; blk < num_blocks;
+       blk += static_cast<int64_t>(gridDim.x) * kEvictCacheWarps) {
+    uint32_t any = 0;
+    for (int h = lane; h < num_heads; h += 32) {
+      float s[BS], wv[BS];
+#pragma unroll
+      for (int p = 0; p < BS; ++p) {
+        s[p] = __ldg(scores + (blk * BS + p) * num_heads + h);
+        wv[p] = s[p];
+      }
+      float thr = -1e38f;
+      for (int k = 0; k < keep; ++k) {
+        float best = -1e38f;
+        int best_pos = -1;
+#pragma unroll
+        for (int p = 0; p < BS; ++p) {
+          if (wv[p] > best) {
+            best = wv[p];
+            best_pos = p;
+          }
+        }
+        thr = best;
+#pragma unroll
+        for (int p = 0; p < BS; ++p)
+          if (p == best_pos) wv[p] = -1e38f;
+      }
+      uint32_t m = 0;
+#pragma unroll
+      for (int p = 0; p < BS; ++p) m |= (s[p] < thr) ? (1u << p) : 0u;
+      masks[h] = m;
+      any |= m;
+    }
+    any = __reduce_or_sync(0xffffffffu, any);
+    __syncwarp();
+    for (int p = 0; p < BS; ++p) {
+      if (!((any >> p) & 1u)) continue;
+      const int64_t base = (blk * BS + p) * cpr;
+      for (int c = lane; c < cpr; c += 32) {
+        if ((masks[c / cph] >> p) & 1u) {
+          kpool[base + c] = make_uint4(0, 0, 0, 0);
+          vpool[base + c] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // One thread per (physical block, head); heads fastest for coalesced reads.
 template <int BS>
 __global__ void __launch_bounds__(256)
@@ -398,7 +466,30 @@ extern "C" int memopt_evict_cache(const float* scores, int num_blocks, int block
   cudaStream_t s = as_stream(stream);
   __half* k = reinterpret_cast<__half*>(key_pool);
   __half* v = reinterpret_cast<__half*>(value_pool);
-  if (block_size == 16) {
+  const bool rows_ok = head_dim % 8 == 0 && num_heads <= 2048 &&
+                       ((reinterpret_cast<uintptr_t>(key_pool) | reinterpret_cast<uintptr_t>(value_pool)) & 15u) == 0;
+  if (rows_ok && (block_size == 16 || block_size == 32)) {
+    const int64_t want = (num_blocks + kEvictCacheWarps - 1) / kEvictCacheWarps;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    const int g = static_cast<int>(want < cap ? want : cap);
+    const size_t smem = static_cast<size_t>(kEvictCacheWarps) * num_heads * 4;
+    uint4* k4 = reinterpret_cast<uint4*>(key_pool);
+    uint4* v4 = reinterpret_cast<uint4*>(value_pool);
+    if (smem > 48 * 1024) {
+      cudaError_t e = block_size == 16
+                          ? cudaFuncSetAttribute(evict_cache_rows_kernel<16>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))
+                          : cudaFuncSetAttribute(evict_cache_rows_kernel<32>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return cuda_fail(e, "evict_cache: shared-memory attribute");
+    }
+    if (block_size == 16)
+      evict_cache_rows_kernel<16><<<g, kEvictCacheWarps * 32, smem, s>>>(scores, num_blocks, num_heads, head_dim,
+                                                                          k4, v4, retain_ratio);
+    else
+      evict_cache_rows_kernel<32><<<g, kEvictCacheWarps * 32, smem, s>>>(scores, num_blocks, num_heads, head_dim,
+                                                                          k4, v4, retain_ratio);
+  } else if (block_size == 16) {
     evict_cache_kernel<16><<<grid, 256, 0, s>>>(scores, num_blocks, num_heads, head_dim, k, v, retain_ratio);
   } else if (block_size == 32) {
     evict_cache_kernel<32><<<grid, 256, 0, s>>>(scores, num_blocks, num_heads, head_dim, k, v, retain_ratio);

@@ -6,8 +6,8 @@
 //   scale  = absmax > 0 ? absmax / 7.0f : 1.0f       (IEEE fp32 division)
 //   q      = clamp((int)roundf(x / scale) + 8, 0, 15) (roundf: ties away)
 //   byte i = q[2i] | q[2i+1] << 4                      (low nibble = even)
-// A group of 64 fp16 values is handled by 8 consecutive lanes, 8 values
-// (16 bytes) each; lanes 8k..8k+7 must all be present for the shuffles.
+// A group of 64 fp16 values is handled by 4 consecutive lanes, 16 values
+// (32 bytes) each; lanes 4k..4k+3 must all be present for the shuffles.
 #pragma once
 #include "common.cuh"
 
@@ -23,17 +23,6 @@ __device__ __forceinline__ void unpack_half8(const uint4& v, float f[8]) {
   }
 }
 
-// Max of |x| over the 8-lane group containing this lane.
-__device__ __forceinline__ float group8_absmax(const float f[8]) {
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-  return m;
-}
-
 __device__ __forceinline__ float int4_scale_from_absmax(float absmax) {
   return (absmax > 0.f) ? (absmax / 7.0f) : 1.0f;
 }
@@ -45,14 +34,33 @@ __device__ __forceinline__ uint32_t int4_code(float x, float scale) {
   return static_cast<uint32_t>(min(max(iq, 0), 15));
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): lane-wise IEEE round-to-nearest.
+__device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-// Max over the 8-lane group with NaN propagation: NaN if any element of the
-// group is NaN (fmaxf in group8_absmax would skip it).
+// Max with NaN propagation: NaN if either input is NaN (fmaxf would skip it).
 __device__ __forceinline__ float fmax_nan(float a, float b) {
   float d;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
@@ -77,71 +85,17 @@ __device__ __forceinline__ float int4_scale_div7(float m) {
   return scale;
 }
 
-// The lane's 8 codes of a group of 64 (8 lanes per group, all present) and
-// the group's scale, bit-identical to int4_scale_from_absmax(group8_absmax)
-// and int4_code.  Groups holding a NaN or an infinity take that exact path.
-// Otherwise |x / scale| <= 7 (+ rounding), and roundf(x / scale) =
-// sign(q) floor(|q| + 1/2) can differ from the value computed from
-// q = x * rcp(scale) (a few ulp of 8 away, < 3e-6) only when |q| + 1/2 is
-// within 1.6e-5 of an integer; so each code is sign(q) floor(|q| + 1/2) + 8
-// in [1, 15], built without float->int conversion or clamps:
-// copysign(k, q) + (8 + 2^23) puts the code in the low mantissa bits, and
-// byte permutes pack the nibbles.  If any of the lane's 8 quotients is near a
-// rounding boundary (| frac - 1/2 | >= 1/2 - 1.6e-5) its word is recomputed
-// with the exact division.
-__device__ __forceinline__ uint32_t int4_quant8(const float f[8], float& scale_out) {
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmax_nan(m, fabsf(f[i]));
-  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 4));
-  if (!(m < INFINITY)) {  // NaN or inf in the group (uniform over its 8 lanes): the reference path
-    const float scale = int4_scale_from_absmax(group8_absmax(f));
-    scale_out = scale;
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
-    return w;
-  }
-  const float scale = int4_scale_div7(m);
-  scale_out = scale;
-  const float rinv = rcp_approx(scale);
-  uint32_t u[8];
-  float dmax = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float q = f[j] * rinv;
-    const float t = fabsf(q) + 0.5f;
-    const float k = floorf(t);
-    dmax = fmaxf(dmax, fabsf((t - k) - 0.5f));
-    u[j] = __float_as_uint(copysignf(k, q) + 8388616.0f);  // 2^23 + 8 + code - 8
-  }
-  // nibble j = low 4 bits of u[j]
-  const uint32_t b01 = (u[0] & 0xFu) | ((u[1] & 0xFu) << 4);
-  const uint32_t b23 = (u[2] & 0xFu) | ((u[3] & 0xFu) << 4);
-  const uint32_t b45 = (u[4] & 0xFu) | ((u[5] & 0xFu) << 4);
-  const uint32_t b67 = (u[6] & 0xFu) | ((u[7] & 0xFu) << 4);
-  uint32_t w = __byte_perm(__byte_perm(b01, b23, 0x0040), __byte_perm(b45, b67, 0x0040), 0x5410);
-  if (dmax >= 0.5f - 1.6e-5f) {
-    w = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w |= int4_code(f[j], scale) << (4 * j);
-  }
-  return w;
-}
-
 // The lane's 16 codes of a group of 64 shared by 4 consecutive lanes (16
 // elements each, given as two 16-byte vectors a, b in element order) and the
 // group's scale, bit-identical to int4_scale_from_absmax(absmax) and
 // int4_code.  Returned as two code words (byte i = code 2i | code 2i+1 << 4).
 // The group max is taken on the fp16 pairs (exact; NaN propagates), a group
 // holding a NaN or an infinity takes the reference path.  Otherwise, with
-// q = x * rcp(scale) (within 2e-6 of x / scale, |q| <= 7 + rounding),
-// q + (2^23 + 8) rounded to nearest puts 8 + rint(q) in the low byte of its
+// q = x * rcp(scale) (exact product, within 2e-6 of x / scale, |q| <= 7 +
+// rounding), fma(x, rcp, 2^23 + 8) puts 8 + rint(q) in the low byte of its
 // bit pattern; rint (ties to even) and the reference's roundf (ties away)
 // of x / scale can only differ when q is within 1.6e-5 of a half-integer,
-// which |q - rint(q)| shows, and then the lane recomputes its codes with the
+// which |q - rint(q)| shows, and then those codes are recomputed with the
 // exact division.  Bytes are gathered with byte permutes and the two nibbles
 // of each output byte joined by one shift-add.
 __device__ __forceinline__ uint2 int4_quant16(const uint4& a, const uint4& b, float& scale_out) {
@@ -178,22 +132,36 @@ __device__ __forceinline__ uint2 int4_quant16(const uint4& a, const uint4& b, fl
   scale_out = scale;
   const float rinv = rcp_approx(scale);
   constexpr float kMagic = 8388616.0f;  // 2^23 + 8
+  constexpr float kNearHalf = 0.5f - 1.6e-5f;
   uint32_t u[16];
   float dmax = 0.f;
+  const uint64_t rinv2 = f32x2_pack(rinv, rinv), magic2 = f32x2_pack(kMagic, kMagic);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float q = __fmul_rn(f[j], rinv);
-    const float t = __fadd_rn(q, kMagic);
-    u[j] = __float_as_uint(t);
-    dmax = fmaxf(dmax, fabsf(__fsub_rn(q, __fsub_rn(t, kMagic))));
+  for (int j = 0; j < 16; j += 2) {
+    // Per element (two at a time, packed fp32 ops; each lane of a packed op
+    // rounds as the scalar one): t = RN(x rinv + 2^23 + 8) = 2^23 + 8 +
+    // rint(x rinv) (unit spacing there); d = RN(x rinv - rint(x rinv)), the
+    // distance to the chosen integer.
+    const uint64_t x2 = f32x2_pack(f[j], f[j + 1]);
+    const uint64_t t2 = f32x2_fma(x2, rinv2, magic2);
+    const uint64_t d2 = f32x2_fma(x2, rinv2, f32x2_sub(magic2, t2));
+    float t0, t1, d0, d1;
+    f32x2_unpack(t2, t0, t1);
+    f32x2_unpack(d2, d0, d1);
+    u[j] = __float_as_uint(t0);
+    u[j + 1] = __float_as_uint(t1);
+    dmax = fmaxf(dmax, fmaxf(fabsf(d0), fabsf(d1)));
   }
-  if (dmax >= 0.5f - 1.6e-5f) {
+  if (dmax >= kNearHalf) {
+    // Rare per lane (about 0.8% of lanes on N(0,1) data, mostly exact ties
+    // x / scale = n + 1/2), but it diverges the warp: only the flagged
+    // elements take the exact division, and the low byte of u[j] is patched.
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      w0 |= int4_code(f[j], scale) << (4 * j);
-      w1 |= int4_code(f[8 + j], scale) << (4 * j);
+    for (int j = 0; j < 16; ++j) {
+      const float t = __fmaf_rn(f[j], rinv, kMagic);
+      if (fabsf(__fmaf_rn(f[j], rinv, kMagic - t)) >= kNearHalf)
+        u[j] = (u[j] & 0xFFFFFF00u) | int4_code(f[j], scale);
     }
-    return make_uint2(w0, w1);
   }
   // low byte of u[j] = code j
   const uint32_t e0 = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);

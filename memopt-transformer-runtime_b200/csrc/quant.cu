@@ -12,30 +12,37 @@ namespace {
 
 constexpr int kQuantThreads = 256;
 
-// One lane = 8 consecutive elements (16 bytes in, 4 bytes of codes out).
+// One lane = 16 consecutive elements (32 bytes in, 8 bytes of codes out),
+// 4 lanes per group.
 __global__ void __launch_bounds__(kQuantThreads)
-quantize_int4_kernel(const uint4* __restrict__ in, uint32_t* __restrict__ codes,
-                     float* __restrict__ scales, int64_t num_chunks) {
+quantize_int4_kernel(const uint4* __restrict__ in, uint2* __restrict__ codes,
+                     float* __restrict__ scales, int64_t num_pairs) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   // Every lane of a warp runs the same number of iterations (the loop runs
   // over whole warps) so the group shuffles always see all 32 lanes.
   const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t warp_first = first & ~int64_t(31);
-  for (int64_t base = warp_first; base < num_chunks; base += stride) {
-    const int64_t c = base + (threadIdx.x & 31);
-    const bool live = c < num_chunks;
-    float f[8];
-    if (live) {
-      unpack_half8(ld_stream_v4(in + c), f);
-    } else {
+  // Two warp-strides per iteration: 64 bytes of loads in flight per lane.
+  for (int64_t base = warp_first; base < num_pairs; base += 2 * stride) {
+    uint4 a[2], b[2];
+    int64_t c[2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = 0.f;
+    for (int u = 0; u < 2; ++u) {
+      c[u] = base + u * stride + (threadIdx.x & 31);
+      a[u] = b[u] = make_uint4(0, 0, 0, 0);
+      if (c[u] < num_pairs) {
+        a[u] = ld_stream_v4(in + 2 * c[u]);
+        b[u] = ld_stream_v4(in + 2 * c[u] + 1);
+      }
     }
-    float scale;
-    const uint32_t w = int4_quant8(f, scale);
-    if (live) {
-      codes[c] = w;
-      if ((c & 7) == 0) scales[c >> 3] = scale;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float scale;
+      const uint2 w = int4_quant16(a[u], b[u], scale);
+      if (c[u] < num_pairs) {
+        codes[c[u]] = w;
+        if ((c[u] & 3) == 0) scales[c[u] >> 2] = scale;
+      }
     }
   }
 }
@@ -86,12 +93,12 @@ extern "C" int memopt_quantize_int4(const void* input_f16, int64_t numel, int gr
   if (numel == 0) return MEMOPT_OK;
   if (!input_f16 || !packed || !scales)
     return fail(MEMOPT_ERR_INVALID_ARG, "quantize_kv_cache_int4: null pointer");
-  if (!aligned16(input_f16) || (reinterpret_cast<uintptr_t>(packed) & 3u))
+  if (!aligned16(input_f16) || (reinterpret_cast<uintptr_t>(packed) & 7u))
     return fail(MEMOPT_ERR_INVALID_ARG,
-                "quantize_kv_cache_int4: input must be 16-byte aligned, packed 4-byte aligned");
-  const int64_t chunks = numel / 8;
-  quantize_int4_kernel<<<grid_for(chunks), kQuantThreads, 0, as_stream(stream)>>>(
-      reinterpret_cast<const uint4*>(input_f16), reinterpret_cast<uint32_t*>(packed), scales, chunks);
+                "quantize_kv_cache_int4: input must be 16-byte aligned, packed 8-byte aligned");
+  const int64_t pairs = numel / 16;
+  quantize_int4_kernel<<<grid_for(pairs), kQuantThreads, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint4*>(input_f16), reinterpret_cast<uint2*>(packed), scales, pairs);
   MEMOPT_LAUNCH_CHECK("quantize_int4_kernel launch");
   return MEMOPT_OK;
 }

@@ -86,15 +86,24 @@ __global__ void write_cache_f16_scalar_kernel(const __half* __restrict__ keys,
   }
 }
 
-// One warp per token; 8 lanes per 64-element group, 4 groups per warp step.
-__global__ void __launch_bounds__(kWarpsPerCta * 32)
+// One warp per token; 4 lanes per 64-element group (16 elements = two
+// 16-byte vectors each), 8 groups per warp step.  A lane stores 8 bytes of K
+// codes and 8 of V codes (a group's 32-byte code row is written whole by its
+// 4 lanes); the group's first lane stores the two fp16 scales.  head_dim is
+// a template parameter (64 or 128), so the group -> (head, group in head)
+// split is a shift; other multiples of 64 take D = 0 (run-time division).
+constexpr int kInt4WriteWarps = 8;
+
+template <int D>
+__global__ void __launch_bounds__(kInt4WriteWarps * 32, 3)
 write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict__ values,
                         const int32_t* __restrict__ slots, int64_t num_tokens, int num_heads,
-                        int head_dim, int block_size, int64_t num_slots,
+                        int head_dim_rt, int block_size, int64_t num_slots,
                         uint8_t* __restrict__ pages, int64_t page_bytes, int32_t* __restrict__ bad) {
+  const int head_dim = D > 0 ? D : head_dim_rt;
   const int lane = threadIdx.x & 31;
-  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kInt4WriteWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kInt4WriteWarps;
   const int gpr = head_dim / 64;                // groups per (token, head)
   const int chunks = num_heads * head_dim / 8;  // 16-byte chunks per token row
   const int64_t codes_bytes = static_cast<int64_t>(block_size) * (head_dim / 2);
@@ -109,45 +118,35 @@ write_cache_int4_kernel(const uint4* __restrict__ keys, const uint4* __restrict_
     const int pos = slot - static_cast<int32_t>(blk * block_size);
     const uint4* ksrc = keys + t * chunks;
     const uint4* vsrc = values + t * chunks;
-    // chunks is a multiple of 8 (head_dim % 64 == 0), so every warp step
-    // covers whole groups and all lanes take the same trip count.
-    for (int c0 = 0; c0 < chunks; c0 += 32 * 2) {
-      uint4 kv[2], vv[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < chunks) {
-          kv[u] = ld_stream_v4(ksrc + c);
-          vv[u] = ld_stream_v4(vsrc + c);
-        } else {
-          kv[u] = make_uint4(0, 0, 0, 0);
-          vv[u] = make_uint4(0, 0, 0, 0);
-        }
+    uint8_t* page0 = pages + blk * num_heads * page_bytes;
+    const int64_t row = static_cast<int64_t>(pos) * (head_dim / 2);
+    // chunks is a multiple of 8 (head_dim % 64 == 0): a group's 4 lanes are
+    // all live or all idle, and every lane runs the same trip count.
+    for (int c0 = 0; c0 < chunks; c0 += 64) {
+      const int c = c0 + 2 * lane;
+      uint4 ka = make_uint4(0, 0, 0, 0), kb = ka, va = ka, vb = ka;
+      if (c < chunks) {
+        ka = ld_stream_v4(ksrc + c);
+        kb = ld_stream_v4(ksrc + c + 1);
+        va = ld_stream_v4(vsrc + c);
+        vb = ld_stream_v4(vsrc + c + 1);
       }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = c0 + u * 32 + lane;
-        float fk[8], fv[8];
-        unpack_half8(kv[u], fk);
-        unpack_half8(vv[u], fv);
-        float sk, sv;
-        const uint32_t wk = int4_quant8(fk, sk);
-        const uint32_t wv = int4_quant8(fv, sv);
-        if (c < chunks) {
-          const int g = c >> 3;  // group within the token row
-          const int h = g / gpr;
-          const int gi = g - h * gpr;
-          uint8_t* page = pages + (blk * num_heads + h) * page_bytes;
-          const int byte = gi * 32 + (c & 7) * 4;  // logical byte of the row
-          const int64_t row = static_cast<int64_t>(pos) * (head_dim / 2);
-          *reinterpret_cast<uint32_t*>(page + row + byte) = wk;
-          *reinterpret_cast<uint32_t*>(page + codes_bytes + row + int4_vrow_swizzle(pos, byte, head_dim)) = wv;
-          if ((c & 7) == 0) {
-            __half* ks = reinterpret_cast<__half*>(page + 2 * codes_bytes);
-            __half* vs = reinterpret_cast<__half*>(page + 2 * codes_bytes + scale_bytes);
-            ks[pos * gpr + gi] = __float2half_rn(sk);
-            vs[int4_vscale_index(pos, gi, gpr)] = __float2half_rn(sv);
-          }
+      float sk, sv;
+      const uint2 wk = int4_quant16(ka, kb, sk);
+      const uint2 wv = int4_quant16(va, vb, sv);
+      if (c < chunks) {
+        const int g = c >> 3;  // group within the token row
+        const int h = D == 128 ? (g >> 1) : (D == 64 ? g : g / gpr);
+        const int gi = g - h * gpr;
+        uint8_t* page = page0 + h * page_bytes;
+        const int byte = gi * 32 + (c & 7) * 4;  // logical byte of the row (c even: 8-byte aligned)
+        *reinterpret_cast<uint2*>(page + row + byte) = wk;
+        *reinterpret_cast<uint2*>(page + codes_bytes + row + int4_vrow_swizzle(pos, byte, head_dim)) = wv;
+        if ((c & 7) == 0) {
+          __half* ks = reinterpret_cast<__half*>(page + 2 * codes_bytes);
+          __half* vs = reinterpret_cast<__half*>(page + 2 * codes_bytes + scale_bytes);
+          ks[pos * gpr + gi] = __float2half_rn(sk);
+          vs[int4_vscale_index(pos, gi, gpr)] = __float2half_rn(sv);
         }
       }
     }
@@ -218,7 +217,12 @@ extern "C" int memopt_write_cache_int4(const void* keys, const void* values,
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: null pointer");
   if (!aligned16(keys) || !aligned16(values) || !aligned16(kv_pages))
     return fail(MEMOPT_ERR_INVALID_ARG, "write_cache_int4: misaligned pointer");
-  write_cache_int4_kernel<<<grid_for_tokens(num_tokens), kWarpsPerCta * 32, 0, as_stream(stream)>>>(
+  const int64_t want = (num_tokens + kInt4WriteWarps - 1) / kInt4WriteWarps;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  auto kern = head_dim == 128 ? write_cache_int4_kernel<128>
+                              : (head_dim == 64 ? write_cache_int4_kernel<64> : write_cache_int4_kernel<0>);
+  kern<<<grid, kInt4WriteWarps * 32, 0, as_stream(stream)>>>(
       reinterpret_cast<const uint4*>(keys), reinterpret_cast<const uint4*>(values), slot_mapping,
       num_tokens, num_heads, head_dim, block_size, num_blocks * block_size, kv_pages,
       static_cast<int64_t>(memopt_int4_page_bytes(block_size, head_dim)), bad_slot_count);

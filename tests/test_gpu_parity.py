@@ -310,7 +310,8 @@ def test_evict_topk_one_part_equals_unsharded():
 
 
 @pytest.mark.parametrize("NB,BS,H,D,r", [(10, 16, 4, 64, 0.75), (7, 32, 3, 128, 0.5), (5, 8, 2, 64, 0.9),
-                                         (6, 5, 2, 64, 0.6), (3, 16, 2, 64, 0.01)])
+                                         (6, 5, 2, 64, 0.6), (3, 16, 2, 64, 0.01), (37, 16, 32, 128, 0.75),
+                                         (9, 16, 40, 128, 0.5), (4, 32, 33, 64, 0.3), (5, 16, 3, 20, 0.5)])
 def test_evict_cache_bit_exact(NB, BS, H, D, r):
     rng = np.random.default_rng(NB * BS)
     sc = rng.integers(0, 5, (NB, BS, H)).astype(np.float32)  # many ties

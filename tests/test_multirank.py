@@ -122,3 +122,36 @@ def test_head_range_and_single_rank_gather():
     t = torch.arange(6.0).reshape(2, 3)
     g = RankGroup()
     assert torch.equal(g.all_gather_rows(t), t[None])
+
+
+def check_multi_pool(out_dir, world: int) -> None:
+    """Each home rank's attention over its sequence (pages on both GPUs)
+    equals the oracle over the sequence's rows; the page placement is the
+    replicated allocator's (home first, spill to the GPU with most room)."""
+    sys.path.insert(0, HERE)
+    import multirank_pool_worker as W
+
+    zs = [np.load(os.path.join(out_dir, f"rank{r}.npz")) for r in range(world)]
+    for z in zs[1:]:  # identical replicas
+        assert np.array_equal(z["pagesA"], zs[0]["pagesA"]) and np.array_equal(z["pagesB"], zs[0]["pagesB"])
+        assert np.array_equal(z["free"], zs[0]["free"])
+    pa, pb = zs[0]["pagesA"], zs[0]["pagesB"]
+    assert [int(d) for d, _ in pa] == [0] * W.BLOCKS + [1, 1]  # A: 130 tokens, 9 pages, 2 spilled
+    assert all(int(d) == 1 for d, _ in pb)
+    assert list(zs[0]["free"]) == [0, W.BLOCKS - 2 - len(pb)]
+    for r, name in ((0, "A"), (1, "B")):
+        k, v = W.full_rows(name)
+        L = k.shape[0]
+        MB = (L + W.BS - 1) // W.BS
+        kp = np.zeros((MB, W.BS, W.H, W.D), np.float16)
+        vp = np.zeros_like(kp)
+        kp.reshape(-1, W.H, W.D)[:L] = k
+        vp.reshape(-1, W.H, W.D)[:L] = v
+        ref = O.paged_attention_f16(W.query(name), kp, vp, np.arange(MB, dtype=np.int32)[None],
+                                    np.array([L], np.int32), L, L)
+        np.testing.assert_allclose(zs[r]["out"], ref, atol=2e-3, rtol=1e-2)
+
+
+def test_two_rank_gloo_multi_device_pool(tmp_path):
+    _spawn("multirank_pool_worker.py", 2, [tmp_path, "gloo"])
+    check_multi_pool(tmp_path, 2)
