@@ -77,9 +77,15 @@ def _spawn(worker: str, world: int, args, extra_env=None, timeout=240):
                    RANK=str(r), LOCAL_RANK=str(r), **(extra_env or {}))
         procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, worker), *map(str, args)],
                                       env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
-    for p in procs:
-        out, _ = p.communicate(timeout=timeout)
-        assert p.returncode == 0, out.decode()[-3000:]
+    try:
+        for p in procs:
+            out, _ = p.communicate(timeout=timeout)
+            assert p.returncode == 0, out.decode()[-3000:]
+    finally:
+        for p in procs:  # a rank that failed or timed out must not outlive the test
+            if p.poll() is None:
+                p.kill()
+                p.wait()
 
 
 def check_head_sharded_evict(out_dir, world: int) -> None:
