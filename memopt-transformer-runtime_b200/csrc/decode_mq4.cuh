@@ -347,6 +347,11 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
             }
           }
         }
+        // Both tiles present and inside every valid row's visible range: no
+        // per-score mask (rows past the group's end hold q = 0; their
+        // finite scores feed only their own, never written, columns).
+        const int t_lo = min(ttok[0], ttok[1]), t_hi = max(ttok[0], ttok[1]) + 16;
+        const bool interior = __all_sync(0xffffffffu, has_b && (!rvalid || (t_lo >= rlo && t_hi <= rhi)));
         float s[2][2][2];
 #pragma unroll
         for (int ti = 0; ti < 2; ++ti) {
@@ -366,9 +371,13 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
                     static_cast<float>(sacc[ti][0][nt][e] * 256 + sacc[ti][0][nt][e + 2]);
               }
               v *= sfac;
-              const int tok = ttok[ti] + nt * 8 + t4 + 4 * e;
-              const bool vis = (ti == 0 || has_b) && tok >= rlo && tok < rhi;
-              s[ti][nt][e] = vis ? v : -INFINITY;
+              if (interior) {
+                s[ti][nt][e] = v;
+              } else {
+                const int tok = ttok[ti] + nt * 8 + t4 + 4 * e;
+                const bool vis = (ti == 0 || has_b) && tok >= rlo && tok < rhi;
+                s[ti][nt][e] = vis ? v : -INFINITY;
+              }
             }
           }
         }

@@ -68,12 +68,10 @@ struct Cfg {
   static constexpr int KV_HALF = kBN * 128;            // 64 rows x 128 B
   static constexpr int Q_TILE = HALVES * Q_HALF;
   static constexpr int KV_STAGE = HALVES * KV_HALF;
-  static constexpr int P_BUF = 128 * 128;              // 128 rows x 64 tokens fp16
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + kTiles * Q_TILE;
   static constexpr int V_OFF = K_OFF + kNSK * KV_STAGE;
-  static constexpr int P_OFF = V_OFF + kNSV * KV_STAGE;  // [tile][buffer]
-  static constexpr int BT_OFF = P_OFF + kTiles * 2 * P_BUF;
+  static constexpr int BT_OFF = V_OFF + kNSV * KV_STAGE;
   static constexpr int SMEM = BT_OFF + 4 * kBtCache + 1024;  // + alignment slack
   static constexpr uint32_t PAGE_TX = 1u * HALVES * BS * 128u;  // bytes of one page of K (or V)
   static constexpr uint32_t IDESC_S = tc::idesc_f16(128, kBN, false, false);
@@ -265,7 +263,6 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       for (int t = 0; t < kTiles; ++t) dq[t] = tc::sdesc_sw128(sbase + C::Q_OFF + t * C::Q_TILE, 16, 1024);
       const uint64_t dk0 = tc::sdesc_sw128(sbase + C::K_OFF, 16, 1024);
       const uint64_t dv0 = tc::sdesc_sw128(sbase + C::V_OFF, C::KV_HALF, 1024);
-      const uint64_t dp0 = tc::sdesc_sw128(sbase + C::P_OFF, 16, 1024);
       auto issue_s = [&](int t, int j) {
         const uint64_t dk = dk0 + static_cast<uint64_t>(((j % kNSK) * C::KV_STAGE) >> 4);
 #pragma unroll
@@ -278,11 +275,12 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       };
       auto issue_pv = [&](int t, int j) {
         const uint64_t dv = dv0 + static_cast<uint64_t>(((j % kNSV) * C::KV_STAGE) >> 4);
-        const uint64_t dp = dp0 + static_cast<uint64_t>(((t * 2 + (j & 1)) * C::P_BUF) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          tc::mma_f16_elect(tO(t), dp + static_cast<uint64_t>((kk * 32) >> 4),
-                            dv + static_cast<uint64_t>((kk * 2048) >> 4), C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          // A = P from tensor memory: columns 8 kk .. 8 kk + 7 of the score
+          // buffer hold tokens 16 kk .. 16 kk + 15 as fp16 pairs.
+          tc::mma_f16_tmem_a_elect(tO(t), tS(t, j) + 8u * kk, dv + static_cast<uint64_t>((kk * 2048) >> 4),
+                                   C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc::commit_elect(bar_pfree(t, j));
       };
@@ -324,7 +322,6 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     const int t = warp >> 2;                 // query tile
     const int row = (warp & 3) * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t sProw = sbase + C::P_OFF + t * 2 * C::P_BUF + row * 128;
     const int ctx_r = row_ctx(qt * kRows + t * 128 + row);  // this row's visible tokens
     const int ws_r = row_ws(ctx_r);
     float m_run = -INFINITY, l_run = 0.f;
@@ -394,9 +391,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l_run = l_run * alpha + psum;
       m_run = m_use;
-      // P buffer j % 2 was last read by P.V(j-2).
       if (tid == 0) PF_TRACE(6, j);
-      if (j >= 2) ok = wait_bar(bar_pfree(t, j - 2), ph_2(j - 2));
       if (__any_sync(0xffffffffu, rescale)) {
         // O holds P.V up to block j-1 only after P.V(j-1) completed.
         if (j >= 1 && ok) ok = wait_bar(bar_pfree(t, j - 1), ph_2(j - 1));
@@ -415,16 +410,21 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       }
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      // 64 P values -> P buffer j % 2 of the tile, K-major with 128-byte swizzle.
-      const uint32_t dst0 = sProw + (j & 1) * C::P_BUF;
+      // P (64 fp16 values as 32 pairs) over the scores it replaces in the
+      // tile's score buffer j % 2 (this thread's lane, columns 0-31): the
+      // A operand of P.V(j).  S(j+2) reuses the buffer only after P.V(j),
+      // issued before it by the same thread.
+      {
+        uint32_t lo[16], hi[16];
 #pragma unroll
-      for (int chunk = 0; chunk < 8; ++chunk) {
-        const uint32_t dst = dst0 + ((chunk ^ (row & 7)) * 16);
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(ph[4 * chunk]), "r"(ph[4 * chunk + 1]),
-                     "r"(ph[4 * chunk + 2]), "r"(ph[4 * chunk + 3])
-                     : "memory");
+        for (int i = 0; i < 16; ++i) {
+          lo[i] = ph[i];
+          hi[i] = ph[16 + i];
+        }
+        tc::st16(tS(t, j) + lane_base, lo);
+        tc::st16(tS(t, j) + lane_base + 16, hi);
+        tc::wait_st();
       }
-      fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull(t, j));
