@@ -94,6 +94,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete may
+// be suspended for up to `ns` nanoseconds (woken early when the phase
+// completes) instead of returning at once, so a waiting warp spends fewer
+// issue slots polling.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) accesses of the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

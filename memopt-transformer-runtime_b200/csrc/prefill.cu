@@ -9,25 +9,29 @@
 //
 // One CTA = (two 128-query tiles, head, sequence); keys are consumed in blocks
 // of 64 tokens (64/BS pages) shared by both tiles.
-//   * warp 8 stages Q once and K/V blocks by TMA (3-D tensor maps over the
-//     query tensor and the fp16 pool, 128-byte swizzle, no multicast) into
-//     rings of 3 K and 2 V stages, and its lane 0 issues the tcgen05.mma
-//     instructions: per tile, S(j) = Q K(j)^T (M=128, N=64, K=D) into one of
-//     two TMEM score buffers and O += P(j) V(j) (M=128, N=D, K=64; V is the
-//     MN-major operand) into the tile's O columns;
+//   * warps 9 and 10 stage Q once and K/V blocks by TMA (3-D tensor maps over
+//     the query tensor and the fp16 pool, 128-byte swizzle, no multicast) into
+//     rings of 3 K and 2 V stages;
+//   * warp 8 issues the tcgen05.mma instructions (warp-uniform code, one lane
+//     elected per instruction): per tile, S(j) = Q K(j)^T (M=128, N=64, K=D)
+//     into one of two TMEM score buffers and O += P(j) V(j) (M=128, N=D,
+//     K=64) with P read from tensor memory (the A operand) and V the MN-major
+//     operand from shared memory;
 //   * warps 0-3 (tile 0) and 4-7 (tile 1) run the softmax, one thread per
 //     query row (= TMEM lane): it loads its 64 scores with tcgen05.ld,
 //     releases the score buffer, runs the online softmax in the log2 domain,
-//     writes P (fp16) into one of the tile's two shared-memory P buffers
-//     (K-major, 128-byte swizzle) and rescales its O row in TMEM only when
-//     its running max grows by more than 2^8 (stale maxima below that bound
-//     keep P <= 256, exact enough in fp16).
-// With two score and two P buffers per tile, S(j+2) and P.V(j) run on the
-// tensor pipe while the softmax works on block j+1, and the two tiles'
-// softmax warps interleave on every SM sub-partition; no CTA-wide barrier is
-// taken per block.  The epilogue divides O by the row sum and stores fp16.
-// Pages that are skipped (entry < 0 or >= num_blocks) are zero-filled in smem
-// and masked; every mbarrier wait is bounded and reports through `err`.
+//     writes P (fp16 pairs) over the first 32 columns of the same score
+//     buffer with tcgen05.st and rescales its O row in TMEM only when its
+//     running max grows by more than 2^8 (stale maxima below that bound keep
+//     P <= 256, exact enough in fp16).
+// With two score buffers per tile, S(j+2) and P.V(j) run on the tensor pipe
+// while the softmax works on block j+1; S(j+2) overwrites P(j) only after
+// P.V(j), issued before it by the same thread (tcgen05.mma instructions of
+// one thread execute in order).  The two tiles' softmax warps interleave on
+// every SM sub-partition; no CTA-wide barrier is taken per block.  The
+// epilogue divides O by the row sum and stores fp16.  Pages that are skipped
+// (entry < 0 or >= num_blocks) are zero-filled in smem and masked; every
+// mbarrier wait is bounded and reports through `err`.
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -80,10 +84,15 @@ struct Cfg {
   static_assert(kTiles * (2 * kBN + D) <= 512, "tensor memory columns");
 };
 
+#ifndef MEMOPT_PF_HINT_NS
+#define MEMOPT_PF_HINT_NS 1000
+#endif
+// Bounded wait: at most 2^21 polls of at most MEMOPT_PF_HINT_NS each (about
+// two seconds), then the caller records a failure.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
   uint32_t polls = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if (++polls >= kMaxPolls) return false;
+  while (!mbar_try_wait_hint(bar, parity, MEMOPT_PF_HINT_NS)) {
+    if (++polls >= (1u << 21)) return false;
   }
   return true;
 }
