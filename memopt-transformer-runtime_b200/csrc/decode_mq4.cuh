@@ -116,6 +116,7 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
   int p_phys = -1;
   int p_kvh = 0;
   uint32_t p_seq = 0;
+  int p_st = 0;  // p_seq % NS, kept incrementally (NS need not be a power of two)
   bool p_done = false;
 
   auto produce = [&]() {
@@ -140,7 +141,7 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
     {
       // Warp-collective issue: one elected lane arms the stage and starts the
       // copy, with no divergent branch around it.
-      const int st = static_cast<int>(p_seq % NS);
+      const int st = p_st;
       const uint32_t bar = bar0 + 8 * st;
       const uint8_t* src = p.pages + (static_cast<int64_t>(phys) * p.KVH + p_kvh) * C::PAGE_RAW;
       asm volatile(
@@ -153,13 +154,12 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
           : "memory");
     }
     ++p_seq;
+    p_st = p_st + 1 == NS ? 0 : p_st + 1;
   };
 
   for (int s = 0; s < NS; ++s) produce();
 
-  auto wait_stage = [&](uint32_t seq) -> bool {
-    const int st = static_cast<int>(seq % NS);
-    const uint32_t parity = (seq / NS) & 1u;
+  auto wait_stage = [&](int st, uint32_t parity) -> bool {
     uint32_t polls = 0;
     bool ready = mbar_try_wait(bar0 + 8 * st, parity);
     while (!__all_sync(0xffffffffu, ready) && ++polls < kMaxPolls) {
@@ -183,6 +183,8 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
   // V scales of tokens (t4, t4 + 4) and (t4 + 8, t4 + 12): adjacent halves.
   const uint32_t o_vs = C::V_SCALE + 4 * t4;
   uint32_t c_seq = 0;
+  int c_st = 0;          // c_seq % NS
+  uint32_t c_ph = 0;     // (c_seq / NS) & 1
   bool failed = false;
 
   for (int64_t item = first; item < p.total_items && !failed; item += nwarps) {
@@ -310,14 +312,16 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
           mask &= mask - 1;
         }
         const int nst = (HALVES == 1 && jb >= 0) ? 2 : 1;  // ring stages this step
-        if (!wait_stage(c_seq) || (nst == 2 && !wait_stage(c_seq + 1))) {
+        const int c_st1 = c_st + 1 == NS ? 0 : c_st + 1;  // stage of c_seq + 1
+        const uint32_t c_ph1 = c_st1 == 0 ? c_ph ^ 1u : c_ph;
+        if (!wait_stage(c_st, c_ph) || (nst == 2 && !wait_stage(c_st1, c_ph1))) {
           failed = true;
           break;
         }
         const bool has_b = HALVES == 2 || jb >= 0;
         uint32_t tstg[2];
         int thalf[2], ttok[2];
-        tstg[0] = st0 + static_cast<uint32_t>(c_seq % NS) * C::STAGE;
+        tstg[0] = st0 + static_cast<uint32_t>(c_st) * C::STAGE;
         thalf[0] = 0;
         ttok[0] = (c_lo + ja) * BS;
         if (HALVES == 2) {
@@ -325,7 +329,7 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
           thalf[1] = 1;
           ttok[1] = ttok[0] + 16;
         } else {
-          tstg[1] = st0 + static_cast<uint32_t>((c_seq + 1) % NS) * C::STAGE;
+          tstg[1] = st0 + static_cast<uint32_t>(c_st1) * C::STAGE;
           thalf[1] = 0;
           ttok[1] = (c_lo + (jb >= 0 ? jb : ja)) * BS;
         }
@@ -470,6 +474,10 @@ paged_decode_mq4_kernel(const __grid_constant__ Params p, int32_t* __restrict__ 
         __syncwarp();
         for (int k = 0; k < nst; ++k) {
           ++c_seq;
+          if (++c_st == NS) {
+            c_st = 0;
+            c_ph ^= 1u;
+          }
           produce();
         }
       }

@@ -387,17 +387,28 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
         rescale = true;
       }
       const float msub = (m_use == -INFINITY) ? 0.f : m_use;  // all-masked rows: every p = ex2(-inf) = 0
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // x = s qscale - msub two at a time (packed fp32 fma), p = 2^x, P in
+      // fp16 pairs; the row sum adds exactly those fp16 values (fp16 pairs
+      // over 4 steps each, then fp32), so l matches the P that P.V uses.
+      const uint64_t qs2 = f32x2_pack(p.qscale, p.qscale), nm2 = f32x2_pack(-msub, -msub);
+      __half2 hs[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) hs[k] = __float2half2_rn(0.f);
       uint32_t ph[kBN / 2];
 #pragma unroll
       for (int i = 0; i < kBN / 2; ++i) {
-        const float p0 = tc::ex2(fmaf(s[2 * i], p.qscale, -msub));
-        const float p1 = tc::ex2(fmaf(s[2 * i + 1], p.qscale, -msub));
-        ps[i & 7] += p0 + p1;
-        const __half2 hv = __floats2half2_rn(p0, p1);
+        float x0, x1;
+        f32x2_unpack(f32x2_fma(f32x2_pack(s[2 * i], s[2 * i + 1]), qs2, nm2), x0, x1);
+        const __half2 hv = __floats2half2_rn(tc::ex2(x0), tc::ex2(x1));
         ph[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        hs[i & 7] = __hadd2(hs[i & 7], hv);
       }
-      const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      float psum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float2 f = __half22float2(hs[k]);
+        psum += f.x + f.y;
+      }
       l_run = l_run * alpha + psum;
       m_run = m_use;
       if (tid == 0) PF_TRACE(6, j);
