@@ -65,3 +65,45 @@ def test_gather_plan_groups_remote_pages_by_owner_and_dedupes():
     with pytest.raises(_capi.MemoptError, match="staging"):
         mdpool_plan(dev, blk, home=0, staging_base=100, staging_capacity=3)
     assert mdpool_plan([], [], 0, 0, 0) == ([], [])
+
+
+def _cpu_pool(blocks, staging=4, H=2, D=64, BS=16):
+    import torch
+
+    from memopt.multi_pool import MultiDevicePagePool
+    from memopt.sharding import RankGroup
+
+    def write_rows(k, v, slots):
+        kp, vp = pool.tensors
+        kp.view(-1, H, D)[slots.long()] = k
+        vp.view(-1, H, D)[slots.long()] = v
+
+    pool = MultiDevicePagePool(RankGroup(), blocks, staging, BS, H, D, device=torch.device("cpu"),
+                               pack=lambda src, ids, out: out.copy_(src.index_select(0, ids.long())),
+                               write_rows=write_rows, attend_fn=lambda *a: None)
+    return pool
+
+
+def test_single_rank_pool_bookkeeping_and_exhaustion():
+    import torch
+
+    pool = _cpu_pool(4)
+    a = pool.add_sequence(0)
+    b = pool.add_sequence(0)
+    k = torch.randn(40, 2, 64).half()
+    pool.append(a, k, k)  # 3 pages
+    assert pool.length(a) == 40 and [p[0] for p in pool.pages(a)] == [0, 0, 0] and pool.free_count(0) == 1
+    kp, _ = pool.tensors
+    pg = pool.pages(a)
+    assert torch.equal(kp[pg[2][1], :8], k[32:40])  # token t in page t // 16, slot t % 16
+    with pytest.raises(MemoryError):
+        pool.append(b, torch.randn(20, 2, 64).half(), torch.randn(20, 2, 64).half())  # needs 2 pages, 1 left
+    assert pool.length(b) == 0 and pool.free_count(0) == 1  # the failed append took nothing
+    pool.append(b, k[:16], k[:16])
+    assert pool.free_count(0) == 0
+    pool.free_sequence(a)
+    assert pool.free_count(0) == 3
+    with pytest.raises(ValueError):
+        pool.add_sequence(1)  # a world of one rank
+    with pytest.raises(ValueError):
+        pool.append(b)  # the home rank must pass k and v
