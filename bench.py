@@ -58,12 +58,30 @@ def peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+_CLOCK_SAMPLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1].encode()) if sys.argv[1] else \
+    pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+        pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
+mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+print("ready", mx, flush=True)
+while True:
+    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), "".join("1" if r & b else "0" for b in bits),
+          flush=True)
+"""
+
+
 class Clocks:
     """SM clock and clock-event reasons sampled during the timed region.
 
-    NVML is polled from a thread every millisecond (a decode step lasts a
-    fraction of a millisecond, so nvidia-smi's 100 ms loop sees nothing);
-    nvidia-smi is the fallback when NVML cannot be opened.  Read-only."""
+    A separate process polls NVML back to back (a decode step lasts a
+    fraction of a millisecond, so nvidia-smi's 100 ms loop sees nothing, and
+    a thread of this process would contend for the interpreter lock with the
+    launches being timed); entering the block waits until it samples.
+    nvidia-smi is the fallback when NVML cannot be used.  Read-only."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -74,52 +92,31 @@ class Clocks:
         self.index = index
         self.proc = None
         self.sm, self.mx, self.reasons = [], 0.0, set()
-        self._stop = None
-        self._thread = None
         self.source = "none"
-
-    def _nvml_handle(self):
-        import pynvml
-        import torch
-
-        pynvml.nvmlInit()
-        try:
-            p = torch.cuda.get_device_properties(self.index)
-            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
-            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
-        except Exception:  # noqa: BLE001
-            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
-
-    def _poll(self, nv, h):
-        import time as _t
-
-        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
-                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
-                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
-                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
-        while True:
-            try:
-                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
-                self.mx = max(self.mx, float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.reasons.update(n for n, b in bits.items() if r & b)
-            except Exception:  # noqa: BLE001
-                pass
-            if self._stop.wait(0.001):
-                return
+        self.nvml = False
 
     def __enter__(self):
-        import threading
-
+        bus = ""
         try:
-            nv, h = self._nvml_handle()
-            self._stop = threading.Event()
-            self._thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
-            self._thread.start()
-            self.source = "nvml"
-            return self
+            import torch
+
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
         except Exception:  # noqa: BLE001
-            self._thread = None
+            pass
+        try:
+            self.proc = subprocess.Popen([sys.executable, "-c", _CLOCK_SAMPLER, bus, str(self.index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline().split()
+            if first and first[0] == "ready":
+                self.mx = float(first[1])
+                self.nvml = True
+                self.source = "nvml"
+                return self
+            self.proc.kill()
+            self.proc.wait()
+        except Exception:  # noqa: BLE001
+            self.proc = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -130,9 +127,6 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
         out = ""
         if self.proc is not None:
             self.proc.terminate()
@@ -141,6 +135,18 @@ class Clocks:
             except Exception:  # noqa: BLE001
                 self.proc.kill()
         for line in (out or "").splitlines():
+            if self.nvml:
+                f = line.split()
+                if len(f) != 2:
+                    continue
+                try:
+                    self.sm.append(float(f[0]))
+                except ValueError:
+                    continue
+                for n, bit in zip(self.NAMES, f[1]):
+                    if bit == "1":
+                        self.reasons.add(n)
+                continue
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
