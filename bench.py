@@ -66,10 +66,13 @@ h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1].encode()) if sys.argv[1] el
 bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
 mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
 print("ready", mx, flush=True)
 while True:
+    t = time.time()
     r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-    print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), "".join("1" if r & b else "0" for b in bits),
+    print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), "".join("1" if r & b else "0" for b in bits),
           flush=True)
 """
 
@@ -94,6 +97,8 @@ class Clocks:
         self.sm, self.mx, self.reasons = [], 0.0, set()
         self.source = "none"
         self.nvml = False
+        self.t0 = self.t1 = 0.0
+        self.near = []  # every NVML sample, the block's and those around it
 
     def __enter__(self):
         bus = ""
@@ -112,6 +117,7 @@ class Clocks:
                 self.mx = float(first[1])
                 self.nvml = True
                 self.source = "nvml"
+                self.t0 = time.time()
                 return self
             self.proc.kill()
             self.proc.wait()
@@ -128,6 +134,9 @@ class Clocks:
 
     def __exit__(self, *a):
         out = ""
+        self.t1 = time.time()
+        if self.proc is not None and self.nvml:
+            time.sleep(0.02)  # let samples taken inside the block reach the pipe
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -137,13 +146,17 @@ class Clocks:
         for line in (out or "").splitlines():
             if self.nvml:
                 f = line.split()
-                if len(f) != 2:
+                if len(f) != 3:
                     continue
                 try:
-                    self.sm.append(float(f[0]))
+                    ts, mhz = float(f[0]), float(f[1])
                 except ValueError:
                     continue
-                for n, bit in zip(self.NAMES, f[1]):
+                self.near.append(mhz)
+                if not self.t0 <= ts <= self.t1:  # taken outside the block
+                    continue
+                self.sm.append(mhz)
+                for n, bit in zip(self.NAMES, f[2]):
                     if bit == "1":
                         self.reasons.add(n)
                 continue
@@ -162,7 +175,9 @@ class Clocks:
     def summary(self) -> dict:
         sm = self.sm
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.mx or None,
-                "reasons": sorted(self.reasons), "samples": len(sm), "source": self.source}
+                "reasons": sorted(self.reasons), "samples": len(sm), "source": self.source,
+                "window_ms": round((self.t1 - self.t0) * 1e3, 2),
+                "sm_mhz_around": statistics.median(self.near) if self.near else None}
 
 
 def dist_env():
