@@ -27,8 +27,9 @@
 // With two score buffers per tile, S(j+2) and P.V(j) run on the tensor pipe
 // while the softmax works on block j+1; S(j+2) overwrites P(j) only after
 // P.V(j), issued before it by the same thread (tcgen05.mma instructions of
-// one thread execute in order).  The two tiles' softmax warps interleave on
-// every SM sub-partition; no CTA-wide barrier is taken per block.  The
+// one thread execute in order).  The two tiles' softmax warps share every SM
+// sub-partition, tile 1 running about half a block behind tile 0 (it starts
+// after P(0) of tile 0); no CTA-wide barrier is taken per block.  The
 // epilogue divides O by the row sum and stores fp16.  Pages that are skipped
 // (entry < 0 or >= num_blocks) are zero-filled in smem and masked; every
 // mbarrier wait is bounded and reports through `err`.
@@ -109,7 +110,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity) {
 constexpr int kBars = 11 + 8 * kTiles;
 
 #ifdef MEMOPT_PF_TRACE
-__device__ unsigned long long g_pf_trace[8][512];
+__device__ unsigned long long g_pf_trace[12][512];
 #define PF_TRACE(ev, j)                                                                   \
   do {                                                                                    \
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 512) g_pf_trace[ev][(j)] = clock64(); \
@@ -336,6 +337,15 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nblocks && ok; ++j) {
+      if (j == 0 && t == 1) {
+        // Tile 1 starts once tile 0 has stored P(0).  The two tiles then keep
+        // that offset (S(j + 2) of both follows both P(j)), so one tile's
+        // exponentials run while the other loads scores, takes the row max
+        // or waits; started together, they stay in step and the exponential
+        // unit idles in those phases.
+        ok = __all_sync(0xffffffffu, wait_bar(bar_pfull(0, 0), 0));
+        if (!ok) break;
+      }
       ok = wait_bar(bar_sfull(t, j), ph_2(j));
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -376,6 +386,8 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                        fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       mx *= p.qscale;  // qscale > 0: the max of the scaled scores
+      if (tid == 0) PF_TRACE(10, j);
+      if (tid == 128) PF_TRACE(11, j);
       const float m_new = fmaxf(m_run, mx);
       float m_use = m_run, alpha = 1.f;
       bool rescale = false;
@@ -412,6 +424,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       l_run = l_run * alpha + psum;
       m_run = m_use;
       if (tid == 0) PF_TRACE(6, j);
+      if (tid == 128) PF_TRACE(9, j);
       if (__any_sync(0xffffffffu, rescale)) {
         // O holds P.V up to block j-1 only after P.V(j-1) completed.
         if (j >= 1 && ok) ok = wait_bar(bar_pfree(t, j - 1), ph_2(j - 1));
@@ -449,6 +462,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull(t, j));
       if (tid == 0) PF_TRACE(5, j);
+      if (tid == 128) PF_TRACE(8, j);
     }
     // ---- epilogue ------------------------------------------------------------
     const int qi = qt * kRows + t * 128 + row;

@@ -8,7 +8,10 @@ from __future__ import annotations
 import ctypes as C
 import os
 
-_LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "libmemopt_b200.so")
+# MEMOPT_LIB names another build of the same library (a variant compiled with
+# different tuning macros); by default the in-tree build is loaded.
+_LIB_PATH = os.environ.get("MEMOPT_LIB") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "libmemopt_b200.so")
 P, I, I64, F, SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 _lib = None
 

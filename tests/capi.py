@@ -19,7 +19,7 @@ P, I, I64, F, SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        _lib = C.CDLL(os.path.join(PKG, "libmemopt_b200.so"))
+        _lib = C.CDLL(os.environ.get("MEMOPT_LIB") or os.path.join(PKG, "libmemopt_b200.so"))
         _lib.memopt_last_error.restype = C.c_char_p
         _lib.memopt_paged_attention_workspace_size.restype = SZ
         _lib.memopt_paged_attention_ticket_bytes.restype = SZ
