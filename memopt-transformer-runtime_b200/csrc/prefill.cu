@@ -354,15 +354,17 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       tc::fence_after_sync();
       float s[kBN];
       {
-        float v[32];
-        tc::ld32(tS(t, j) + lane_base, v);
+        float va[32], vb[32];
+        tc::ld32(tS(t, j) + lane_base, va);
+        tc::ld32(tS(t, j) + lane_base + 32, vb);
+        tc::wait_ld(va);
+        tc::wait_ld(vb);  // nothing left in flight: orders the uses of vb
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = v[i];
-        tc::ld32(tS(t, j) + lane_base + 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = v[i];
+        for (int i = 0; i < 32; ++i) {
+          s[i] = va[i];
+          s[32 + i] = vb[i];
+        }
       }
-      tc::wait_ld();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sfree(t, j));
@@ -434,7 +436,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
           float v[32];
           const uint32_t col = tO(t) + lane_base + c * 32;
           tc::ld32(col, v);
-          tc::wait_ld();
+          tc::wait_ld(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
           tc::st32(col, v);
@@ -476,7 +478,7 @@ prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtenso
       for (int c = 0; c < D / 32; ++c) {
         float v[32];
         tc::ld32(tO(t) + lane_base + c * 32, v);
-        tc::wait_ld();
+        tc::wait_ld(v);
         if (qi < p.QL) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
