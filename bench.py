@@ -558,7 +558,8 @@ def run_ours(args) -> None:
 
 # Order of the one-line summaries printed after the JSON line: the north-star
 # legs come last, so that a reader of the last lines of the output sees them.
-LEG_ORDER = ["evict_tokens", "evict_tokens_l2_flushed", "evict_cache", "evict_topk_compact", "evict_topk_compact_int4",
+LEG_ORDER = ["evict_tokens", "evict_tokens_l2_flushed", "evict_tokens_no_sinks_l2_flushed", "evict_cache",
+             "evict_topk_compact", "evict_topk_compact_int4",
              "evict_topk_head_sharded", "window_decode", "quantize_int4", "dequantize_int4", "write_cache_f16",
              "multi_row_decode_f16", "gqa_decode_f16", "gqa_decode_int4", "long_context_decode_retain_0.75",
              "long_context_decode", "prefill", "int4_write_cache", "int4_decode"]
@@ -900,6 +901,17 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
     ms_ev = max_over_ranks(time_loop(torch, evict, ev_steps, args.warmup, barrier, stream))
     # the same calls with the L2 flushed before each (scores streamed from HBM)
     ms_ev_cold = max_over_ranks(time_each(torch, evict, max(20, ev_steps), stream, l2_flusher(torch, dev)))
+    # Without sinks the threshold falls among the scores: the exact select of
+    # the keep-th largest score runs and a quarter of the tokens are evicted
+    # (their partial rows zeroed in K and V).  The pool is refilled below
+    # before anything reads it.
+    def evict_no_sinks():
+        _capi.evict_tokens(scores, bt, ibf, kp, vp, 0.75, 0, idx_buf, cnt_buf, sp)
+
+    ms_ev0 = max_over_ranks(time_each(torch, evict_no_sinks, max(20, ev_steps), stream, l2_flusher(torch, dev)))
+    evicted0 = int((ectx - cnt_buf).sum().item())
+    # scores read, index list written, D/32 halves zeroed per evicted token, head and pool
+    ev0_bytes = 2 * eb * H * ectx * 4 + evicted0 * 2 * (D // 32) * 2
     idx, cnt = memopt_C.evict_tokens(scores, bt, ibf, 0.75, 4, return_retained=True)
     kept = float(cnt.float().mean().item()) / ectx
     ev_bytes = 2 * eb * H * ectx * 4  # scores read + kept-index list written (no row is evicted with sinks)
@@ -973,6 +985,15 @@ def evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over
                                         "value": round(ev_bytes * ws_n / (ms_ev_cold * 1e-3) / 1e9, 2), "unit": "GB/s",
                                         "ms_per_call": round(ms_ev_cold, 5),
                                         "frac_of_hbm_peak": round(ev_bytes / ms_ev_cold / 1e6 / peaks()[0], 4)},
+            "evict_tokens_no_sinks_l2_flushed": {
+                "workload": "the same scores without sink tokens (the threshold falls among them: exact select, "
+                            "25% of tokens evicted, their partial rows zeroed), L2 flushed before each call",
+                "value": round(ev0_bytes * ws_n / (ms_ev0 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_call": round(ms_ev0, 5), "evicted_tokens": evicted0,
+                "note": "bound by the reference's partial-row zeroing: 2-byte stores at d = t % 32 + 32k, so each "
+                        "evicted (token, head) dirties 2 x D/32 separate 32-byte sectors that L2 must fill from "
+                        "and write back to HBM (about 64 B of DRAM traffic per zeroed element)",
+                "frac_of_hbm_peak": round(ev0_bytes / ms_ev0 / 1e6 / peaks()[0], 4)},
             "evict_topk_compact": {"workload": "BASELINE configs[3] scores, exact top-k shared across heads "
                                                "(retain 0.75, 4 sinks), kept K/V rows compacted, pages released",
                                    "value": round(topk_bytes * ws_n / (ms_topk * 1e-3) / 1e9, 2), "unit": "GB/s",

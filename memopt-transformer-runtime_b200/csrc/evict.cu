@@ -14,9 +14,12 @@
 //     so it can reach block_size only when block_size == 1 (:993-1014).
 // The reference runs one 128-thread CTA per (seq, head) with the scores in
 // shared memory and three barriers per bisection step; here one CTA keeps the
-// scores in registers (<= 64 per thread), each step costs one
-// barrier (double-buffered warp partials), and the kept tokens are also
-// stream-compacted into an ascending index list.
+// scores in registers (<= 64 per thread) and runs no block-wide step per
+// bisection: the steps' outcomes depend on the scores only through the
+// keep-th largest comparable score, which bounds decide for most steps and an
+// exact radix select gives for the rest, so the 32 steps are replayed on
+// scalars.  The kept tokens are also stream-compacted into an ascending index
+// list.
 //
 // evict_cache: replaces evict_cache_kernel (kv_cache.cu:379-483): per
 // (physical block, head) the threshold is the keep-th largest score found by
@@ -36,6 +39,16 @@ __device__ __forceinline__ int warp_sum_i(int v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Order-preserving key of a float (x < y as floats <=> key(x) < key(y) as
+// unsigned, -0 just below +0) and its inverse.
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float(k ^ ((k & 0x80000000u) ? 0x80000000u : 0xFFFFFFFFu));
 }
 
 template <int VPT, int kEvictThreads>
@@ -58,6 +71,11 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
   __shared__ float red_f[2][kEvictWarps];
   __shared__ int red_i[2][kEvictWarps];
   __shared__ int warp_tot[kEvictWarps];
+  // Radix select: one histogram copy per lane (a warp's atomics never meet),
+  // the bin totals and the chosen digit with the remaining rank.
+  __shared__ int hist[256][32];
+  __shared__ int bin_tot[256];
+  __shared__ int sel_digit[2];
 
   // ---- load: warp w owns tokens [w*32*VPT, (w+1)*32*VPT); in round k lane
   // holds the 4 tokens chunk + 128 k + 4 lane .. +3, so every warp load and
@@ -125,32 +143,129 @@ evict_tokens_kernel(const float* __restrict__ scores, int num_seqs, int num_head
     gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
   }
 
+  // Exact keep-th largest comparable score of the block (keep <= the number
+  // of comparable scores): radix select over order-preserving 32-bit keys,
+  // four 8-bit digits from the most significant, each pass one histogram of
+  // the digit over the keys that match the digits chosen so far.
+  auto radix_select = [&](const float (&vals)[VPT], int rank) -> float {
+    uint32_t prefix = 0, pmask = 0;
+    int kk = rank;  // rank among the keys that match the prefix, from the top
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256 * 32; i += kEvictThreads) hist[i >> 5][i & 31] = 0;
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const uint32_t key = order_key(vals[i]);
+        if (vals[i] == vals[i] && (key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u][lane], 1);
+      }
+      __syncthreads();
+      if (tid < 256) {
+        int c = 0;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) c += hist[tid][(j + tid) & 31];  // rotated: no bank conflicts
+        bin_tot[tid] = c;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // lane l holds digits 255 - 8l .. 248 - 8l, in descending order
+        int c8[8], sum = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          c8[e] = bin_tot[255 - 8 * lane - e];
+          sum += c8[e];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        int above = incl - sum;  // keys with a larger digit than this lane's first
+        if (above < kk && kk <= incl) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (above < kk && kk <= above + c8[e]) {
+              sel_digit[0] = 255 - 8 * lane - e;
+              sel_digit[1] = kk - above;
+            }
+            above += c8[e];
+          }
+        }
+      }
+      __syncthreads();
+      prefix |= static_cast<uint32_t>(sel_digit[0]) << shift;
+      pmask |= 255u << shift;
+      kk = sel_digit[1];
+      __syncthreads();  // sel_digit is written again by the next pass
+    }
+    return key_float(prefix);
+  };
+
   // ---- threshold ---------------------------------------------------------
   const int keep = max(1, min(L, static_cast<int>(ceilf(retain_ratio * static_cast<float>(L)))));
   float thr;
   if (gmin >= gmax) {
     thr = gmin - 1.0f;
   } else {
+    // count(s >= mid) >= keep holds exactly when w >= mid, w being the
+    // keep-th largest comparable (non-NaN) score, and never when fewer than
+    // keep scores are comparable.  So the 32 bisection steps depend on the
+    // scores only through w and are replayed here on scalars with the same
+    // fma.  Most steps are decided by bounds of w: w <= u (u = the largest
+    // score below the maximum when fewer than keep scores equal the maximum,
+    // else the maximum) and w >= gmin; only a midpoint inside (gmin, u]
+    // needs w itself, found once by an exact radix select.
+    float mx2 = -INFINITY;
+    int neq = 0;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      neq += (v[i] == gmax) ? 1 : 0;
+      if (v[i] < gmax) mx2 = fmaxf(mx2, v[i]);
+    }
+    int tot_cmp = ncmp, tot_eq = neq;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      tot_cmp += __shfl_xor_sync(0xffffffffu, tot_cmp, o);
+      tot_eq += __shfl_xor_sync(0xffffffffu, tot_eq, o);
+      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, o));
+    }
+    __syncthreads();  // every warp has read the min / max partials in red_f
+    if (lane == 0) {
+      red_i[0][warp] = tot_cmp;
+      red_i[1][warp] = tot_eq;
+      red_f[0][warp] = mx2;
+    }
+    __syncthreads();
+    tot_cmp = lane < kEvictWarps ? red_i[0][lane] : 0;
+    tot_eq = lane < kEvictWarps ? red_i[1][lane] : 0;
+    mx2 = lane < kEvictWarps ? red_f[0][lane] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      tot_cmp += __shfl_xor_sync(0xffffffffu, tot_cmp, o);
+      tot_eq += __shfl_xor_sync(0xffffffffu, tot_eq, o);
+      mx2 = fmaxf(mx2, __shfl_xor_sync(0xffffffffu, mx2, o));
+    }
+    const float u = tot_eq < keep ? mx2 : gmax;
+    bool have_w = false;
+    float w = 0.f;
     float lo = gmin, hi = gmax;
 #pragma unroll 1
     for (int it = 0; it < 32; ++it) {
       const float mid = __fmaf_rn(hi - lo, 0.5f, lo);
-      // A midpoint above this thread's largest score counts nothing, one at
-      // or below its smallest counts every comparable score: no scan needed.
-      int c = mid > tmax ? 0 : ncmp;
-      if (mid > tmin && mid <= tmax) {
-        int cp[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // eight independent chains instead of one of VPT adds
-#pragma unroll
-        for (int i = 0; i < VPT; ++i) cp[i & 7] += (v[i] >= mid) ? 1 : 0;
-        c = ((cp[0] + cp[1]) + (cp[2] + cp[3])) + ((cp[4] + cp[5]) + (cp[6] + cp[7]));
+      bool ge;
+      if (tot_cmp < keep || mid != mid || mid > u) {
+        ge = false;
+      } else if (mid <= gmin) {
+        ge = true;
+      } else {
+        if (!have_w) {  // block-uniform: every input above is the same in all threads
+          w = radix_select(v, keep);
+          have_w = true;
+        }
+        ge = w >= mid;
       }
-      c = warp_sum_i(c);
-      const int buf = it & 1;
-      if (lane == 0) red_i[buf][warp] = c;
-      __syncthreads();
-      int tot = lane < kEvictWarps ? red_i[buf][lane] : 0;
-      tot = warp_sum_i(tot);
-      if (tot >= keep) lo = mid; else hi = mid;
+      if (ge) lo = mid; else hi = mid;
     }
     thr = lo;
   }

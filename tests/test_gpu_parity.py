@@ -138,6 +138,15 @@ def _evict_case(S, H, L, BS, D, r, sinks, seed, dist="lognormal", extra_pages=3,
         sc[(m >= 0.025) & (m < 0.03)] = -np.inf
         sc[(m >= 0.03) & (m < 0.032)] = 3e38
         sc[0, 0, : min(L, 70)] = np.nan  # a whole thread's worth of NaN
+    elif dist == "maxheavy":  # most scores equal to the row maximum
+        sc = rng.lognormal(0, 1, (S, H, L)).astype(np.float32)
+        sc[rng.random((S, H, L)) < 0.8] = 50.0
+    elif dist == "signed_zero":  # -0, +0 and negative scores only
+        sc = -rng.integers(0, 3, (S, H, L)).astype(np.float32)
+        sc[rng.random((S, H, L)) < 0.3] = -0.0
+    elif dist == "mostly_nan":  # fewer comparable scores than kept tokens
+        sc = rng.standard_normal((S, H, L)).astype(np.float32)
+        sc[rng.random((S, H, L)) < 0.9] = np.nan
     else:
         sc = rng.standard_normal((S, H, L)).astype(np.float32)
     MB = (L + BS - 1) // BS
@@ -169,6 +178,11 @@ def _evict_case(S, H, L, BS, D, r, sinks, seed, dist="lognormal", extra_pages=3,
     (1, 2, 20001, 16, 64, 0.75, 0, "specials", False),
     (1, 2, 32767, 16, 64, 0.75, 5, "specials", False),
     (1, 2, 16384, 16, 64, 0.9, 0, "ties", False),
+    (1, 2, 32768, 16, 64, 0.5, 0, "maxheavy", False),   # keep-th largest among the maxima
+    (1, 2, 32768, 16, 64, 0.9, 0, "maxheavy", False),   # ... and below them
+    (1, 2, 5000, 16, 64, 0.6, 0, "signed_zero", False),
+    (1, 2, 32768, 16, 64, 0.5, 0, "mostly_nan", False),
+    (1, 2, 32768, 16, 64, 0.05, 0, "mostly_nan", False),
 ])
 def test_evict_tokens_bit_exact(S, H, L, BS, D, r, sinks, dist, holes):
     sc, bt, kp, vp = _evict_case(S, H, L, BS, D, r, sinks, L + S, dist, holes=holes)
