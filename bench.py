@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -68,12 +69,16 @@ bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwTh
 mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
 pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
 pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+out = open(sys.argv[3], "w") if len(sys.argv) > 3 else sys.stdout
+pause = float(sys.argv[4]) if len(sys.argv) > 4 else 0.0
 print("ready", mx, flush=True)
 while True:
     t = time.time()
     r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
     print(t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), "".join("1" if r & b else "0" for b in bits),
-          flush=True)
+          file=out, flush=True)
+    if pause:
+        time.sleep(pause)
 """
 
 
@@ -91,8 +96,10 @@ class Clocks:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, log_path: str = ""):
         self.index = index
+        self.log_path = log_path  # samples go to this file, one per millisecond (long blocks)
+        self.samples = []  # (time, SM MHz, reason bits) of every NVML sample
         self.proc = None
         self.sm, self.mx, self.reasons = [], 0.0, set()
         self.source = "none"
@@ -110,7 +117,8 @@ class Clocks:
         except Exception:  # noqa: BLE001
             pass
         try:
-            self.proc = subprocess.Popen([sys.executable, "-c", _CLOCK_SAMPLER, bus, str(self.index)],
+            extra = [self.log_path, "0.001"] if self.log_path else []
+            self.proc = subprocess.Popen([sys.executable, "-c", _CLOCK_SAMPLER, bus, str(self.index)] + extra,
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             first = self.proc.stdout.readline().split()
             if first and first[0] == "ready":
@@ -143,6 +151,13 @@ class Clocks:
                 out, _ = self.proc.communicate(timeout=5)
             except Exception:  # noqa: BLE001
                 self.proc.kill()
+        if self.nvml and self.log_path:
+            try:
+                with open(self.log_path) as f:
+                    out = f.read()
+                os.remove(self.log_path)
+            except OSError:
+                out = ""
         for line in (out or "").splitlines():
             if self.nvml:
                 f = line.split()
@@ -153,6 +168,7 @@ class Clocks:
                 except ValueError:
                     continue
                 self.near.append(mhz)
+                self.samples.append((ts, mhz, f[2]))
                 if not self.t0 <= ts <= self.t1:  # taken outside the block
                     continue
                 self.sm.append(mhz)
@@ -171,6 +187,17 @@ class Clocks:
             for n, v in zip(self.NAMES, f[5:9]):
                 if v.lower().startswith("active"):
                     self.reasons.add(n)
+
+    def windows_summary(self, windows) -> dict:
+        """SM clock and reasons over the samples inside any of `windows`
+        ((start, end) wall times): the timed loops of one group of legs."""
+        sm, reasons = [], set()
+        for ts, mhz, bits in self.samples:
+            if any(a <= ts <= b for a, b in windows):
+                sm.append(mhz)
+                reasons.update(n for n, bit in zip(self.NAMES, bits) if bit == "1")
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
 
     def summary(self) -> dict:
         sm = self.sm
@@ -235,6 +262,9 @@ def time_e2e(torch, loop, steps: int, warmup: int, barrier, stream, copy_stream)
     return e0.elapsed_time(e1) / steps
 
 
+TIMED_WINDOWS = []  # wall-clock (start, end) of every timed loop, for the clock record
+
+
 def time_loop(torch, fn, steps: int, warmup: int, barrier, stream):
     for _ in range(warmup):
         fn()
@@ -242,11 +272,13 @@ def time_loop(torch, fn, steps: int, warmup: int, barrier, stream):
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     e0.record(stream)
     for _ in range(steps):
         fn()
     e1.record(stream)
     torch.cuda.synchronize()
+    TIMED_WINDOWS.append((w0, time.time()))
     barrier()
     return e0.elapsed_time(e1) / steps  # ms per step
 
@@ -502,12 +534,32 @@ def run_ours(args) -> None:
     # ---- INT4 decode as a secondary line ---------------
     extra = {}
     if not args.no_int4:
-        extra = int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)
-        extra.update(prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
-        extra.update(evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
-        extra.update(long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
-        extra.update(multi_query_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
-        extra.update(ops_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank))
+        # Each leg starts from an empty allocator cache, so its buffers are
+        # fresh allocations rather than pieces of an earlier leg's segments.
+        legs = [lambda: int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank),
+                lambda: prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank),
+                lambda: evict_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n,
+                                    rank),
+                lambda: long_decode_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank),
+                lambda: multi_query_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank),
+                lambda: ops_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank)]
+        # SM clocks over each group's timed loops (the later legs run with the
+        # GPU warm, often under sw_power_cap), recorded with its legs.
+        groups = []
+        lclk = Clocks(local, log_path=os.path.join(tempfile.gettempdir(), f"memopt_leg_clocks_{os.getpid()}.log"))
+        with lclk:
+            for leg in legs:
+                torch.cuda.synchronize()
+                torch.cuda.empty_cache()
+                n0 = len(TIMED_WINDOWS)
+                r = leg()
+                groups.append((r, TIMED_WINDOWS[n0:]))
+        for r, wins in groups:
+            cs = lclk.windows_summary(wins)
+            for v in r.values():
+                if isinstance(v, dict):
+                    v["clocks"] = cs
+            extra.update(r)
         if ws_n > 1:
             extra.update(evict_head_sharded_extra(torch, memopt_C, dev, stream, group, ws_n))
 
@@ -575,7 +627,9 @@ def print_leg_summary(extra: dict, n: int) -> None:
                      if f in v), None)
         ms = next((v[f] for f in ("ms_per_step", "ms_per_call", "ms_per_launch") if f in v), None)
         fs = f" frac {frac:.3f}" if frac is not None else ""
-        print(f"leg {k} N={n}: {v['value']} {v['unit']}{fs} {ms} ms", flush=True)
+        c = v.get("clocks") or {}
+        cs = f" sm {c['sm_mhz']:.0f} MHz {','.join(c['reasons']) or '-'}" if c.get("sm_mhz") else ""
+        print(f"leg {k} N={n}: {v['value']} {v['unit']}{fs} {ms} ms{cs}", flush=True)
 
 
 def int4_extra(torch, memopt_C, _capi, dev, sp, stream, args, barrier, max_over_ranks, ws_n, rank):
@@ -669,6 +723,7 @@ def time_each(torch, fn, n: int, stream, flush=None) -> float:
     """Median device time (ms) of n calls timed one by one with CUDA events on
     `stream`; `flush` (untimed) runs before each call."""
     evs = []
+    w0 = time.time()
     for _ in range(n):
         if flush is not None:
             flush()
@@ -678,6 +733,7 @@ def time_each(torch, fn, n: int, stream, flush=None) -> float:
         e1.record(stream)
         evs.append((e0, e1))
     torch.cuda.synchronize()
+    TIMED_WINDOWS.append((w0, time.time()))
     return statistics.median(a.elapsed_time(b) for a, b in evs)
 
 
@@ -862,15 +918,19 @@ def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, 
     flops = 4.0 * pb * H * pql * pql * D
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            tpk = float(json.load(f)["bf16_tflops"])
-        kind = "measured"
+            pk = json.load(f)
+        tpk, kind = float(pk["bf16_tflops"]), "measured"
+        tpk_s = float(pk.get("bf16_tflops_sustained") or 0) or None
     except Exception:  # noqa: BLE001
-        tpk, kind = 1590.0, "fallback"
+        tpk, kind, tpk_s = 1590.0, "fallback", 1400.0
     tf = flops / (ms * 1e-3) / 1e12
     return {"prefill": {"workload": "BASELINE configs[4] prefill: 4 x 8192 tokens, 32 heads x 128, fp16, "
                                     "non-causal over context_lens=8192",
                         "value": round(tf * ws_n, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
                         "frac_of_tensor_peak": round(tf / tpk, 4), "peak_kind": kind, "flops_per_launch": flops,
+                        "frac_of_sustained_tensor_peak": round(tf / tpk_s, 4) if tpk_s else None,
+                        "note": "peak: the measured bf16 burst figure (a launch of ~4 ms timed alone); the "
+                                "sustained figure is the same GEMM under the power cap for seconds",
                         "kernel": "prefill_kernel<128,16> (tcgen05)"}}
 
 
