@@ -1,5 +1,6 @@
 """bench.py's host-side pieces on CPU: the algorithmic byte counts quoted for
-each leg, the leg summary lines and the clock sampler's fallback."""
+each leg, the leg summary lines, the clock sampler's fallback and the per-leg
+clock summary over the timed windows."""
 from __future__ import annotations
 
 import json
@@ -37,3 +38,33 @@ def test_clock_sampler_without_a_gpu_reports_no_samples():
         pass
     s = c.summary()
     assert s["samples"] == 0 or s["source"] in ("nvml", "nvidia-smi")
+
+
+def test_leg_clock_summary_counts_only_samples_inside_the_timed_windows(capsys):
+    c = bench.Clocks(0)
+    c.mx = 1965.0
+    c.samples = [(1.0, 1965.0, "0000"), (2.0, 1700.0, "0001"), (2.5, 1710.0, "0001"), (4.0, 1200.0, "1000")]
+    s = c.windows_summary([(1.5, 3.0)])
+    assert s == {"sm_mhz": 1705.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 2}
+    s = c.windows_summary([(0.5, 1.5), (3.5, 4.5)])
+    assert s["samples"] == 2 and s["reasons"] == ["hw_slowdown"]
+    assert c.windows_summary([])["sm_mhz"] is None
+    bench.print_leg_summary({"prefill": {"value": 2.0, "unit": "TFLOP/s", "ms_per_step": 4.0,
+                                         "clocks": {"sm_mhz": 1705.0, "reasons": ["sw_power_cap"]}}}, 1)
+    assert capsys.readouterr().out.strip().endswith("sm 1705 MHz sw_power_cap")
+
+
+def test_timed_loops_record_their_wall_windows():
+    class _S:  # a stream stand-in (no GPU here); the events and synchronize are faked below
+        pass
+
+    n0 = len(bench.TIMED_WINDOWS)
+    calls = []
+    ev = type("E", (), {"record": lambda self, s: None, "elapsed_time": lambda self, o: 2.0})
+    fake = type("T", (), {"cuda": type("C", (), {"Event": staticmethod(lambda enable_timing: ev()),
+                                                  "synchronize": staticmethod(lambda: None)})})
+    ms = bench.time_loop(fake, lambda: calls.append(1), 4, 3, lambda: None, _S())
+    assert ms == 0.5 and len(calls) == 7
+    assert bench.time_each(fake, lambda: calls.append(1), 3, _S()) == 2.0
+    w = bench.TIMED_WINDOWS[n0:]
+    assert len(w) == 2 and all(a <= b for a, b in w)
