@@ -289,6 +289,15 @@ size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads
 size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len, int num_heads, int num_kv_heads,
                                                 int head_dim, int max_blocks_per_seq, int block_size,
                                                 int max_seq_len, int window_size);
+/* Workspace of memopt_paged_attention_int4 / _int4_ex: the size above plus,  */
+/* for q_len >= 64 (head_dim 64/128, block_size 16/32), an fp16 scratch of   */
+/* batch * max_blocks_per_seq pages into which the call dequantises the      */
+/* sequences' INT4 pages before running the tcgen05 prefill kernel on them,  */
+/* as the reference dequantises an INT4 cache before fp16 attention          */
+/* (quantization.cu:371-428 -> attention.cu:371-521).  Ticket rules as above. */
+size_t memopt_paged_attention_int4_workspace_size_ex(int batch, int q_len, int num_heads, int num_kv_heads,
+                                                     int head_dim, int max_blocks_per_seq, int block_size,
+                                                     int max_seq_len, int window_size);
 /* Bytes at the start of the workspace that hold tickets (must start zeroed). */
 size_t memopt_paged_attention_ticket_bytes(int batch, int q_len, int num_heads);
 

@@ -23,6 +23,12 @@ int prefill_f16(const void* query, const void* kpool, const void* vpool, const i
                 int B, int QL, int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal,
                 void* out, cudaStream_t s);
 constexpr int kPrefillMinRows = 64;
+// INT4 pools: pages dequantised into an fp16 scratch, then the same kernel.
+bool prefill_int4_supported(int D, int BS);
+size_t prefill_int4_scratch_bytes(int B, int KVH, int D, int MB, int BS);
+int prefill_int4(const void* query, const uint8_t* pages, const int32_t* bt, const int32_t* ctx, int B, int QL,
+                 int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal, void* out,
+                 void* scratch, size_t scratch_bytes, cudaStream_t s);
 
 // One predicate for the workspace size and the dispatch: q_len >= 64 runs on
 // the tcgen05 prefill kernel (no split-K workspace); MEMOPT_DISABLE_PREFILL=1
@@ -148,8 +154,14 @@ WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
 // Multi-query decode: at least two query rows per KV head, and for the fp16
 // pool a q_len below the prefill threshold (the INT4 pool has no prefill
 // kernel: every q_len runs here).
-bool use_mq(bool int4, int q_len, int H, int KVH) {
-  return (int4 || !use_prefill(q_len)) && KVH > 0 && (H / KVH) * q_len >= 2;
+// INT4 calls of q_len >= 64 take the prefill path when its kernel supports
+// (head_dim, block_size); otherwise, like every call below 64 rows with at
+// least two query rows per KV head, the multi-query decode kernel.
+bool use_prefill_int4(int q_len, int D, int BS) { return use_prefill(q_len) && prefill_int4_supported(D, BS); }
+
+bool use_mq(bool int4, int q_len, int H, int KVH, int D, int BS) {
+  const bool prefill = int4 ? use_prefill_int4(q_len, D, BS) : use_prefill(q_len);
+  return !prefill && KVH > 0 && (H / KVH) * q_len >= 2;
 }
 // Query rows per tile: 16 on the fp16 pool, 8 on the INT4 pool (whose score
 // mma holds each row's two integer halves as separate rows).
@@ -403,7 +415,7 @@ extern "C" size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len,
                              head_dim).total;
   if (b > need) need = b;
   for (int f = 0; f < 2; ++f) {
-    if (!use_mq(f == 1, q_len, num_heads, num_kv_heads)) continue;
+    if (!use_mq(f == 1, q_len, num_heads, num_kv_heads, head_dim, block_size)) continue;
     const size_t c = ws_layout(pairs,
                                mq_split(f == 1, batch, q_len, num_heads, num_kv_heads, max_blocks_per_seq,
                                         block_size, w).n_chunks,
@@ -411,6 +423,17 @@ extern "C" size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len,
     if (c > need) need = c;
   }
   return need;
+}
+
+extern "C" size_t memopt_paged_attention_int4_workspace_size_ex(int batch, int q_len, int num_heads,
+                                                                int num_kv_heads, int head_dim,
+                                                                int max_blocks_per_seq, int block_size,
+                                                                int max_seq_len, int window_size) {
+  const size_t split = memopt_paged_attention_workspace_size_ex(batch, q_len, num_heads, num_kv_heads, head_dim,
+                                                                max_blocks_per_seq, block_size, max_seq_len,
+                                                                window_size);
+  if (batch <= 0 || q_len <= 0 || num_kv_heads <= 0 || !use_prefill_int4(q_len, head_dim, block_size)) return split;
+  return align256(split) + prefill_int4_scratch_bytes(batch, num_kv_heads, head_dim, max_blocks_per_seq, block_size);
 }
 
 extern "C" size_t memopt_paged_attention_workspace_size(int batch, int q_len, int num_heads,
@@ -449,7 +472,7 @@ extern "C" int memopt_paged_attention_f16_ex(const void* query, const void* key_
     return prefill_f16(query, key_pool, value_pool, block_tables, context_lens, batch, q_len, num_heads,
                        num_kv_heads, head_dim, max_blocks_per_seq, num_blocks, block_size, p.window, causal, out,
                        as_stream(stream));
-  if (use_mq(false, q_len, num_heads, num_kv_heads))
+  if (use_mq(false, q_len, num_heads, num_kv_heads, head_dim, block_size))
     return run_mq(p, key_pool, value_pool, head_dim, block_size, workspace, workspace_bytes, as_stream(stream));
   alignas(64) CUtensorMap km, vm;
   st = make_pool_map(&km, key_pool, num_blocks * block_size, num_kv_heads, head_dim, block_size);
@@ -489,7 +512,18 @@ extern "C" int memopt_paged_attention_int4_ex(const void* query, const uint8_t* 
   if (reinterpret_cast<uintptr_t>(kv_pages) & 15u)
     return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: pages must be 16-byte aligned");
   p.pages = kv_pages;
-  if (use_mq(true, q_len, num_heads, num_kv_heads))
+  if (use_prefill_int4(q_len, head_dim, block_size)) {
+    // The fp16 page scratch follows the split workspace (whose tickets stay zero).
+    const size_t off = align256(memopt_paged_attention_workspace_size_ex(
+        batch, q_len, num_heads, num_kv_heads, head_dim, max_blocks_per_seq, block_size, max_seq_len, window_size));
+    if (workspace == nullptr || workspace_bytes < off)
+      return fail(MEMOPT_ERR_WORKSPACE, "dynamic_sparse_attention_int4: workspace too small (size it with "
+                                        "memopt_paged_attention_int4_workspace_size_ex)");
+    return prefill_int4(query, kv_pages, block_tables, context_lens, batch, q_len, num_heads, num_kv_heads, head_dim,
+                        max_blocks_per_seq, num_blocks, block_size, p.window, causal, out,
+                        static_cast<uint8_t*>(workspace) + off, workspace_bytes - off, as_stream(stream));
+  }
+  if (use_mq(true, q_len, num_heads, num_kv_heads, head_dim, block_size))
     return run_mq(p, nullptr, kv_pages, head_dim, block_size, workspace, workspace_bytes, as_stream(stream));
   alignas(64) CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));

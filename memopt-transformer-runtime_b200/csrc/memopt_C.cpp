@@ -438,10 +438,11 @@ std::mutex g_ws_mu;
 std::map<std::pair<int, cudaStream_t>, WsEntry> g_ws;
 
 torch::Tensor attn_workspace(const torch::Tensor& query, int KVH, int MB, int BS, int max_seq_len,
-                             int window_size, size_t* bytes) {
+                             int window_size, size_t* bytes, bool int4 = false) {
   const int B = static_cast<int>(query.size(0)), QL = static_cast<int>(query.size(1));
   const int H = static_cast<int>(query.size(2)), D = static_cast<int>(query.size(3));
-  *bytes = memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, max_seq_len, window_size);
+  *bytes = int4 ? memopt_paged_attention_int4_workspace_size_ex(B, QL, H, KVH, D, MB, BS, max_seq_len, window_size)
+                : memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, max_seq_len, window_size);
   if (*bytes == 0) return torch::Tensor();
   const size_t tb = memopt_paged_attention_ticket_bytes(B, QL, H);
   cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
@@ -532,7 +533,7 @@ torch::Tensor dynamic_sparse_attention_int4(torch::Tensor query, torch::Tensor k
   const at::cuda::CUDAGuard g(query.device());
   auto q = aligned_contig(query);
   size_t wsb = 0;
-  auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb);
+  auto ws = attn_workspace(q, KVH, MB, BS, max_seq_len, window_size, &wsb, true);
   check_attn(memopt_paged_attention_int4_ex(q.data_ptr(), kv_pages.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
                                        context_lens.data_ptr<int32_t>(), B, QL, H, KVH, D, MB, kv_pages.size(0), BS,
                                        max_seq_len, window_size, causal ? 1 : 0, out.data_ptr(),

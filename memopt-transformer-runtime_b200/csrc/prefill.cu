@@ -39,6 +39,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "int4.cuh"
 #include "tc.cuh"
 
 namespace memopt {
@@ -564,6 +565,130 @@ extern "C" __attribute__((visibility("default"))) int memopt_prefill_trace(unsig
   return static_cast<int>(cudaMemcpyFromSymbol(host, prefill::g_pf_trace, sizeof(prefill::g_pf_trace)));
 }
 #endif
+
+// ---- INT4 pools: pages dequantised into an fp16 paged scratch, then the
+// fp16 prefill kernel.  This follows the reference's INT4 path
+// (quantization.cu:371-428: dequantize_kv_cache_int4 into an fp16 cache,
+// then fp16 attention): every K and V value is (code - 8) * its group's fp16
+// scale, exact in fp32 and rounded once to fp16.
+namespace {
+
+// One CTA per (sequence, block-table slot); its warps take the KV heads and
+// each lane one (token, 64-dim group) unit: 32 code bytes and one scale in,
+// 64 fp16 values (128 bytes) out, for K and for V.  Scratch page b * MB + i
+// holds slot i of sequence b; its table entry is -1 where the slot is a hole
+// (entry < 0 or >= NB) or lies past the sequence's context, which the
+// prefill kernel skips exactly as it skips such entries of an fp16 pool.
+template <int D, int BS>
+__global__ void __launch_bounds__(128) int4_pages_to_f16_kernel(const uint8_t* __restrict__ pages,
+                                                                const int32_t* __restrict__ bt,
+                                                                const int32_t* __restrict__ ctx, int MB,
+                                                                int64_t NB, int KVH, __half* __restrict__ k16,
+                                                                __half* __restrict__ v16,
+                                                                int32_t* __restrict__ bt16) {
+  constexpr int G = D / 64;
+  constexpr int64_t kPage = static_cast<int64_t>(BS) * D + static_cast<int64_t>(BS) * G * 4;
+  const int i = blockIdx.x, b = blockIdx.y;
+  const int64_t slot = static_cast<int64_t>(b) * MB + i;
+  const int c = __ldg(ctx + b);
+  const int e = __ldg(bt + slot);
+  const bool valid = e >= 0 && e < NB && c > 0 && i < (c + BS - 1) / BS;
+  if (threadIdx.x == 0) bt16[slot] = valid ? static_cast<int32_t>(slot) : -1;
+  if (!valid) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int h = warp; h < KVH; h += 4) {
+    const uint8_t* pg = pages + (static_cast<int64_t>(e) * KVH + h) * kPage;
+    const __half* ks = reinterpret_cast<const __half*>(pg + BS * D);
+    const __half* vs = reinterpret_cast<const __half*>(pg + BS * D + BS * G * 2);
+    for (int u = lane; u < BS * G; u += 32) {
+      const int pos = u / G, g = u - pos * G;
+      const int vg = (D == 128 && (pos & 2)) ? g ^ 1 : g;  // V rows with bit 1 set store their halves swapped
+      const uint4* kc = reinterpret_cast<const uint4*>(pg + pos * (D / 2) + 32 * g);
+      const uint4* vc = reinterpret_cast<const uint4*>(pg + BS * (D / 2) + pos * (D / 2) + 32 * vg);
+      const float sk = __half2float(ks[pos * G + g]);
+      const float sv = __half2float(vs[int4_vscale_index(pos, g, G)]);
+      const int64_t orow = ((slot * BS + pos) * KVH + h) * D + 64 * g;
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv) {
+        const uint4* src = kv ? vc : kc;
+        const float sc = kv ? sv : sk;
+        uint4* dst = reinterpret_cast<uint4*>((kv ? v16 : k16) + orow);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint4 w = src[q];
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // 4 bytes = 8 codes = 8 dims -> one 16-byte store
+            uint32_t hv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t byte = (words[k] >> (8 * j)) & 0xFFu;
+              const __half2 pr = __floats2half2_rn(static_cast<float>(static_cast<int>(byte & 15u) - 8) * sc,
+                                                   static_cast<float>(static_cast<int>(byte >> 4) - 8) * sc);
+              hv[j] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            dst[4 * q + k] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          }
+        }
+      }
+    }
+  }
+}
+
+struct Int4Scratch {
+  size_t k, v, bt, total;
+};
+Int4Scratch int4_scratch_layout(int B, int KVH, int D, int MB, int BS) {
+  auto a256 = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  Int4Scratch l{};
+  const size_t kv = a256(static_cast<size_t>(B) * MB * BS * KVH * D * 2);
+  l.k = 0;
+  l.v = kv;
+  l.bt = 2 * kv;
+  l.total = 2 * kv + a256(static_cast<size_t>(B) * MB * 4);
+  return l;
+}
+
+}  // namespace
+
+int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,
+                int B, int QL, int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal,
+                void* out, cudaStream_t s);
+
+bool prefill_int4_supported(int D, int BS) { return (D == 64 || D == 128) && (BS == 16 || BS == 32); }
+
+size_t prefill_int4_scratch_bytes(int B, int KVH, int D, int MB, int BS) {
+  if (B <= 0 || KVH <= 0 || MB <= 0 || !prefill_int4_supported(D, BS)) return 0;
+  return int4_scratch_layout(B, KVH, D, MB, BS).total;
+}
+
+// Called by memopt_paged_attention_int4_ex for q_len >= kPrefillMinRows;
+// `scratch` (prefill_int4_scratch_bytes) is 256-byte aligned.
+int prefill_int4(const void* query, const uint8_t* pages, const int32_t* bt, const int32_t* ctx, int B, int QL,
+                 int H, int KVH, int D, int MB, int64_t NB, int BS, int window_clamped, int causal, void* out,
+                 void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (!prefill_int4_supported(D, BS)) return fail(MEMOPT_ERR_UNSUPPORTED, "prefill_int4: unsupported (block_size, head_dim)");
+  const Int4Scratch l = int4_scratch_layout(B, KVH, D, MB, BS);
+  if (scratch == nullptr || scratch_bytes < l.total || (reinterpret_cast<uintptr_t>(scratch) & 255u))
+    return fail(MEMOPT_ERR_WORKSPACE, "dynamic_sparse_attention_int4: workspace too small for the fp16 page scratch "
+                                      "(need " + std::to_string(l.total) + " bytes past the split workspace)");
+  const int64_t nb16 = static_cast<int64_t>(B) * MB;
+  if (B > 65535) return fail(MEMOPT_ERR_UNSUPPORTED, "prefill_int4: more than 65535 sequences");
+  if (nb16 * BS > 0x7fffffffLL) return fail(MEMOPT_ERR_UNSUPPORTED, "prefill_int4: more than 2^31 scratch rows");
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  __half* k16 = reinterpret_cast<__half*>(base + l.k);
+  __half* v16 = reinterpret_cast<__half*>(base + l.v);
+  int32_t* bt16 = reinterpret_cast<int32_t*>(base + l.bt);
+  const dim3 grid(MB, B);
+#define MEMOPT_INT4_GATHER(DD, BB)                                                                                int4_pages_to_f16_kernel<DD, BB><<<grid, 128, 0, s>>>(pages, bt, ctx, MB, NB, KVH, k16, v16, bt16)
+  if (D == 128 && BS == 16) MEMOPT_INT4_GATHER(128, 16);
+  else if (D == 128 && BS == 32) MEMOPT_INT4_GATHER(128, 32);
+  else if (D == 64 && BS == 16) MEMOPT_INT4_GATHER(64, 16);
+  else MEMOPT_INT4_GATHER(64, 32);
+#undef MEMOPT_INT4_GATHER
+  MEMOPT_LAUNCH_CHECK("int4_pages_to_f16_kernel launch");
+  return prefill_f16(query, k16, v16, bt16, ctx, B, QL, H, KVH, D, MB, nb16, BS, window_clamped, causal, out, s);
+}
 
 // Called by memopt_paged_attention_f16 for q_len >= kPrefillMinRows.
 int prefill_f16(const void* query, const void* kpool, const void* vpool, const int32_t* bt, const int32_t* ctx,

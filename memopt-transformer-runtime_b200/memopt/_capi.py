@@ -29,6 +29,7 @@ def lib() -> C.CDLL:
         _lib.memopt_last_error.restype = C.c_char_p
         _lib.memopt_paged_attention_workspace_size.restype = SZ
         _lib.memopt_paged_attention_workspace_size_ex.restype = SZ
+        _lib.memopt_paged_attention_int4_workspace_size_ex.restype = SZ
         _lib.memopt_paged_attention_ticket_bytes.restype = SZ
     return _lib
 
@@ -93,6 +94,12 @@ def evict_topk_compact_int4(scores, bt, ctx, pages, block_size, head_dim, retain
 
 def workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win) -> int:
     return int(lib().memopt_paged_attention_workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win))
+
+
+def int4_workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win) -> int:
+    """Workspace of an INT4-pool call: the split workspace plus, for q_len >=
+    64, the fp16 page scratch of the prefill path."""
+    return int(lib().memopt_paged_attention_int4_workspace_size_ex(B, QL, H, KVH, D, MB, BS, msl, win))
 
 
 def workspace_size(B, QL, H, D, MB, BS, msl, win) -> int:

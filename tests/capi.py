@@ -80,9 +80,10 @@ def evict_cache(scores, kpool, vpool, r):
                                 F(r), stream()))
 
 
-def workspace(B, QL, H, D, MB, BS, msl, win, device="cuda", kvh=None):
-    lib().memopt_paged_attention_workspace_size_ex.restype = SZ
-    n = lib().memopt_paged_attention_workspace_size_ex(B, QL, H, H if kvh is None else kvh, D, MB, BS, msl, win)
+def workspace(B, QL, H, D, MB, BS, msl, win, device="cuda", kvh=None, int4=False):
+    fn = lib().memopt_paged_attention_int4_workspace_size_ex if int4 else lib().memopt_paged_attention_workspace_size_ex
+    fn.restype = SZ
+    n = fn(B, QL, H, H if kvh is None else kvh, D, MB, BS, msl, win)
     if n == 0:
         return None, 0
     ws = torch.zeros(n, dtype=torch.uint8, device=device)
@@ -108,7 +109,7 @@ def attention_int4(q, pages, block_size, bt, ctx, msl, win, ws=None):
     MB = bt.shape[1]
     out = torch.empty_like(q)
     if ws is None:
-        ws, n = workspace(B, QL, H, D, MB, block_size, msl, win)
+        ws, n = workspace(B, QL, H, D, MB, block_size, msl, win, int4=True)
     else:
         n = ws.numel()
     ok(lib().memopt_paged_attention_int4(ptr(q), ptr(pages), ptr(bt), ptr(ctx), I(B), I(QL), I(H), I(D), I(MB),
@@ -212,7 +213,7 @@ def attention_int4_ex(q, pages, block_size, bt, ctx, msl, win, causal=False):
     B, QL, H, D = q.shape
     MB = bt.shape[1]
     out = torch.empty_like(q)
-    ws, n = workspace(B, QL, H, D, MB, block_size, msl, win, kvh=pages.shape[1])
+    ws, n = workspace(B, QL, H, D, MB, block_size, msl, win, kvh=pages.shape[1], int4=True)
     ok(lib().memopt_paged_attention_int4_ex(ptr(q), ptr(pages), ptr(bt), ptr(ctx), I(B), I(QL), I(H),
                                             I(pages.shape[1]), I(D), I(MB), I64(pages.shape[0]), I(block_size),
                                             I(msl), I(win), I(int(causal)), ptr(out), ptr(ws), SZ(n), stream()))

@@ -15,6 +15,7 @@ import oracle as O
 
 pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-3, 1e-2
+WORKSPACE_ERR = -6  # MEMOPT_ERR_WORKSPACE
 DEV = "cuda"
 
 
@@ -504,7 +505,7 @@ def test_attention_multi_query_f16_vs_oracle(case):
 
 
 @pytest.mark.parametrize("case", MQ_CASES + [
-    (2, 70, 4, 2, 128, 16, [200, 90], 16, 256, 256, True, 0.0),    # INT4 has no prefill kernel: q_len 70
+    (2, 70, 4, 2, 128, 16, [200, 90], 16, 256, 256, True, 0.0),    # q_len 70: the INT4 prefill path
     (1, 2, 2, 2, 64, 16, [50], 4, 64, 64, False, 0.0),             # MHA q_len 2, D 64
 ])
 def test_attention_multi_query_int4_vs_oracle(case):
@@ -520,6 +521,75 @@ def test_attention_multi_query_int4_vs_oracle(case):
                                  torch.from_numpy(cl).to(DEV), msl, win, causal)
     ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS, causal=causal)
     np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+# --------------------- INT4 prefill (q_len >= 64: pages -> fp16 scratch -> tcgen05)
+INT4_PREFILL_CASES = [
+    # B, QL, H, KVH, D, BS, ctx, MB, max_seq_len, window, causal, holes
+    (1, 64, 2, 2, 128, 16, [128], 8, 128, 128, False, 0.0),
+    (2, 130, 4, 2, 128, 16, [300, 77], 20, 320, 320, False, 0.0),
+    (2, 256, 4, 4, 64, 16, [1000, 1024], 64, 1024, 1024, False, 0.1),
+    (1, 200, 4, 2, 128, 32, [777], 30, 960, 300, False, 0.1),
+    (1, 200, 4, 2, 128, 16, [777], 64, 1024, 1024, True, 0.0),   # causal GQA
+    (2, 130, 8, 2, 64, 16, [300, 1000], 64, 1024, 256, True, 0.1),  # causal window, holes
+    (2, 64, 2, 1, 64, 32, [64, 0], 4, 128, -1, False, 0.0),        # MQA, an empty context
+    (1, 512, 8, 8, 128, 16, [4096], 256, 4096, 1000, False, 0.0),
+]
+
+
+def _int4_pages(kp, vp, BS):
+    NB, _, KVH, D = kp.shape
+    T = NB * BS
+    pages = torch.zeros(NB, KVH, capi.int4_page_bytes(BS, D), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(torch.from_numpy(kp.reshape(T, KVH, D)).to(DEV), torch.from_numpy(vp.reshape(T, KVH, D)).to(DEV),
+                          torch.from_numpy(np.arange(T, dtype=np.int32)).to(DEV), pages, BS)
+    return pages
+
+
+@pytest.mark.parametrize("case", INT4_PREFILL_CASES)
+def test_prefill_int4_vs_oracle(case):
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = case
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, QL * 19 + H + KVH)
+    pages = _int4_pages(kp, vp, BS)
+    got = capi.attention_int4_ex(torch.from_numpy(q).to(DEV), pages, BS, torch.from_numpy(bt).to(DEV),
+                                 torch.from_numpy(cl).to(DEV), msl, win, causal)
+    # the oracle dequantises exactly (fp64); the device rounds K and V to fp16 as the reference does
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS, causal=causal)
+    np.testing.assert_allclose(np16(got).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_prefill_int4_workspace_size_scratch_and_reuse():
+    B, QL, H, KVH, D, BS, ctx, MB, msl, win, causal, holes = INT4_PREFILL_CASES[1]
+    q, kp, vp, bt, cl = _gqa_case(B, QL, H, KVH, D, BS, ctx, MB, holes, 3)
+    pages = _int4_pages(kp, vp, BS)
+    gq, gbt, gcl = (torch.from_numpy(a).to(DEV) for a in (q, bt, cl))
+    small, n_small = capi.workspace(B, QL, H, D, MB, BS, msl, win, kvh=KVH)
+    ws, n = capi.workspace(B, QL, H, D, MB, BS, msl, win, kvh=KVH, int4=True)
+    assert n >= n_small + B * MB * BS * KVH * D * 4  # fp16 K and V scratch past the split workspace
+    lib = capi.lib()
+
+    def call(qt, out, ws_t, n_ws, causal_flag):
+        return lib.memopt_paged_attention_int4_ex(
+            capi.ptr(qt), capi.ptr(pages), capi.ptr(gbt), capi.ptr(gcl), capi.I(B), capi.I(qt.shape[1]), capi.I(H),
+            capi.I(KVH), capi.I(D), capi.I(MB), capi.I64(pages.shape[0]), capi.I(BS), capi.I(msl), capi.I(win),
+            capi.I(int(causal_flag)), capi.ptr(out), capi.ptr(ws_t), capi.SZ(n_ws), capi.stream())
+
+    out = torch.empty_like(gq)
+    if small is not None:
+        assert call(gq, out, small, n_small, causal) == WORKSPACE_ERR  # no room for the scratch
+        assert b"workspace" in lib.memopt_last_error()
+    assert call(gq, out, ws, n, causal) == 0
+    ref = O.paged_attention_int4(q, np16(pages), bt, cl, msl, win, BS, causal=causal)
+    np.testing.assert_allclose(np16(out).astype(np.float64), ref, atol=ATOL, rtol=RTOL)
+    tickets = lib.memopt_paged_attention_ticket_bytes(B, QL, H)
+    assert int(ws[:tickets].count_nonzero().item()) == 0
+    # a decode call (one query row) on the same workspace after the prefill
+    q1 = np.ascontiguousarray(q[:, -1:])
+    g1 = torch.from_numpy(q1).to(DEV)
+    o1 = torch.empty_like(g1)
+    assert call(g1, o1, ws, n, False) == 0
+    ref1 = O.paged_attention_int4(q1, np16(pages), bt, cl, msl, win, BS, causal=False)
+    np.testing.assert_allclose(np16(o1).astype(np.float64), ref1, atol=ATOL, rtol=RTOL)
 
 
 def test_attention_multi_query_deterministic_and_tickets_reset():
