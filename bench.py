@@ -614,7 +614,7 @@ LEG_ORDER = ["evict_tokens", "evict_tokens_l2_flushed", "evict_tokens_no_sinks_l
              "evict_topk_compact", "evict_topk_compact_int4",
              "evict_topk_head_sharded", "window_decode", "quantize_int4", "dequantize_int4", "write_cache_f16",
              "multi_row_decode_f16", "gqa_decode_f16", "gqa_decode_int4", "long_context_decode_retain_0.75",
-             "long_context_decode", "prefill", "int4_write_cache", "int4_decode"]
+             "long_context_decode", "int4_prefill", "prefill", "int4_write_cache", "int4_decode"]
 
 
 def print_leg_summary(extra: dict, n: int) -> None:
@@ -924,7 +924,34 @@ def prefill_extra(torch, _capi, dev, sp, stream, args, barrier, max_over_ranks, 
     except Exception:  # noqa: BLE001
         tpk, kind, tpk_s = 1590.0, "fallback", 1400.0
     tf = flops / (ms * 1e-3) / 1e12
-    return {"prefill": {"workload": "BASELINE configs[4] prefill: 4 x 8192 tokens, 32 heads x 128, fp16, "
+    # The same prefill over an INT4 pool holding those K/V rows: the call
+    # dequantises the sequences' pages into an fp16 scratch in its workspace,
+    # then runs the same kernel (the reference dequantises an INT4 cache before
+    # fp16 attention).  Same FLOPs; the dequantisation is inside the time.
+    nb = kp.shape[0]
+    pbytes = BS * D + BS * (D // 64) * 4
+    pages = torch.zeros(nb, H, pbytes, dtype=torch.uint8, device=dev)
+    slots = torch.arange(nb * BS, dtype=torch.int32, device=dev)
+    _capi.write_cache_int4(kp.view(-1, H, D), vp.view(-1, H, D), slots, pages, BS, sp)
+    del kp, vp, slots
+    mb = bt.shape[1]
+    wsb4 = _capi.int4_workspace_size_ex(pb, pql, H, H, D, mb, BS, pql, pql)
+    ws4 = torch.zeros(max(wsb4, 1), dtype=torch.uint8, device=dev)
+
+    def step4():
+        _capi.paged_attention_int4(q, pages, BS, bt, ctx, out, pql, pql, ws4, wsb4, sp)
+
+    ms4 = max_over_ranks(time_loop(torch, step4, steps, args.warmup, barrier, stream))
+    tf4 = flops / (ms4 * 1e-3) / 1e12
+    del pages, ws4
+    int4_leg = {"workload": "BASELINE configs[4] prefill over an INT4 pool (the same K/V rows written by the fused "
+                            "INT4 write_cache): 4 x 8192 tokens, 32 heads x 128, non-causal",
+                "value": round(tf4 * ws_n, 2), "unit": "TFLOP/s", "ms_per_step": round(ms4, 4),
+                "frac_of_tensor_peak": round(tf4 / tpk, 4), "peak_kind": kind,
+                "workspace_bytes": wsb4,
+                "kernel": "int4_pages_to_f16_kernel (pages -> fp16 scratch) + prefill_kernel<128,16> (tcgen05)"}
+    return {"int4_prefill": int4_leg,
+            "prefill": {"workload": "BASELINE configs[4] prefill: 4 x 8192 tokens, 32 heads x 128, fp16, "
                                     "non-causal over context_lens=8192",
                         "value": round(tf * ws_n, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
                         "frac_of_tensor_peak": round(tf / tpk, 4), "peak_kind": kind, "flops_per_launch": flops,

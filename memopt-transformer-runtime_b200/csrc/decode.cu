@@ -151,10 +151,8 @@ WsLayout ws_layout(int64_t pairs, int n_chunks, int D) {
   return w;
 }
 
-// Multi-query decode: at least two query rows per KV head, and for the fp16
-// pool a q_len below the prefill threshold (the INT4 pool has no prefill
-// kernel: every q_len runs here).
-// INT4 calls of q_len >= 64 take the prefill path when its kernel supports
+// Multi-query decode: at least two query rows per KV head and a q_len below
+// the prefill threshold.  INT4 calls of q_len >= 64 take the prefill path when its kernel supports
 // (head_dim, block_size); otherwise, like every call below 64 rows with at
 // least two query rows per KV head, the multi-query decode kernel.
 bool use_prefill_int4(int q_len, int D, int BS) { return use_prefill(q_len) && prefill_int4_supported(D, BS); }

@@ -573,12 +573,13 @@ extern "C" __attribute__((visibility("default"))) int memopt_prefill_trace(unsig
 // scale, exact in fp32 and rounded once to fp16.
 namespace {
 
-// One CTA per (sequence, block-table slot); its warps take the KV heads and
-// each lane one (token, 64-dim group) unit: 32 code bytes and one scale in,
-// 64 fp16 values (128 bytes) out, for K and for V.  Scratch page b * MB + i
-// holds slot i of sequence b; its table entry is -1 where the slot is a hole
-// (entry < 0 or >= NB) or lies past the sequence's context, which the
-// prefill kernel skips exactly as it skips such entries of an fp16 pool.
+// One CTA per (sequence, block-table slot, 4 KV heads), one warp per head.
+// D/8 lanes cover one token row (each 8 dims: 4 code bytes in, one 16-byte
+// fp16 store out), so a warp instruction writes 32/(D/8) whole rows of K or
+// V; every value is (code - 8) * its group's fp16 scale.  Scratch page
+// b * MB + i holds slot i of sequence b; its table entry is -1 where the slot
+// is a hole (entry < 0 or >= NB) or lies past the sequence's context, which
+// the prefill kernel skips exactly as it skips such entries of an fp16 pool.
 template <int D, int BS>
 __global__ void __launch_bounds__(128) int4_pages_to_f16_kernel(const uint8_t* __restrict__ pages,
                                                                 const int32_t* __restrict__ bt,
@@ -587,50 +588,49 @@ __global__ void __launch_bounds__(128) int4_pages_to_f16_kernel(const uint8_t* _
                                                                 __half* __restrict__ v16,
                                                                 int32_t* __restrict__ bt16) {
   constexpr int G = D / 64;
+  constexpr int LPR = D / 8;        // lanes per token row
+  constexpr int RPI = 32 / LPR;     // rows per warp instruction
   constexpr int64_t kPage = static_cast<int64_t>(BS) * D + static_cast<int64_t>(BS) * G * 4;
-  const int i = blockIdx.x, b = blockIdx.y;
+  const int hq = (KVH + 3) / 4;
+  const int i = blockIdx.x / hq, b = blockIdx.y;
   const int64_t slot = static_cast<int64_t>(b) * MB + i;
   const int c = __ldg(ctx + b);
   const int e = __ldg(bt + slot);
   const bool valid = e >= 0 && e < NB && c > 0 && i < (c + BS - 1) / BS;
-  if (threadIdx.x == 0) bt16[slot] = valid ? static_cast<int32_t>(slot) : -1;
+  const int hg = blockIdx.x - i * hq;
+  if (threadIdx.x == 0 && hg == 0) bt16[slot] = valid ? static_cast<int32_t>(slot) : -1;
   if (!valid) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int h = warp; h < KVH; h += 4) {
-    const uint8_t* pg = pages + (static_cast<int64_t>(e) * KVH + h) * kPage;
-    const __half* ks = reinterpret_cast<const __half*>(pg + BS * D);
-    const __half* vs = reinterpret_cast<const __half*>(pg + BS * D + BS * G * 2);
-    for (int u = lane; u < BS * G; u += 32) {
-      const int pos = u / G, g = u - pos * G;
-      const int vg = (D == 128 && (pos & 2)) ? g ^ 1 : g;  // V rows with bit 1 set store their halves swapped
-      const uint4* kc = reinterpret_cast<const uint4*>(pg + pos * (D / 2) + 32 * g);
-      const uint4* vc = reinterpret_cast<const uint4*>(pg + BS * (D / 2) + pos * (D / 2) + 32 * vg);
-      const float sk = __half2float(ks[pos * G + g]);
-      const float sv = __half2float(vs[int4_vscale_index(pos, g, G)]);
-      const int64_t orow = ((slot * BS + pos) * KVH + h) * D + 64 * g;
+  const int h = hg * 4 + warp;
+  if (h >= KVH) return;
+  const uint8_t* pg = pages + (static_cast<int64_t>(e) * KVH + h) * kPage;
+  const __half* ks = reinterpret_cast<const __half*>(pg + BS * D);
+  const __half* vs = reinterpret_cast<const __half*>(pg + BS * D + BS * G * 2);
+  const int cl = lane % LPR;      // 8-dim chunk of the row: code bytes 4 cl .. 4 cl + 3
+  const int g = cl / 8;           // its 64-dim scale group
 #pragma unroll
-      for (int kv = 0; kv < 2; ++kv) {
-        const uint4* src = kv ? vc : kc;
-        const float sc = kv ? sv : sk;
-        uint4* dst = reinterpret_cast<uint4*>((kv ? v16 : k16) + orow);
+  for (int r0 = 0; r0 < BS; r0 += RPI) {
+    const int pos = r0 + lane / LPR;
+    // V rows whose position has bit 1 set hold their two 32-byte halves swapped (D = 128)
+    const int vb = (D == 128 && (pos & 2)) ? (4 * cl) ^ 32 : 4 * cl;
+    const uint32_t kw = *reinterpret_cast<const uint32_t*>(pg + pos * (D / 2) + 4 * cl);
+    const uint32_t vw = *reinterpret_cast<const uint32_t*>(pg + BS * (D / 2) + pos * (D / 2) + vb);
+    const float sk = __half2float(ks[pos * G + g]);
+    const float sv = __half2float(vs[int4_vscale_index(pos, g, G)]);
+    const int64_t orow = ((slot * BS + pos) * KVH + h) * D + 8 * cl;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint4 w = src[q];
-          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint32_t w = kv ? vw : kw;
+      const float sc = kv ? sv : sk;
+      uint32_t hv[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {  // 4 bytes = 8 codes = 8 dims -> one 16-byte store
-            uint32_t hv[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t byte = (words[k] >> (8 * j)) & 0xFFu;
-              const __half2 pr = __floats2half2_rn(static_cast<float>(static_cast<int>(byte & 15u) - 8) * sc,
-                                                   static_cast<float>(static_cast<int>(byte >> 4) - 8) * sc);
-              hv[j] = *reinterpret_cast<const uint32_t*>(&pr);
-            }
-            dst[4 * q + k] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-          }
-        }
+      for (int j = 0; j < 4; ++j) {  // byte j: dims 2j (low nibble), 2j + 1 (high nibble)
+        const uint32_t byte = (w >> (8 * j)) & 0xFFu;
+        const __half2 pr = __floats2half2_rn(static_cast<float>(static_cast<int>(byte & 15u) - 8) * sc,
+                                             static_cast<float>(static_cast<int>(byte >> 4) - 8) * sc);
+        hv[j] = *reinterpret_cast<const uint32_t*>(&pr);
       }
+      *reinterpret_cast<uint4*>((kv ? v16 : k16) + orow) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
     }
   }
 }
@@ -679,7 +679,9 @@ int prefill_int4(const void* query, const uint8_t* pages, const int32_t* bt, con
   __half* k16 = reinterpret_cast<__half*>(base + l.k);
   __half* v16 = reinterpret_cast<__half*>(base + l.v);
   int32_t* bt16 = reinterpret_cast<int32_t*>(base + l.bt);
-  const dim3 grid(MB, B);
+  if (static_cast<int64_t>(MB) * ((KVH + 3) / 4) > 0x7fffffffLL)
+    return fail(MEMOPT_ERR_UNSUPPORTED, "prefill_int4: too many pages per sequence");
+  const dim3 grid(MB * ((KVH + 3) / 4), B);
 #define MEMOPT_INT4_GATHER(DD, BB)                                                                                int4_pages_to_f16_kernel<DD, BB><<<grid, 128, 0, s>>>(pages, bt, ctx, MB, NB, KVH, k16, v16, bt16)
   if (D == 128 && BS == 16) MEMOPT_INT4_GATHER(128, 16);
   else if (D == 128 && BS == 32) MEMOPT_INT4_GATHER(128, 32);
