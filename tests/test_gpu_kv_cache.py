@@ -235,3 +235,30 @@ def test_exact_eviction_on_the_int4_pool():
     torch.testing.assert_close(after, fresh.attend(q, fs), atol=0, rtol=0)
     assert not torch.equal(before, after)
 
+
+
+def test_int4_cache_prefill_chunk_matches_oracle():
+    """A 96-row chunk on the INT4 cache takes the prefill path (pages
+    dequantised into the workspace's fp16 scratch, then the tcgen05 kernel)
+    through memopt_C, which sizes that workspace itself."""
+    torch.manual_seed(4)
+    H, D, BS = 4, 128, 16
+    cache = PagedKVCache(64, H, D, BS)
+    sids = [cache.add_sequence(), cache.add_sequence()]
+    cache.append(sids, torch.randn(2, 300, H, D, device=DEV, dtype=torch.float16),
+                 torch.randn(2, 300, H, D, device=DEV, dtype=torch.float16))
+    cache.to_int4()
+    cache.append(sids, torch.randn(2, 96, H, D, device=DEV, dtype=torch.float16),
+                 torch.randn(2, 96, H, D, device=DEV, dtype=torch.float16))
+    q = torch.randn(2, 96, H, D, device=DEV, dtype=torch.float16)
+    out = cache.attend(q, sids)
+    pages = memopt.memopt_C.get_int4_pages().cpu().numpy()
+    bt = cache.block_tables(sids).cpu().numpy()
+    cl = cache.context_lens(sids).cpu().numpy()
+    assert cl.tolist() == [396, 396]
+    ref = O.paged_attention_int4(q.cpu().numpy(), pages, bt, cl, int(cl.max()), int(cl.max()), BS)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
+    # a decode step afterwards reuses the same cached workspace
+    q1 = torch.randn(2, 1, H, D, device=DEV, dtype=torch.float16)
+    ref1 = O.paged_attention_int4(q1.cpu().numpy(), pages, bt, cl, int(cl.max()), int(cl.max()), BS)
+    np.testing.assert_allclose(cache.attend(q1, sids).float().cpu().numpy(), ref1, atol=2e-3, rtol=1e-2)
