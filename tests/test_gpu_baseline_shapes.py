@@ -6,12 +6,14 @@
   over 8192 tokens, 32 heads), 128 sampled query rows of every sequence and
   head against the fp64 oracle (non-causal rows are independent, so the
   oracle runs on the sampled rows alone).
+* configs[4] prefill over INT4 pages (the same rows written by the fused
+  writer): 64 sampled query rows of every sequence and head.
 * configs[4] decode: INT4 pages written by the fused write_cache for a
   131072-token sequence, 32 heads, decode against the oracle.
 * 64-bit offsets: an fp16 pool of 40000 pages x 16 x 32 x 128 (2.6e9
   elements per pool) and an INT4 pool of 32000 pages x 32 heads x 2176 B
   (2.2e9 bytes), with the sequences on the highest physical pages; write,
-  decode (one-row and multi-query), prefill, evict_tokens and both
+  decode (one-row and multi-query), prefill (fp16 and INT4), evict_tokens and both
   compactions run there and are checked on a compact copy of the touched
   pages.
 
@@ -76,6 +78,27 @@ def test_cfg4_prefill_benchmark_workload_sampled_rows():
         cbt, _, (ckp, cvp) = _compact(bt_h[b:b + 1], kp, vp)
         qs = np.ascontiguousarray(np16(q[b:b + 1].index_select(1, rt)))
         ref = O.paged_attention_f16(qs, ckp, cvp, cbt, ctx_h[b:b + 1], QL, QL)
+        _close(out[b:b + 1].index_select(1, rt), ref)
+
+
+def test_cfg4_prefill_on_int4_pages_sampled_rows():
+    # the benchmark's int4_prefill leg: its K/V rows written into INT4 pages by the fused writer
+    kp, vp, bt, q, ctx = bench.make_prefill_workload(torch, DEV)
+    QL = bench.PREFILL_QL
+    NB, BSZ, NH, HD = kp.shape
+    pages = torch.zeros(NB, NH, capi.int4_page_bytes(BSZ, HD), dtype=torch.uint8, device=DEV)
+    capi.write_cache_int4(kp.view(-1, NH, HD), vp.view(-1, NH, HD),
+                          torch.arange(NB * BSZ, dtype=torch.int32, device=DEV), pages, BSZ)
+    del kp, vp
+    out = capi.attention_int4(q, pages, BSZ, bt, ctx, QL, QL)
+    rows = np.sort(np.random.default_rng(4096).choice(QL, size=64, replace=False))
+    rows[0], rows[-1] = 0, QL - 1
+    rt = torch.from_numpy(rows).to(DEV)
+    bt_h, ctx_h = np16(bt), np16(ctx)
+    for b in range(q.shape[0]):
+        cbt, _, (cpages,) = _compact(bt_h[b:b + 1], pages)
+        qs = np.ascontiguousarray(np16(q[b:b + 1].index_select(1, rt)))
+        ref = O.paged_attention_int4(qs, cpages, cbt, ctx_h[b:b + 1], QL, QL, BSZ)
         _close(out[b:b + 1].index_select(1, rt), ref)
 
 
@@ -241,7 +264,7 @@ def test_int4_pool_beyond_2p31_write_attention_compaction(big_int4):
     gbt = torch.from_numpy(bt).to(DEV)
     ctx = np.array([LSEQ, LSEQ - 300], np.int32)
     gctx = torch.from_numpy(ctx).to(DEV)
-    for QL, nh in ((1, H), (1, 2 * H), (3, H)):
+    for QL, nh in ((1, H), (1, 2 * H), (3, H), (96, H)):  # q_len 96: the INT4 prefill path
         q = torch.from_numpy(rng.standard_normal((S, QL, nh, D)).astype(np.float16)).to(DEV)
         got = capi.attention_int4_ex(q, pages, BS, gbt, gctx, LSEQ, LSEQ)
         _close(got, O.paged_attention_int4(np16(q), cpages, cbt, ctx, LSEQ, LSEQ, BS))
