@@ -628,11 +628,15 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
     const uint16_t* ksp = reinterpret_cast<const uint16_t*>(pg + BS * D) + spos * G;
     const uint16_t* vsp = reinterpret_cast<const uint16_t*>(pg + BS * D + BS * G * 2);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      ks[hi][g] = ksp[g];
-      vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
+    if constexpr (G == 2) {  // a position's two K scales are one aligned 4-byte word
+      const uint32_t k2 = *reinterpret_cast<const uint32_t*>(ksp);
+      ks[hi][0] = static_cast<uint16_t>(k2);
+      ks[hi][1] = static_cast<uint16_t>(k2 >> 16);
+    } else {
+      ks[hi][0] = ksp[0];
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
@@ -675,11 +679,13 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
     uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
     uint16_t* ksp = reinterpret_cast<uint16_t*>(pg + BS * D) + dpos * G;
     uint16_t* vsp = reinterpret_cast<uint16_t*>(pg + BS * D + BS * G * 2);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      ksp[g] = ks[hi][g];
-      vsp[int4_vscale_index(dpos, g, G)] = vs[hi][g];
+    if constexpr (G == 2) {
+      *reinterpret_cast<uint32_t*>(ksp) = static_cast<uint32_t>(ks[hi][0]) | (static_cast<uint32_t>(ks[hi][1]) << 16);
+    } else {
+      ksp[0] = ks[hi][0];
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) vsp[int4_vscale_index(dpos, g, G)] = vs[hi][g];
   }
 }
 
