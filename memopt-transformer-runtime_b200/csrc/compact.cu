@@ -593,99 +593,159 @@ __global__ void __launch_bounds__(32 * kMoveWarps) move_rows_int4_kernel(
   extern __shared__ __align__(128) uint8_t stage_rows[];  // per warp: KVH x (K row, V row) code bytes
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   __shared__ int cta_ticket;
+  // Scales of the rows this CTA moves, stored together once every warp has
+  // passed its dependency wait: the CTA's rows are consecutive positions of
+  // one destination page, so (when all move) their K scales are 32
+  // contiguous bytes per head and their V scales 16 per group.
+  __shared__ uint16_t s_sc[kMoveWarps][64][4];  // [row][head][K g0, K g1, V g0, V g1] (KVH <= 64)
+  __shared__ int s_dp[kMoveWarps], s_dpos[kMoveWarps], s_ok[kMoveWarps];
   if (threadIdx.x == 0) cta_ticket = atomicAdd(&ctrl[0], 1);
   __syncthreads();
   const int ticket = cta_ticket * kMoveWarps + w;  // this warp's row, in ticket order
-  if (ticket >= total_rows) return;
-  const int b = ticket / nseg, row = ticket % nseg;  // one row per segment
-  if (row >= kept_count[b]) return;
-  const int64_t rb = static_cast<int64_t>(b) * max_len;
-  int* my_flag = flags + static_cast<int64_t>(b) * seg_stride + row;
-  if (src_ord[rb + row] == row) {  // already in place
-    if (lane == 0 && !withhold_flags) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
-    return;
-  }
-  const int t = kept_idx[rb + row];
-  const int sp = old_bt[static_cast<int64_t>(b) * MB + t / BS], spos = t % BS;
-  const int dp = new_bt[static_cast<int64_t>(b) * MB + row / BS], dpos = row % BS;
-  const int sswap = (D == 128 && (spos & 2)) ? 2 : 0, dswap = (D == 128 && (dpos & 2)) ? 2 : 0;
-  uint8_t* stage = stage_rows + static_cast<size_t>(w) * KVH * 2 * CB;
-  const uint32_t sst = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
-  // Lane -> (head hs of each group of HPI heads, 16-byte chunk c of its rows):
-  // a warp instruction covers HPI whole code rows (coalesced 64-byte runs).
-  const int hs = lane / LPR, c = lane % LPR;
-  for (int h = hs; h < KVH; h += HPI) {
-    const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
-    cp_async16(sst + (2 * h) * CB + 16 * c, pg + spos * CB + 16 * c);
-    cp_async16(sst + (2 * h + 1) * CB + 16 * c, pg + BS * CB + spos * CB + 16 * (c ^ sswap));  // logical chunk c
-  }
-  // Scales (2 G halves per head) through registers: lane h, h + 32.
-  uint16_t ks[2][G], vs[2][G];
-#pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-    const int h = lane + 32 * hi;
-    if (h >= KVH) continue;
-    const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
-    const uint16_t* ksp = reinterpret_cast<const uint16_t*>(pg + BS * D) + spos * G;
-    const uint16_t* vsp = reinterpret_cast<const uint16_t*>(pg + BS * D + BS * G * 2);
-    if constexpr (G == 2) {  // a position's two K scales are one aligned 4-byte word
-      const uint32_t k2 = *reinterpret_cast<const uint32_t*>(ksp);
-      ks[hi][0] = static_cast<uint16_t>(k2);
-      ks[hi][1] = static_cast<uint16_t>(k2 >> 16);
-    } else {
-      ks[hi][0] = ksp[0];
+  // Returns true when the row was moved (its codes stored) and its scales,
+  // left in s_sc, are to be stored at (s_dp, s_dpos).
+  auto move_row = [&]() -> bool {
+    if (ticket >= total_rows) return false;
+    const int b = ticket / nseg, row = ticket % nseg;  // one row per segment
+    if (row >= kept_count[b]) return false;
+    const int64_t rb = static_cast<int64_t>(b) * max_len;
+    int* my_flag = flags + static_cast<int64_t>(b) * seg_stride + row;
+    if (src_ord[rb + row] == row) {  // already in place
+      if (lane == 0 && !withhold_flags)
+        asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+      return false;
     }
+    const int t = kept_idx[rb + row];
+    const int sp = old_bt[static_cast<int64_t>(b) * MB + t / BS], spos = t % BS;
+    const int dp = new_bt[static_cast<int64_t>(b) * MB + row / BS], dpos = row % BS;
+    const int sswap = (D == 128 && (spos & 2)) ? 2 : 0, dswap = (D == 128 && (dpos & 2)) ? 2 : 0;
+    uint8_t* stage = stage_rows + static_cast<size_t>(w) * KVH * 2 * CB;
+    const uint32_t sst = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+    // Lane -> (head hs of each group of HPI heads, 16-byte chunk c of its rows):
+    // a warp instruction covers HPI whole code rows (coalesced 64-byte runs).
+    const int hs = lane / LPR, c = lane % LPR;
+    for (int h = hs; h < KVH; h += HPI) {
+      const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
+      cp_async16(sst + (2 * h) * CB + 16 * c, pg + spos * CB + 16 * c);
+      cp_async16(sst + (2 * h + 1) * CB + 16 * c, pg + BS * CB + spos * CB + 16 * (c ^ sswap));  // logical chunk c
+    }
+    // Scales (2 G halves per head) through registers: lane h, h + 32.
+    uint16_t ks[2][G], vs[2][G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncwarp();
-  int gave_up = 0;
-  if (lane == 0) {
-    __threadfence();
-    if (!withhold_flags) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
-    // Wait until the row that lives at this row's destination has been read.
-    const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + row];
-    for (int m = d; m < row && m <= d + 1 && !gave_up; ++m) {
-      const int* f = flags + static_cast<int64_t>(b) * seg_stride + m;
-      uint32_t polls = 0;
-      int v = 0;
-      while (true) {
-        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-        if (v) break;
-        if (++polls > flag_polls) {
-          atomicExch(&ctrl[1], 1);
-          gave_up = 1;
-          break;
+    for (int hi = 0; hi < 2; ++hi) {
+      const int h = lane + 32 * hi;
+      if (h >= KVH) continue;
+      const uint8_t* pg = pages + (static_cast<int64_t>(sp) * KVH + h) * page_bytes;
+      const uint16_t* ksp = reinterpret_cast<const uint16_t*>(pg + BS * D) + spos * G;
+      const uint16_t* vsp = reinterpret_cast<const uint16_t*>(pg + BS * D + BS * G * 2);
+      if constexpr (G == 2) {  // a position's two K scales are one aligned 4-byte word
+        const uint32_t k2 = *reinterpret_cast<const uint32_t*>(ksp);
+        ks[hi][0] = static_cast<uint16_t>(k2);
+        ks[hi][1] = static_cast<uint16_t>(k2 >> 16);
+      } else {
+        ks[hi][0] = ksp[0];
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) vs[hi][g] = vsp[int4_vscale_index(spos, g, G)];
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+    int gave_up = 0;
+    if (lane == 0) {
+      __threadfence();
+      if (!withhold_flags) asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(my_flag), "r"(1) : "memory");
+      // Wait until the row that lives at this row's destination has been read.
+      const int d = seg_dep[static_cast<int64_t>(b) * seg_stride + row];
+      for (int m = d; m < row && m <= d + 1 && !gave_up; ++m) {
+        const int* f = flags + static_cast<int64_t>(b) * seg_stride + m;
+        uint32_t polls = 0;
+        int v = 0;
+        while (true) {
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+          if (v) break;
+          if (++polls > flag_polls) {
+            atomicExch(&ctrl[1], 1);
+            gave_up = 1;
+            break;
+          }
+          __nanosleep(64);
         }
-        __nanosleep(64);
       }
     }
-  }
-  // After a give-up the row is not stored: its destination may still hold an
-  // unread kept row.
-  if (__shfl_sync(0xffffffffu, gave_up, 0)) return;
-  for (int h = hs; h < KVH; h += HPI) {
-    uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
-    const uint4 kv = *reinterpret_cast<const uint4*>(stage + (2 * h) * CB + 16 * c);
-    const uint4 vv = *reinterpret_cast<const uint4*>(stage + (2 * h + 1) * CB + 16 * c);
-    *reinterpret_cast<uint4*>(pg + dpos * CB + 16 * c) = kv;
-    *reinterpret_cast<uint4*>(pg + BS * CB + dpos * CB + 16 * (c ^ dswap)) = vv;
-  }
-#pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-    const int h = lane + 32 * hi;
-    if (h >= KVH) continue;
-    uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
-    uint16_t* ksp = reinterpret_cast<uint16_t*>(pg + BS * D) + dpos * G;
-    uint16_t* vsp = reinterpret_cast<uint16_t*>(pg + BS * D + BS * G * 2);
-    if constexpr (G == 2) {
-      *reinterpret_cast<uint32_t*>(ksp) = static_cast<uint32_t>(ks[hi][0]) | (static_cast<uint32_t>(ks[hi][1]) << 16);
-    } else {
-      ksp[0] = ks[hi][0];
+    // After a give-up the row is not stored: its destination may still hold an
+    // unread kept row.
+    if (__shfl_sync(0xffffffffu, gave_up, 0)) return false;
+    for (int h = hs; h < KVH; h += HPI) {
+      uint8_t* pg = pages + (static_cast<int64_t>(dp) * KVH + h) * page_bytes;
+      const uint4 kv = *reinterpret_cast<const uint4*>(stage + (2 * h) * CB + 16 * c);
+      const uint4 vv = *reinterpret_cast<const uint4*>(stage + (2 * h + 1) * CB + 16 * c);
+      *reinterpret_cast<uint4*>(pg + dpos * CB + 16 * c) = kv;
+      *reinterpret_cast<uint4*>(pg + BS * CB + dpos * CB + 16 * (c ^ dswap)) = vv;
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g) vsp[int4_vscale_index(dpos, g, G)] = vs[hi][g];
+    for (int hi = 0; hi < 2; ++hi) {
+      const int h = lane + 32 * hi;
+      if (h >= KVH) continue;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        s_sc[w][h][g] = ks[hi][g];
+        s_sc[w][h][2 + g] = vs[hi][g];
+      }
+    }
+    if (lane == 0) {
+      s_dp[w] = dp;
+      s_dpos[w] = dpos;
+    }
+    return true;
+  };
+  const bool moved = move_row();
+  if (lane == 0) s_ok[w] = moved ? 1 : 0;
+  __syncthreads();
+  bool whole = (kMoveWarps == 8) && s_dpos[0] % 8 == 0;
+#pragma unroll
+  for (int r = 0; r < kMoveWarps; ++r)
+    whole = whole && s_ok[r] && s_dp[r] == s_dp[0] && s_dpos[r] == s_dpos[0] + r;
+  if (whole) {
+    // Thread (head, part): part 0..G-1 the K scales of 4 rows each (16 B),
+    // part G..2G-1 the 8 V scales of group part - G (16 B; per-tile slot order).
+    const int h = threadIdx.x / (2 * G), part = threadIdx.x % (2 * G);
+    if (threadIdx.x < KVH * 2 * G) {
+      uint8_t* pg = pages + (static_cast<int64_t>(s_dp[0]) * KVH + h) * page_bytes;
+      const int p0 = s_dpos[0];
+      uint16_t v8[8];
+      uint4* dst;
+      if (part < G) {
+        // K scales of positions p0 .. p0 + 7: [pos][G] halves; this thread's 8 halves
+        const int first = part * (8 / G);  // G = 2: rows 0-3 or 4-7; G = 1: rows 0-7
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v8[e] = s_sc[first + e / G][h][e % G];
+        dst = reinterpret_cast<uint4*>(pg + BS * D + (p0 + first) * G * 2);
+      } else {
+        const int g = part - G;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          // p0 is a multiple of 8, so position p0 + r takes slot (p0 & 8) + this
+          // of its 16-token tile (the order int4_vscale_index gives)
+          v8[2 * (r & 3) + ((r >> 2) & 1)] = s_sc[r][h][2 + g];
+        }
+        dst = reinterpret_cast<uint4*>(pg + BS * D + BS * G * 2 + 2 * (((p0 >> 4) * G + g) * 16 + (p0 & 8)));
+      }
+      *dst = make_uint4(v8[0] | (static_cast<uint32_t>(v8[1]) << 16), v8[2] | (static_cast<uint32_t>(v8[3]) << 16),
+                        v8[4] | (static_cast<uint32_t>(v8[5]) << 16), v8[6] | (static_cast<uint32_t>(v8[7]) << 16));
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < kMoveWarps * KVH; idx += blockDim.x) {
+      const int r = idx / KVH, h = idx % KVH;
+      if (!s_ok[r]) continue;
+      uint8_t* pg = pages + (static_cast<int64_t>(s_dp[r]) * KVH + h) * page_bytes;
+      uint16_t* ksp = reinterpret_cast<uint16_t*>(pg + BS * D) + s_dpos[r] * G;
+      uint16_t* vsp = reinterpret_cast<uint16_t*>(pg + BS * D + BS * G * 2);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        ksp[g] = s_sc[r][h][g];
+        vsp[int4_vscale_index(s_dpos[r], g, G)] = s_sc[r][h][2 + g];
+      }
+    }
   }
 }
 
