@@ -14,7 +14,10 @@ constexpr int kQuantThreads = 256;
 
 // One lane = 16 consecutive elements (32 bytes in, 8 bytes of codes out),
 // 4 lanes per group.
-__global__ void __launch_bounds__(kQuantThreads)
+// At most 64 registers: four 256-thread CTAs per SM.  The next warp-stride's
+// 32 bytes per lane are loaded while the current ones are converted and
+// stored, so every lane keeps a load in flight.
+__global__ void __launch_bounds__(kQuantThreads, 4)
 quantize_int4_kernel(const uint4* __restrict__ in, uint2* __restrict__ codes,
                      float* __restrict__ scales, int64_t num_pairs) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -22,28 +25,28 @@ quantize_int4_kernel(const uint4* __restrict__ in, uint2* __restrict__ codes,
   // over whole warps) so the group shuffles always see all 32 lanes.
   const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t warp_first = first & ~int64_t(31);
-  // Two warp-strides per iteration: 64 bytes of loads in flight per lane.
-  for (int64_t base = warp_first; base < num_pairs; base += 2 * stride) {
-    uint4 a[2], b[2];
-    int64_t c[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      c[u] = base + u * stride + (threadIdx.x & 31);
-      a[u] = b[u] = make_uint4(0, 0, 0, 0);
-      if (c[u] < num_pairs) {
-        a[u] = ld_stream_v4(in + 2 * c[u]);
-        b[u] = ld_stream_v4(in + 2 * c[u] + 1);
-      }
+  int64_t c = warp_first + (threadIdx.x & 31);
+  uint4 a = make_uint4(0, 0, 0, 0), b = a;
+  if (c < num_pairs) {
+    a = ld_stream_v4(in + 2 * c);
+    b = ld_stream_v4(in + 2 * c + 1);
+  }
+  for (int64_t base = warp_first; base < num_pairs; base += stride) {
+    const int64_t cn = c + stride;
+    uint4 an = make_uint4(0, 0, 0, 0), bn = an;
+    if (cn < num_pairs) {
+      an = ld_stream_v4(in + 2 * cn);
+      bn = ld_stream_v4(in + 2 * cn + 1);
     }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      float scale;
-      const uint2 w = int4_quant16(a[u], b[u], scale);
-      if (c[u] < num_pairs) {
-        codes[c[u]] = w;
-        if ((c[u] & 3) == 0) scales[c[u] >> 2] = scale;
-      }
+    float scale;
+    const uint2 w = int4_quant16(a, b, scale);
+    if (c < num_pairs) {
+      codes[c] = w;
+      if ((c & 3) == 0) scales[c >> 2] = scale;
     }
+    a = an;
+    b = bn;
+    c = cn;
   }
 }
 
