@@ -93,6 +93,23 @@ def test_kernel_entry_points_validate_without_gpu(lib):
     assert sz(0, 1, 1, 64, 1, 16, 16, 16) == 0
 
 
+def test_int4_workspace_adds_the_prefill_scratch_only_for_prefill_calls(lib):
+    gen = lib.memopt_paged_attention_workspace_size_ex
+    i4 = lib.memopt_paged_attention_int4_workspace_size_ex
+    gen.restype = i4.restype = C.c_size_t
+    # decode (q_len 1): the same size for both pool formats
+    assert i4(4, 1, 32, 8, 128, 512, 16, 8192, 8192) == gen(4, 1, 32, 8, 128, 512, 16, 8192, 8192)
+    # prefill (q_len >= 64): the split workspace (256-aligned) + fp16 K and V pages + a table
+    B, QL, H, KVH, D, MB, BS = 4, 8192, 32, 32, 128, 512, 16
+    split = gen(B, QL, H, KVH, D, MB, BS, 8192, 8192)
+    kv = B * MB * BS * KVH * D * 2
+    table = -(-(B * MB * 4) // 256) * 256
+    assert i4(B, QL, H, KVH, D, MB, BS, 8192, 8192) == -(-split // 256) * 256 + 2 * kv + table
+    # head_dim / block_size pairs without a prefill kernel keep the multi-query path's size
+    assert i4(1, 128, 4, 2, 192, 8, 16, 128, 128) == gen(1, 128, 4, 2, 192, 8, 16, 128, 128)
+    assert i4(0, 128, 4, 2, 128, 8, 16, 128, 128) == 0
+
+
 def test_memopt_c_module_surface():
     import memopt_C
 
