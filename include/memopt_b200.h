@@ -294,7 +294,8 @@ size_t memopt_paged_attention_workspace_size_ex(int batch, int q_len, int num_he
 /* batch * max_blocks_per_seq pages into which the call dequantises the      */
 /* sequences' INT4 pages before running the tcgen05 prefill kernel on them,  */
 /* as the reference dequantises an INT4 cache before fp16 attention          */
-/* (quantization.cu:371-428 -> attention.cu:371-521).  Ticket rules as above. */
+/* (quantization.cu:371-428 -> attention.cu:371-521).  Ticket rules as above; */
+/* such calls need a 256-byte aligned workspace (cudaMalloc's alignment).    */
 size_t memopt_paged_attention_int4_workspace_size_ex(int batch, int q_len, int num_heads, int num_kv_heads,
                                                      int head_dim, int max_blocks_per_seq, int block_size,
                                                      int max_seq_len, int window_size);

@@ -669,7 +669,9 @@ int prefill_int4(const void* query, const uint8_t* pages, const int32_t* bt, con
                  void* scratch, size_t scratch_bytes, cudaStream_t s) {
   if (!prefill_int4_supported(D, BS)) return fail(MEMOPT_ERR_UNSUPPORTED, "prefill_int4: unsupported (block_size, head_dim)");
   const Int4Scratch l = int4_scratch_layout(B, KVH, D, MB, BS);
-  if (scratch == nullptr || scratch_bytes < l.total || (reinterpret_cast<uintptr_t>(scratch) & 255u))
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u)
+    return fail(MEMOPT_ERR_INVALID_ARG, "dynamic_sparse_attention_int4: workspace must be 256-byte aligned");
+  if (scratch == nullptr || scratch_bytes < l.total)
     return fail(MEMOPT_ERR_WORKSPACE, "dynamic_sparse_attention_int4: workspace too small for the fp16 page scratch "
                                       "(need " + std::to_string(l.total) + " bytes past the split workspace)");
   const int64_t nb16 = static_cast<int64_t>(B) * MB;
