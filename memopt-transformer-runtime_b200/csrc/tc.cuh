@@ -143,7 +143,6 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&v)[16]) {
       "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
-__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Wait for this thread's tcgen05.ld results with the loaded registers as
 // operands, so that no use of them is scheduled before the wait.
 __device__ __forceinline__ void wait_ld(float (&v)[32]) {
